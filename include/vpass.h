@@ -1,0 +1,182 @@
+/*
+ * vpass.h - C ABI of the B200 speculative-decoding verification pass (Qwen2.5-0.5B architecture).
+ *
+ * The reference engine (instantllm, Swift + Metal) has no FFI layer: its operator surface is the
+ * Engine class. Each entry point below names the Engine member or Metal kernel it replaces
+ * (paths inside the instantllm project).
+ *
+ * Conventions
+ *  - Every function returns VP_OK (0) or a negative VP_ERR_* code; nothing throws or aborts.
+ *  - Pointers named d_* are device pointers (or any pointer cudaMemcpyDefault accepts where noted).
+ *    `stream` is a cudaStream_t passed as void* so this header needs no CUDA include.
+ *  - Work is stream-ordered. Only vp_read_state synchronises (on the given stream).
+ *  - A context owns its scratch (activations, KV cache, partials, state, token buffer). Weights are
+ *    borrowed: the caller keeps the packed weight buffers alive (Engine.swift:96-99 borrows the
+ *    mmapped model the same way).
+ *  - One context serves one request at a time on one GPU and is not thread-safe. Contexts on
+ *    different GPUs are independent (request-level sharding needs no communication).
+ *  - Device-side failures (bad tree, context overflow, wait timeout) never trap: they set
+ *    vp_state.err and vp_state.done, and every later kernel of the request returns at once.
+ */
+#ifndef VPASS_H
+#define VPASS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Architecture constants (docs/SPEC.md:31-44; tools/reference/qwen_ref.py:40-51). */
+#define VP_HIDDEN 896
+#define VP_FFN 4864
+#define VP_NQ_HEADS 14
+#define VP_NKV_HEADS 2
+#define VP_HEAD_DIM 64
+#define VP_QKV_ROWS 1152
+#define VP_MAX_LAYERS 24
+#define VP_MAX_ROWS 16 /* rows per verify pass: root + 15 drafts (Shaders.swift:23-30) */
+#define VP_GROUP 64    /* quantisation group along K for q4 and q8 */
+
+/* Tree buffer, int32[VP_TREE_INTS] (Shaders.swift:23-30, written by k_ildraft :846-866):
+ * [0] n rows; [1+i] depth[i]; [17+i] parent[i]; [33+i] tok[i]; [49+i] ancestor bitmask[i].
+ * Row 0 is the last committed token (its tok entry is ignored: the device state supplies it).
+ * Row i > 0 is a draft whose parent row parent[i] < i, with depth[i] = depth[parent[i]] + 1.
+ * Row i sits at KV slot pos + i and is rotated (RoPE) as position pos + depth[i]. */
+#define VP_TREE_INTS 65
+#define VP_TR_N 0
+#define VP_TR_DEPTH 1
+#define VP_TR_PARENT 17
+#define VP_TR_TOK 33
+#define VP_TR_ANC 49
+
+enum vp_format { VP_FMT_F16 = 0, VP_FMT_Q8 = 1, VP_FMT_Q4 = 2 };
+
+/* Matrix roles for vp_pack_matrix: the packer applies the row order the fused epilogues need. */
+enum vp_matrix_kind {
+  VP_MAT_PLAIN = 0,  /* O, down and the tied embedding / lm_head: natural row order */
+  VP_MAT_QKV = 1,    /* [q(896); k(128); v(128)] rows of a layer: RoPE pairs (d, d+32) kept together */
+  VP_MAT_GATEUP = 2  /* [gate(4864); up(4864)] rows: gate j and up j kept together */
+};
+
+enum vp_error {
+  VP_OK = 0,
+  VP_ERR_ARG = -1,     /* bad argument (null pointer, size out of range, unsupported format) */
+  VP_ERR_CUDA = -2,    /* a CUDA runtime call failed; vp_last_error() has the text */
+  VP_ERR_STATE = -3,   /* call out of order (e.g. verify before weights are set) */
+  VP_ERR_NOMEM = -4,   /* device allocation failed */
+  VP_ERR_DEVICE = -5   /* the device reported an error in vp_state.err */
+};
+
+/* Device-side error bits in vp_state.err. */
+#define VP_DEV_ERR_TREE 1     /* malformed tree buffer */
+#define VP_DEV_ERR_CTX 2      /* pos + rows would pass max_ctx */
+#define VP_DEV_ERR_TIMEOUT 4  /* a bounded wait (mbarrier / copy) gave up */
+#define VP_DEV_ERR_STEPS 8    /* out_tokens full */
+
+typedef struct vp_ctx vp_ctx;
+
+typedef struct {
+  int32_t format;    /* enum vp_format */
+  int32_t n_layers;  /* 1..24 (24 for Qwen2.5-0.5B) */
+  int32_t vocab;     /* multiple of 16, e.g. 151936 */
+  int32_t max_ctx;   /* KV slots per layer; must cover prefix + generated + VP_MAX_ROWS */
+  int32_t max_steps; /* capacity of the committed-token buffer */
+  int32_t device;    /* CUDA device ordinal */
+} vp_config;
+
+/* Device pass state (Shaders.swift:37-54 `State`, initialised by Engine.generate :945-964). */
+typedef struct {
+  int32_t pos;       /* KV slots holding committed context (first slot of the next pass) */
+  int32_t n;         /* rows of the last pass */
+  int32_t step;      /* committed tokens so far */
+  int32_t done;      /* stop flag: set on EOS, max_steps or error; every kernel then returns */
+  int32_t maxctx;
+  int32_t maxsteps;
+  int32_t eos0;
+  int32_t eos1;
+  int32_t nver;      /* rows whose argmax the next commit reads */
+  int32_t vrow0;     /* first of those rows (n-1 after a prefill chunk, else 0) */
+  int32_t passes;    /* committed passes (diagnostics, Shaders.swift:308) */
+  int32_t accepted;  /* accepted drafts (diagnostics, Shaders.swift:324) */
+  int32_t err;       /* VP_DEV_ERR_* bits */
+  int32_t last_token;/* last committed token: row 0 of the next pass */
+  int32_t mode;      /* 0 verify, 1 prefill (set by the pass's embed kernel) */
+  int32_t advance;   /* prefill: rows to add to pos at commit */
+} vp_state;
+
+/* Borrowed, packed weights of one model (vp_pack_matrix output for matrices, fp32 vectors). */
+typedef struct {
+  const void* embed;                 /* [vocab][896], kind PLAIN; tied lm_head */
+  const float* final_norm;           /* [896] */
+  const void* wqkv[VP_MAX_LAYERS];   /* [1152][896], kind QKV */
+  const float* bqkv[VP_MAX_LAYERS];  /* [1152] natural order q, k, v */
+  const void* wo[VP_MAX_LAYERS];     /* [896][896] */
+  const void* wgu[VP_MAX_LAYERS];    /* [9728][896], kind GATEUP */
+  const void* wd[VP_MAX_LAYERS];     /* [896][4864] */
+  const float* ln1[VP_MAX_LAYERS];   /* [896] input_layernorm */
+  const float* ln2[VP_MAX_LAYERS];   /* [896] post_attention_layernorm */
+} vp_weights;
+
+/* ---- weight formats (replaces Convert.swift:254-370 output layouts + ModelFile.swift tensors) ----
+ * Standard input layouts (what a converter writes):
+ *   q4:  codes uint8 [rows][cols/2], weight 2j in the low nibble of byte j (Convert.swift:317);
+ *        scales half2 [rows][cols/64] = (scale, min); w = scale*q + min (Convert.swift:290-317).
+ *   q8:  codes int8 [rows][cols]; scales half [rows][cols/64]; w = scale*q (group 64).
+ *   f16: half [rows][cols]; scales NULL.
+ * vp_pack_matrix rewrites one matrix into the kernel layout (16-row x 64-column tiles in
+ * tensor-core fragment order). Both buffers are device memory. */
+size_t vp_packed_bytes(int32_t format, int32_t rows, int32_t cols);
+int vp_pack_matrix(int32_t format, int32_t kind, int32_t rows, int32_t cols, const void* d_codes,
+                   const void* d_scales, void* d_out, void* stream);
+
+/* ---- context (Engine.init, Engine.swift:71-232) ---- */
+int vp_create(const vp_config* cfg, vp_ctx** out);
+void vp_destroy(vp_ctx* ctx);
+int vp_set_weights(vp_ctx* ctx, const vp_weights* w);
+const char* vp_last_error(void);
+
+/* ---- request set-up (Engine.generate state init, Engine.swift:937-964) ----
+ * cached: KV slots already valid (shared prefix); max_new: tokens to generate (incl. a stop). */
+int vp_begin(vp_ctx* ctx, int32_t cached, int32_t max_new, int32_t eos0, int32_t eos1, void* stream);
+
+/* ---- prefill (Engine.encodePrefill :588-601 = k_embed_prompt + 24 layers + lm_head + commit) ----
+ * Runs n prompt tokens at slots pos..pos+n-1 in chunks of 16 rows, then the lm_head on the last
+ * row and a 1-row greedy commit (k_commit, Shaders.swift:194-244): out_tokens[step] = argmax. */
+int vp_prefill(vp_ctx* ctx, const int32_t* d_tokens, int32_t n, void* stream);
+
+/* ---- verify pass (Engine.encodeWidePass :567-579 with the tree of k_ildraft) ----
+ * tree: VP_TREE_INTS int32 (host or device pointer, copied with cudaMemcpyDefault). Runs embed,
+ * 24 layers and lm_head with per-row argmax partials; does not commit. */
+int vp_verify(vp_ctx* ctx, const int32_t* tree, void* stream);
+/* Chain form: row 0 = last token, rows 1..nd = drafts (Shaders.swift:322 prefix acceptance). */
+int vp_verify_chain(vp_ctx* ctx, const int32_t* drafts, int32_t nd, void* stream);
+
+/* ---- accept / commit (k_commit_spec, Shaders.swift:254-365) ----
+ * Argmax per row, longest matching tree path, committed tokens to out_tokens, pos += m+1,
+ * KV compaction of the accepted rows. */
+int vp_commit(vp_ctx* ctx, void* stream);
+
+/* ---- whole pass: verify + commit replayed from one CUDA graph (the pass encoder) ---- */
+int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
+
+/* ---- results ---- */
+int vp_read_state(vp_ctx* ctx, vp_state* host, void* stream);       /* syncs `stream` */
+int vp_read_tokens(vp_ctx* ctx, int32_t* host, int32_t count, void* stream); /* syncs `stream` */
+int32_t* vp_device_tokens(vp_ctx* ctx);   /* out_tokens, int32[max_steps], -1 = not yet written */
+vp_state* vp_device_state(vp_ctx* ctx);
+
+/* ---- parity helpers ----
+ * Full fp32 logits [16][vocab] of the rows of the last verify pass or prefill chunk (the values
+ * whose argmax the commit reduces). */
+int vp_debug_logits(vp_ctx* ctx, float* d_out, void* stream);
+/* Raw scratch buffers for tests: 0 x fp32[16][896], 1 q fp32[16][896], 2 KV cache K,
+ * 3 KV cache V (half [layers][2][max_ctx][64]), 4 argmax values fp32[16][vocab/16],
+ * 5 argmax ids int32[16][vocab/16]. */
+int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VPASS_H */

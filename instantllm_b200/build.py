@@ -1,0 +1,51 @@
+"""Build libvpass.so in-tree for sm_100a (nvcc cross-compiles without a GPU)."""
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+SOURCES = [PKG / "csrc" / "vpass.cu"]
+HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "vpass.h"]
+OUT = PKG / "libvpass.so"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-shared", "-Xcompiler", "-fPIC",
+    # no --use_fast_math: the pass must be shape-invariant and close to the fp32 reference
+]
+
+
+def nvcc() -> str:
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    p = Path(cuda) / "bin" / "nvcc"
+    return str(p) if p.exists() else "nvcc"
+
+
+def needs_build() -> bool:
+    if not OUT.exists():
+        return True
+    t = OUT.stat().st_mtime
+    return any(s.stat().st_mtime > t for s in SOURCES + HEADERS)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not needs_build():
+        return OUT
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(OUT), *map(str, SOURCES)]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    if verbose:
+        print(r.stdout + r.stderr)
+    return OUT
+
+
+if __name__ == "__main__":
+    build(force=True, verbose=True)
+    print(OUT)

@@ -1,0 +1,226 @@
+// Accept / commit, request set-up and weight packing kernels.
+#pragma once
+#include "vp_common.cuh"
+
+namespace vp {
+
+constexpr int COMMIT_THREADS = 1024;
+
+struct CommitParams {
+  int nrb_lm;   // lm_head row-blocks = vocab / 16 (argmax partials per row)
+  Scratch s;
+};
+
+// Greedy accept + commit (k_commit_spec, Shaders.swift:254-365, and k_commit :194-244):
+//  1. g[t] = argmax of pass row vrow0+t over the lm_head partials, lowest id on ties (:281-306).
+//  2. Tree: from the root, repeatedly take the first row whose parent is the current row and whose
+//     draft equals the current row's argmax (:311-320). The root's argmax is always committed.
+//  3. Commit g along the path to out_tokens, stopping at EOS or max_steps (:326-333).
+//  4. pos += m + 1 (verify) or += prompt length (prefill, :335-338).
+//  5. KV compaction: accepted row path[k-1] moves from slot pos0+path[k-1] to pos0+k in every
+//     layer; it was already rotated for position pos0+k (its depth is k). Copies run in k order,
+//     which is safe because path rows strictly increase (:351-365).
+__global__ void __launch_bounds__(COMMIT_THREADS) k_commit(CommitParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const Scratch& s = p.s;
+  vp_state* st = s.st;
+  const RowInfo* ri = s.ri;
+  if (!ri->live || st->done) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float rv[32];
+  __shared__ int ri_[32];
+  __shared__ int g[ROWS];
+  __shared__ int path[ROWS];
+  __shared__ int sNpath, sPos0;
+  const int nv = st->nver, r0 = st->vrow0;
+  for (int t = 0; t < nv; ++t) {
+    const float* pv = s.pval + (size_t)(r0 + t) * p.nrb_lm;
+    const int* pi = s.pidx + (size_t)(r0 + t) * p.nrb_lm;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < p.nrb_lm; i += COMMIT_THREADS) {
+      const float v = pv[i];
+      const int id = pi[i];
+      if (v > best || (v == best && id < bi)) { best = v; bi = id; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) { rv[warp] = best; ri_[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+      best = rv[lane];
+      bi = ri_[lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+      }
+      if (lane == 0) g[t] = bi;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    int m = 0;
+    const bool tree = ri->mode == 0 && nv > 1;
+    if (tree) {
+      int cur = 0;
+      for (;;) {
+        int c = -1;
+        for (int i = 1; i < nv; ++i)
+          if (s.tree[VP_TR_PARENT + i] == cur && s.tree[VP_TR_TOK + i] == g[cur]) { c = i; break; }
+        if (c < 0) break;
+        path[m++] = c;
+        cur = c;
+      }
+    }
+    st->passes += 1;
+    st->accepted += m;
+    bool stop = false;
+    int last = st->last_token;
+    for (int i = 0; i <= m && !stop; ++i) {
+      const int tok = g[i == 0 ? 0 : path[i - 1]];
+      if (st->step >= s.max_steps) { atomicOr(&st->err, VP_DEV_ERR_STEPS); stop = true; break; }
+      s.out_tokens[st->step] = tok;
+      st->step += 1;
+      last = tok;
+      if (tok == st->eos0 || tok == st->eos1 || st->step >= st->maxsteps) stop = true;
+    }
+    sPos0 = st->pos;
+    sNpath = tree ? m : 0;
+    st->pos += ri->mode == 1 ? st->advance : m + 1;
+    st->last_token = last;
+    if (stop) st->done = 1;
+  }
+  __syncthreads();
+  const int np = sNpath, pos0 = sPos0;
+  for (int k = 1; k <= np; ++k) {
+    const int src = pos0 + path[k - 1], dst = pos0 + k;
+    if (src != dst) {
+      // 2 caches x layers x 2 KV heads x 64 halves, moved as 16-byte words (8 per row).
+      const int words = 2 * s.n_layers * NKV * (HD / 8);
+      for (int w = tid; w < words; w += COMMIT_THREADS) {
+        const int cache = w / (s.n_layers * NKV * 8);
+        const int rem = w % (s.n_layers * NKV * 8);
+        const int lh = rem / 8, part = rem % 8;
+        __half* base = (cache ? s.vc : s.kc) + (size_t)lh * s.max_ctx * HD;
+        const uint4 v = *reinterpret_cast<const uint4*>(base + (size_t)src * HD + part * 8);
+        *reinterpret_cast<uint4*>(base + (size_t)dst * HD + part * 8) = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Request set-up (Engine.generate, Engine.swift:945-964): one thread.
+__global__ void k_begin(vp_state* st, int32_t* out_tokens, int max_steps_cap, int cached,
+                        int max_new, int eos0, int eos1, int maxctx, int last_token) {
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int j = i; j < max_steps_cap; j += gridDim.x * blockDim.x) out_tokens[j] = -1;
+  if (i == 0) {
+    vp_state z = {};
+    z.pos = cached;
+    z.n = 0;
+    z.maxctx = maxctx;
+    z.maxsteps = max_new;
+    z.eos0 = eos0;
+    z.eos1 = eos1;
+    z.nver = 1;
+    z.last_token = last_token;
+    *st = z;
+  }
+}
+
+// Chain tree from a draft list: rows 0..nd, parent i-1, depth i (Shaders.swift:322 semantics).
+__global__ void k_chain_tree(int32_t* tree, const int32_t* drafts, int nd) {
+  const int i = threadIdx.x;
+  if (i == 0) tree[VP_TR_N] = nd + 1;
+  if (i < ROWS) {
+    tree[VP_TR_DEPTH + i] = i;
+    tree[VP_TR_PARENT + i] = i - 1;
+    tree[VP_TR_TOK + i] = (i >= 1 && i <= nd) ? drafts[i - 1] : 0;
+    tree[VP_TR_ANC + i] = (int)((2u << i) - 1u);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Weight packing: standard layouts -> fragment-ordered tiles (see vp_common.cuh).
+
+__device__ __forceinline__ int src_row(int kind, int rb, int r) {
+  if (kind == VP_MAT_QKV) {
+    const int head = rb >> 2, jj = rb & 3;
+    return head * HD + (r < 8 ? 8 * jj + r : 32 + 8 * jj + (r - 8));
+  }
+  if (kind == VP_MAT_GATEUP) return r < 8 ? rb * 8 + r : F + rb * 8 + (r - 8);
+  return rb * 16 + r;
+}
+
+// One thread per (tile, lane); lane 32 of each tile writes the scale block.
+template <int FMT>
+__global__ void k_pack(int kind, int rows, int cols, const uint8_t* codes, const uint8_t* scales,
+                       uint8_t* out) {
+  constexpr int TB = tile_bytes(FMT);
+  const int ng = cols / GS;
+  const long long ntiles = (long long)(rows / 16) * ng;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= ntiles * 33) return;
+  const long long tileI = idx / 33;
+  const int lane = (int)(idx % 33);
+  const int rb = (int)(tileI / ng), G = (int)(tileI % ng);
+  uint8_t* tile = out + tileI * TB;
+  if (lane == 32) {
+    for (int r = 0; r < 16; ++r) {
+      const int g = r & 7, upper = r >> 3;
+      const int sr = src_row(kind, rb, r);
+      if (FMT == VP_FMT_Q4) {
+        const uint32_t v = reinterpret_cast<const uint32_t*>(scales)[(size_t)sr * ng + G];
+        reinterpret_cast<uint32_t*>(tile + 512)[g * 2 + upper] = v;
+      } else if (FMT == VP_FMT_Q8) {
+        const uint16_t v = reinterpret_cast<const uint16_t*>(scales)[(size_t)sr * ng + G];
+        reinterpret_cast<uint16_t*>(tile + 1024)[g * 2 + upper] = v;
+      }
+    }
+    return;
+  }
+  const int g = lane >> 2, t4 = lane & 3;
+  for (int j = 0; j < 4; ++j) {
+    // a = reg*2 + upper: element (row g + 8*upper, col 16j + 8*reg + 2*t4 + hi)
+    if (FMT == VP_FMT_Q4) {
+      uint32_t w = 0;
+      for (int a = 0; a < 4; ++a)
+        for (int hi = 0; hi < 2; ++hi) {
+          const int sr = src_row(kind, rb, g + 8 * (a & 1));
+          const int k = G * GS + 16 * j + 8 * (a >> 1) + 2 * t4 + hi;
+          const uint8_t b = codes[(size_t)sr * (cols / 2) + (k >> 1)];
+          const uint32_t q = (k & 1) ? (b >> 4) : (b & 15);
+          w |= q << ((hi ? 16 : 0) + 4 * a);
+        }
+      reinterpret_cast<uint32_t*>(tile + lane * 16)[j] = w;
+    } else if (FMT == VP_FMT_Q8) {
+      uint8_t bytes[8];
+      for (int a = 0; a < 4; ++a)
+        for (int hi = 0; hi < 2; ++hi) {
+          const int sr = src_row(kind, rb, g + 8 * (a & 1));
+          const int k = G * GS + 16 * j + 8 * (a >> 1) + 2 * t4 + hi;
+          bytes[(a >> 1) * 4 + (a & 1) * 2 + hi] = codes[(size_t)sr * cols + k];
+        }
+      for (int b = 0; b < 8; ++b) tile[lane * 32 + j * 8 + b] = bytes[b];
+    } else {
+      for (int a = 0; a < 4; ++a)
+        for (int hi = 0; hi < 2; ++hi) {
+          const int sr = src_row(kind, rb, g + 8 * (a & 1));
+          const int k = G * GS + 16 * j + 8 * (a >> 1) + 2 * t4 + hi;
+          reinterpret_cast<uint16_t*>(tile + lane * 64 + j * 16 + a * 4)[hi] =
+              reinterpret_cast<const uint16_t*>(codes)[(size_t)sr * cols + k];
+        }
+    }
+  }
+}
+
+}  // namespace vp

@@ -1,0 +1,180 @@
+// Shared definitions of the verification-pass kernels (sm_100a).
+//
+// Layout vocabulary used throughout:
+//  * tile: 16 weight rows x 64 columns (one quantisation group per row), stored in mma.sync
+//    m16n8k16 A-fragment order so that each lane of a warp fetches its fragments with one
+//    contiguous 16-byte (q4), 32-byte (q8) or 64-byte (f16) read. A matrix is [rows/16][cols/64]
+//    tiles, row-block major.
+//  * act block: 16 tokens x 64 columns of fp16 activations in m16n8k16 B-fragment order
+//    (2 KiB; four 512-byte planes, one per 16-column k-step, lane L's 16 bytes at L*16).
+//    Activations that feed a GEMM are produced directly in this order by the previous stage.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/vpass.h"
+
+namespace vp {
+
+constexpr int H = VP_HIDDEN;
+constexpr int F = VP_FFN;
+constexpr int NQ = VP_NQ_HEADS;
+constexpr int NKV = VP_NKV_HEADS;
+constexpr int HD = VP_HEAD_DIM;
+constexpr int QKV = VP_QKV_ROWS;
+constexpr int ROWS = VP_MAX_ROWS;  // token rows per pass (MMA N dimension, always padded to 16)
+constexpr int GS = VP_GROUP;
+constexpr int HRB = H / 16;        // 56 row-blocks of a hidden-sized output
+constexpr float EPS = 1e-6f;
+constexpr float ATTN_SCALE = 0.125f;  // 64^-0.5, exact
+constexpr int ATT_CHUNK = 64;         // virtual positions per attention split (fixed: shape-invariant)
+
+// Bytes of one packed 16x64 tile per format: codes then per-row scale data.
+__host__ __device__ constexpr int tile_bytes(int fmt) {
+  return fmt == VP_FMT_Q4 ? 512 + 64 : fmt == VP_FMT_Q8 ? 1024 + 32 : 2048;
+}
+__host__ __device__ constexpr int tile_code_bytes(int fmt) {
+  return fmt == VP_FMT_Q4 ? 512 : fmt == VP_FMT_Q8 ? 1024 : 2048;
+}
+
+// Half index of activation (token t, column k) in B-fragment order (see file comment).
+__host__ __device__ inline int act_index(int t, int k) {
+  const int G = k >> 6, kk = k & 63, j = kk >> 4, c = kk & 15;
+  const int nt = t >> 3, gid = t & 7, tid4 = (c & 7) >> 1, reg = c >> 3, hi = c & 1;
+  const int lane = gid * 4 + tid4, word = nt * 2 + reg;
+  return G * 1024 + j * 256 + lane * 8 + word * 2 + hi;
+}
+
+// Per-pass row geometry, written by the pass's embed kernel and read by every later kernel.
+struct RowInfo {
+  int n;               // rows in this pass (1..16)
+  int pos;             // slot of row 0
+  int mode;            // 0 verify, 1 prefill chunk
+  int live;            // 0: the request is done / errored, every kernel returns
+  int depth[ROWS];
+  int path[ROWS][ROWS];  // path[r][d]: row of r's ancestor at depth d (path[r][depth[r]] = r)
+};
+
+// Device scratch of one context (all pointers device memory).
+struct Scratch {
+  vp_state* st;
+  RowInfo* ri;
+  int32_t* tree;        // VP_TREE_INTS
+  int32_t* out_tokens;  // max_steps
+  float* x;             // [16][896] residual stream, fp32
+  float* q;             // [16][896] roped queries, fp32
+  __half* act_h;        // act blocks, K = 896: normed x for QKV / GU / lm_head
+  __half* act_a;        // act blocks, K = 896: attention output for O
+  __half* act_f;        // act blocks, K = 4864: SiLU(gate)*up for down
+  float* ss;            // [HRB][16] per-row-block sums of squares of x (RMSNorm partials)
+  float* part;          // split-K partial tiles [max units][16*16]
+  int* tickets;         // split-K / attention arrival counters (self-resetting)
+  float* att_part;      // attention split partials
+  __half* kc;           // [layers][2][max_ctx][64]
+  __half* vc;
+  float2* rope;         // [max_ctx + 16][32] (cos, sin), angles computed in double
+  float* pval;          // [16][vocab/16] per-row-block max logit
+  int* pidx;            // [16][vocab/16] its id (lowest on ties)
+  float* dbg_logits;    // [16][vocab] or null
+  int max_ctx, max_steps, vocab, n_layers;
+};
+
+// ------------------------------------------------------------------------------------------
+// PTX wrappers (sm_90+ bulk copies and mbarriers, sm_80+ mma.sync)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each try_wait itself suspends for a while), so a
+// lost copy can never hang the GPU. Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint32_t limit = 1u << 22) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// One bulk copy global -> this CTA's shared memory, completing on `bar` (16-byte aligned, size a
+// multiple of 16). Streaming weights are read once per pass: evict-first keeps them from pushing
+// the activations and KV cache out of L2.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
+      "%2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// D += A * B, m16n8k16, fp16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its prologue (weight
+// prefetch) now; wait until the previous kernel's memory is visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void set_error(vp_state* st, int bits) {
+  atomicOr(&st->err, bits);
+  atomicExch(&st->done, 1);
+}
+
+// Reduction helpers with a fixed combination order (results never depend on timing).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace vp

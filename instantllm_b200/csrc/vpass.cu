@@ -1,0 +1,499 @@
+// C ABI of the verification pass (include/vpass.h): context, weight packing, pass encoder.
+//
+// The pass encoder replaces Engine.encodeWidePass / encodePrefill / encodeCommitSpec
+// (Sources/Engine/Engine.swift:484-601): one verify pass is embed, 24 x (QKV, attention, O,
+// gate/up, down), lm_head, commit = 123 kernels, launched with programmatic dependent launch so
+// each kernel streams its weights while the previous one finishes, and replayed from a CUDA graph.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "vp_attn.cuh"
+#include "vp_commit.cuh"
+#include "vp_gemm.cuh"
+
+using namespace vp;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define VP_CUDA(call)                                                                  \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(VP_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));    \
+  } while (0)
+
+struct StageCfg {
+  int nrb, ng, nsplit, cg, cps;
+  size_t smem;
+  int grid() const { return nsplit * cps; }
+};
+
+StageCfg make_stage(int fmt, int rows, int cols, int nsplit) {
+  StageCfg c;
+  c.nrb = rows / 16;
+  c.ng = cols / GS;
+  c.nsplit = nsplit;
+  const int per_chunk = fmt == VP_FMT_Q4 ? 7 : fmt == VP_FMT_Q8 ? 4 : 2;  // ~4 KiB chunks
+  const int ngs = (c.ng + nsplit - 1) / nsplit;
+  c.cg = per_chunk < ngs ? per_chunk : ngs;
+  c.cps = (c.nrb + GEMM_WARPS - 1) / GEMM_WARPS;
+  c.smem = gemm_smem_bytes(fmt, c.ng, nsplit, c.cg);
+  return c;
+}
+
+}  // namespace
+
+struct vp_ctx {
+  vp_config cfg{};
+  vp_weights w{};
+  bool have_w = false;
+  Scratch s{};
+  std::vector<void*> allocs;
+  StageCfg qkv{}, o{}, gu{}, down{}, lm{};
+  int att_grid = 0, max_chunks = 0;
+  cudaStream_t cap = nullptr;
+  cudaGraphExec_t pass_exec = nullptr;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(vp_ctx* c, T** p, size_t bytes) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes < 16 ? 16 : bytes);
+  if (e != cudaSuccess) return fail(VP_ERR_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+  e = cudaMemset(q, 0, bytes < 16 ? 16 : bytes);
+  if (e != cudaSuccess) return fail(VP_ERR_CUDA, std::string("cudaMemset: ") + cudaGetErrorString(e));
+  c->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return VP_OK;
+}
+
+template <typename Kern, typename... Args>
+cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <int FMT, int MODE>
+cudaError_t gemm_launch(const StageCfg& c, const GemmParams& p, cudaStream_t st) {
+  static bool attr_done[2] = {false, false};
+  (void)attr_done;
+  return launch(k_gemm<FMT, MODE>, c.grid(), GEMM_WARPS * 32, c.smem, st, p);
+}
+
+template <int FMT, int MODE>
+int set_smem_attr(size_t smem) {
+  VP_CUDA(cudaFuncSetAttribute(k_gemm<FMT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  return VP_OK;
+}
+
+template <int FMT>
+int set_attrs(vp_ctx* c) {
+  size_t mx = 0;
+  for (const StageCfg* sc : {&c->qkv, &c->o, &c->gu, &c->down, &c->lm}) mx = sc->smem > mx ? sc->smem : mx;
+  int r;
+  if ((r = set_smem_attr<FMT, MODE_QKV>(mx))) return r;
+  if ((r = set_smem_attr<FMT, MODE_RESID>(mx))) return r;
+  if ((r = set_smem_attr<FMT, MODE_SILU>(mx))) return r;
+  if ((r = set_smem_attr<FMT, MODE_ARGMAX>(mx))) return r;
+  return VP_OK;
+}
+
+GemmParams base_params(vp_ctx* c, const StageCfg& sc, const void* w, const __half* act, int layer) {
+  GemmParams p = {};
+  p.w = static_cast<const uint8_t*>(w);
+  p.act = act;
+  p.nrb = sc.nrb;
+  p.ng = sc.ng;
+  p.nsplit = sc.nsplit;
+  p.cg = sc.cg;
+  p.cps = sc.cps;
+  p.layer = layer;
+  p.s = c->s;
+  return p;
+}
+
+template <int FMT>
+int launch_embed(vp_ctx* c, cudaStream_t st, const int32_t* prompt, int chunk_n, int chunk_start,
+                 int total_n, int last) {
+  EmbedParams ep = {};
+  ep.E = static_cast<const uint8_t*>(c->w.embed);
+  ep.ln1 = c->w.ln1[0];
+  ep.prompt = prompt;
+  ep.chunk_n = chunk_n;
+  ep.chunk_start = chunk_start;
+  ep.total_n = total_n;
+  ep.last_chunk = last;
+  ep.s = c->s;
+  VP_CUDA(launch(k_embed<FMT>, ROWS, 256, 0, st, ep));
+  return VP_OK;
+}
+
+template <int FMT>
+int launch_layers_and_head(vp_ctx* c, cudaStream_t st, bool head) {
+  const vp_weights& w = c->w;
+  const int L = c->cfg.n_layers;
+  for (int l = 0; l < L; ++l) {
+    GemmParams p = base_params(c, c->qkv, w.wqkv[l], c->s.act_h, l);
+    p.bias = w.bqkv[l];
+    p.ss_in = c->s.ss;
+    VP_CUDA((gemm_launch<FMT, MODE_QKV>(c->qkv, p, st)));
+
+    AttnParams ap = {};
+    ap.layer = l;
+    ap.max_chunks = c->max_chunks;
+    ap.s = c->s;
+    VP_CUDA(launch(k_attention, c->att_grid, ATT_THREADS, 0, st, ap));
+
+    p = base_params(c, c->o, w.wo[l], c->s.act_a, l);
+    p.wnext = w.ln2[l];
+    p.ss_out = c->s.ss;
+    p.act_out = c->s.act_h;
+    VP_CUDA((gemm_launch<FMT, MODE_RESID>(c->o, p, st)));
+
+    p = base_params(c, c->gu, w.wgu[l], c->s.act_h, l);
+    p.ss_in = c->s.ss;
+    p.act_out = c->s.act_f;
+    VP_CUDA((gemm_launch<FMT, MODE_SILU>(c->gu, p, st)));
+
+    p = base_params(c, c->down, w.wd[l], c->s.act_f, l);
+    p.wnext = l + 1 < L ? w.ln1[l + 1] : w.final_norm;
+    p.ss_out = c->s.ss;
+    p.act_out = c->s.act_h;
+    VP_CUDA((gemm_launch<FMT, MODE_RESID>(c->down, p, st)));
+  }
+  if (head) {
+    GemmParams p = base_params(c, c->lm, w.embed, c->s.act_h, 0);
+    p.ss_in = c->s.ss;
+    p.pval = c->s.pval;
+    p.pidx = c->s.pidx;
+    VP_CUDA((gemm_launch<FMT, MODE_ARGMAX>(c->lm, p, st)));
+  }
+  return VP_OK;
+}
+
+int launch_commit(vp_ctx* c, cudaStream_t st) {
+  CommitParams cp = {};
+  cp.nrb_lm = c->cfg.vocab / 16;
+  cp.s = c->s;
+  VP_CUDA(launch(k_commit, 1, COMMIT_THREADS, 0, st, cp));
+  return VP_OK;
+}
+
+template <int FMT>
+int verify_body(vp_ctx* c, cudaStream_t st) {
+  int r = launch_embed<FMT>(c, st, nullptr, 0, 0, 0, 0);
+  if (r) return r;
+  return launch_layers_and_head<FMT>(c, st, true);
+}
+
+int dispatch_verify(vp_ctx* c, cudaStream_t st) {
+  switch (c->cfg.format) {
+    case VP_FMT_Q4: return verify_body<VP_FMT_Q4>(c, st);
+    case VP_FMT_Q8: return verify_body<VP_FMT_Q8>(c, st);
+    default: return verify_body<VP_FMT_F16>(c, st);
+  }
+}
+
+template <int FMT>
+int prefill_body(vp_ctx* c, const int32_t* toks, int n, cudaStream_t st) {
+  for (int c0 = 0; c0 < n; c0 += ROWS) {
+    const int cn = n - c0 < ROWS ? n - c0 : ROWS;
+    const bool last = c0 + cn == n;
+    int r = launch_embed<FMT>(c, st, toks + c0, cn, c0, n, last);
+    if (r) return r;
+    if ((r = launch_layers_and_head<FMT>(c, st, last))) return r;
+    if (last && (r = launch_commit(c, st))) return r;
+  }
+  return VP_OK;
+}
+
+int check_ctx(vp_ctx* c) {
+  if (!c) return fail(VP_ERR_ARG, "null context");
+  if (!c->have_w) return fail(VP_ERR_STATE, "weights not set");
+  VP_CUDA(cudaSetDevice(c->cfg.device));
+  return VP_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+extern "C" {
+
+const char* vp_last_error(void) { return g_err.c_str(); }
+
+size_t vp_packed_bytes(int32_t format, int32_t rows, int32_t cols) {
+  if (rows <= 0 || cols <= 0 || rows % 16 || cols % GS) return 0;
+  if (format != VP_FMT_Q4 && format != VP_FMT_Q8 && format != VP_FMT_F16) return 0;
+  return (size_t)(rows / 16) * (cols / GS) * tile_bytes(format);
+}
+
+int vp_pack_matrix(int32_t format, int32_t kind, int32_t rows, int32_t cols, const void* d_codes,
+                   const void* d_scales, void* d_out, void* stream) {
+  if (!vp_packed_bytes(format, rows, cols)) return fail(VP_ERR_ARG, "bad format or shape");
+  if (!d_codes || !d_out || (format != VP_FMT_F16 && !d_scales)) return fail(VP_ERR_ARG, "null buffer");
+  if (kind == VP_MAT_QKV && (rows != QKV || cols != H)) return fail(VP_ERR_ARG, "QKV must be 1152x896");
+  if (kind == VP_MAT_GATEUP && (rows != 2 * F || cols != H)) return fail(VP_ERR_ARG, "gate/up must be 9728x896");
+  if (kind < 0 || kind > 2) return fail(VP_ERR_ARG, "bad kind");
+  const long long threads = (long long)(rows / 16) * (cols / GS) * 33;
+  const int block = 256;
+  const int grid = (int)((threads + block - 1) / block);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* cd = static_cast<const uint8_t*>(d_codes);
+  const uint8_t* sc = static_cast<const uint8_t*>(d_scales);
+  uint8_t* out = static_cast<uint8_t*>(d_out);
+  if (format == VP_FMT_Q4) k_pack<VP_FMT_Q4><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
+  else if (format == VP_FMT_Q8) k_pack<VP_FMT_Q8><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
+  else k_pack<VP_FMT_F16><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
+  VP_CUDA(cudaGetLastError());
+  return VP_OK;
+}
+
+int vp_create(const vp_config* cfg, vp_ctx** out) {
+  if (!cfg || !out) return fail(VP_ERR_ARG, "null argument");
+  *out = nullptr;
+  if (cfg->format != VP_FMT_Q4 && cfg->format != VP_FMT_Q8 && cfg->format != VP_FMT_F16)
+    return fail(VP_ERR_ARG, "format must be q4, q8 or f16");
+  if (cfg->n_layers < 1 || cfg->n_layers > VP_MAX_LAYERS) return fail(VP_ERR_ARG, "n_layers out of range");
+  if (cfg->vocab < 16 || cfg->vocab % 16) return fail(VP_ERR_ARG, "vocab must be a positive multiple of 16");
+  if (cfg->max_ctx < ROWS || cfg->max_ctx > (1 << 20)) return fail(VP_ERR_ARG, "max_ctx out of range");
+  if (cfg->max_steps < 1 || cfg->max_steps > (1 << 24)) return fail(VP_ERR_ARG, "max_steps out of range");
+  VP_CUDA(cudaSetDevice(cfg->device));
+  vp_ctx* c = new vp_ctx();
+  c->cfg = *cfg;
+  const int fmt = cfg->format;
+  c->qkv = make_stage(fmt, QKV, H, 7);
+  c->o = make_stage(fmt, H, H, 7);
+  c->gu = make_stage(fmt, 2 * F, H, 1);
+  c->down = make_stage(fmt, H, F, 19);
+  c->lm = make_stage(fmt, cfg->vocab, H, 1);
+  c->lm.cps = 296 < (c->lm.nrb + 3) / 4 ? 296 : (c->lm.nrb + 3) / 4;
+  c->max_chunks = (cfg->max_ctx + ATT_CHUNK - 1) / ATT_CHUNK + 1;
+  c->att_grid = 296;
+
+  Scratch& s = c->s;
+  s.max_ctx = cfg->max_ctx;
+  s.max_steps = cfg->max_steps;
+  s.vocab = cfg->vocab;
+  s.n_layers = cfg->n_layers;
+  const size_t kv = (size_t)cfg->n_layers * NKV * cfg->max_ctx * HD * sizeof(__half);
+  size_t part_units = 0;
+  for (const StageCfg* sc : {&c->qkv, &c->o, &c->down})
+    part_units = (size_t)sc->nrb * sc->nsplit > part_units ? (size_t)sc->nrb * sc->nsplit : part_units;
+  int r = VP_OK;
+  if ((r = dalloc(c, &s.st, sizeof(vp_state))) || (r = dalloc(c, &s.ri, sizeof(RowInfo))) ||
+      (r = dalloc(c, &s.tree, VP_TREE_INTS * sizeof(int32_t))) ||
+      (r = dalloc(c, &s.out_tokens, (size_t)cfg->max_steps * sizeof(int32_t))) ||
+      (r = dalloc(c, &s.x, ROWS * H * sizeof(float))) || (r = dalloc(c, &s.q, ROWS * H * sizeof(float))) ||
+      (r = dalloc(c, &s.act_h, ROWS * H * sizeof(__half))) ||
+      (r = dalloc(c, &s.act_a, ROWS * H * sizeof(__half))) ||
+      (r = dalloc(c, &s.act_f, ROWS * F * sizeof(__half))) ||
+      (r = dalloc(c, &s.ss, HRB * ROWS * sizeof(float))) ||
+      (r = dalloc(c, &s.part, part_units * 256 * sizeof(float))) ||
+      (r = dalloc(c, &s.tickets, 2048 * sizeof(int))) ||
+      (r = dalloc(c, &s.att_part, (size_t)ROWS * NKV * c->max_chunks * ATT_REC * sizeof(float))) ||
+      (r = dalloc(c, &s.kc, kv)) || (r = dalloc(c, &s.vc, kv)) ||
+      (r = dalloc(c, &s.rope, (size_t)(cfg->max_ctx + ROWS) * 32 * sizeof(float2))) ||
+      (r = dalloc(c, &s.pval, (size_t)ROWS * (cfg->vocab / 16) * sizeof(float))) ||
+      (r = dalloc(c, &s.pidx, (size_t)ROWS * (cfg->vocab / 16) * sizeof(int)))) {
+    vp_destroy(c);
+    return r;
+  }
+  // RoPE table: angle = position * theta^(-2i/64) in double, cos/sin rounded once to fp32
+  // (tools/reference/qwen_ref.py:107-116).
+  {
+    std::vector<float2> tab((size_t)(cfg->max_ctx + ROWS) * 32);
+    for (int p = 0; p < cfg->max_ctx + ROWS; ++p)
+      for (int i = 0; i < 32; ++i) {
+        const double inv = 1.0 / std::pow(1000000.0, (double)(2 * i) / 64.0);
+        const double a = (double)p * inv;
+        tab[(size_t)p * 32 + i] = make_float2((float)std::cos(a), (float)std::sin(a));
+      }
+    cudaError_t e = cudaMemcpy(s.rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { vp_destroy(c); return fail(VP_ERR_CUDA, cudaGetErrorString(e)); }
+  }
+  if (fmt == VP_FMT_Q4) r = set_attrs<VP_FMT_Q4>(c);
+  else if (fmt == VP_FMT_Q8) r = set_attrs<VP_FMT_Q8>(c);
+  else r = set_attrs<VP_FMT_F16>(c);
+  if (r) { vp_destroy(c); return r; }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->cap, cudaStreamNonBlocking);
+  if (e != cudaSuccess) { vp_destroy(c); return fail(VP_ERR_CUDA, cudaGetErrorString(e)); }
+  *out = c;
+  return VP_OK;
+}
+
+void vp_destroy(vp_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->cfg.device);
+  if (c->pass_exec) cudaGraphExecDestroy(c->pass_exec);
+  if (c->cap) cudaStreamDestroy(c->cap);
+  for (void* p : c->allocs) cudaFree(p);
+  delete c;
+}
+
+int vp_set_weights(vp_ctx* c, const vp_weights* w) {
+  if (!c || !w) return fail(VP_ERR_ARG, "null argument");
+  if (!w->embed || !w->final_norm) return fail(VP_ERR_ARG, "embed / final_norm missing");
+  for (int l = 0; l < c->cfg.n_layers; ++l)
+    if (!w->wqkv[l] || !w->bqkv[l] || !w->wo[l] || !w->wgu[l] || !w->wd[l] || !w->ln1[l] || !w->ln2[l])
+      return fail(VP_ERR_ARG, "layer weight missing");
+  c->w = *w;
+  c->have_w = true;
+  if (c->pass_exec) {  // pointers are baked into the graph
+    cudaGraphExecDestroy(c->pass_exec);
+    c->pass_exec = nullptr;
+  }
+  return VP_OK;
+}
+
+int vp_begin(vp_ctx* c, int32_t cached, int32_t max_new, int32_t eos0, int32_t eos1, void* stream) {
+  if (!c) return fail(VP_ERR_ARG, "null context");
+  if (cached < 0 || max_new < 1 || max_new > c->cfg.max_steps) return fail(VP_ERR_ARG, "bad request size");
+  if (cached + max_new + ROWS > c->cfg.max_ctx) return fail(VP_ERR_ARG, "request exceeds max_ctx");
+  VP_CUDA(cudaSetDevice(c->cfg.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int last = 0;
+  launch(k_begin, 64, 256, 0, st, c->s.st, c->s.out_tokens, c->cfg.max_steps, (int)cached,
+         (int)max_new, (int)eos0, (int)eos1, c->cfg.max_ctx, last);
+  VP_CUDA(cudaGetLastError());
+  return VP_OK;
+}
+
+int vp_prefill(vp_ctx* c, const int32_t* d_tokens, int32_t n, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!d_tokens || n < 1) return fail(VP_ERR_ARG, "empty prompt");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (c->cfg.format) {
+    case VP_FMT_Q4: return prefill_body<VP_FMT_Q4>(c, d_tokens, n, st);
+    case VP_FMT_Q8: return prefill_body<VP_FMT_Q8>(c, d_tokens, n, st);
+    default: return prefill_body<VP_FMT_F16>(c, d_tokens, n, st);
+  }
+}
+
+int vp_verify(vp_ctx* c, const int32_t* tree, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!tree) return fail(VP_ERR_ARG, "null tree");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
+  return dispatch_verify(c, st);
+}
+
+int vp_verify_chain(vp_ctx* c, const int32_t* drafts, int32_t nd, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (nd < 0 || nd > ROWS - 1 || (nd > 0 && !drafts)) return fail(VP_ERR_ARG, "bad draft count");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  k_chain_tree<<<1, 32, 0, st>>>(c->s.tree, drafts, nd);
+  VP_CUDA(cudaGetLastError());
+  return dispatch_verify(c, st);
+}
+
+int vp_commit(vp_ctx* c, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  return launch_commit(c, static_cast<cudaStream_t>(stream));
+}
+
+int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!tree) return fail(VP_ERR_ARG, "null tree");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!c->pass_exec) {
+    cudaGraph_t g = nullptr;
+    VP_CUDA(cudaStreamBeginCapture(c->cap, cudaStreamCaptureModeThreadLocal));
+    r = dispatch_verify(c, c->cap);
+    if (!r) r = launch_commit(c, c->cap);
+    cudaError_t e = cudaStreamEndCapture(c->cap, &g);
+    if (r) { if (g) cudaGraphDestroy(g); return r; }
+    if (e != cudaSuccess) return fail(VP_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&c->pass_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { c->pass_exec = nullptr; return fail(VP_ERR_CUDA, cudaGetErrorString(e)); }
+  }
+  VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
+  VP_CUDA(cudaGraphLaunch(c->pass_exec, st));
+  return VP_OK;
+}
+
+int vp_read_state(vp_ctx* c, vp_state* host, void* stream) {
+  if (!c || !host) return fail(VP_ERR_ARG, "null argument");
+  VP_CUDA(cudaSetDevice(c->cfg.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  VP_CUDA(cudaMemcpyAsync(host, c->s.st, sizeof(vp_state), cudaMemcpyDeviceToHost, st));
+  VP_CUDA(cudaStreamSynchronize(st));
+  return host->err ? VP_ERR_DEVICE : VP_OK;
+}
+
+int vp_read_tokens(vp_ctx* c, int32_t* host, int32_t count, void* stream) {
+  if (!c || !host || count < 0 || count > c->cfg.max_steps) return fail(VP_ERR_ARG, "bad argument");
+  VP_CUDA(cudaSetDevice(c->cfg.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  VP_CUDA(cudaMemcpyAsync(host, c->s.out_tokens, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  VP_CUDA(cudaStreamSynchronize(st));
+  return VP_OK;
+}
+
+int32_t* vp_device_tokens(vp_ctx* c) { return c ? c->s.out_tokens : nullptr; }
+vp_state* vp_device_state(vp_ctx* c) { return c ? c->s.st : nullptr; }
+
+int vp_debug_logits(vp_ctx* c, float* d_out, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!d_out) return fail(VP_ERR_ARG, "null output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmParams p = base_params(c, c->lm, c->w.embed, c->s.act_h, 0);
+  p.ss_in = c->s.ss;
+  p.pval = c->s.pval;
+  p.pidx = c->s.pidx;
+  p.dbg = d_out;
+  switch (c->cfg.format) {
+    case VP_FMT_Q4: VP_CUDA((gemm_launch<VP_FMT_Q4, MODE_ARGMAX>(c->lm, p, st))); break;
+    case VP_FMT_Q8: VP_CUDA((gemm_launch<VP_FMT_Q8, MODE_ARGMAX>(c->lm, p, st))); break;
+    default: VP_CUDA((gemm_launch<VP_FMT_F16, MODE_ARGMAX>(c->lm, p, st))); break;
+  }
+  return VP_OK;
+}
+
+int vp_buffer(vp_ctx* c, int32_t which, void** ptr, size_t* bytes) {
+  if (!c || !ptr || !bytes) return fail(VP_ERR_ARG, "null argument");
+  const size_t kv = (size_t)c->cfg.n_layers * NKV * c->cfg.max_ctx * HD * sizeof(__half);
+  const size_t pv = (size_t)ROWS * (c->cfg.vocab / 16) * 4;
+  switch (which) {
+    case 0: *ptr = c->s.x; *bytes = ROWS * H * 4; break;
+    case 1: *ptr = c->s.q; *bytes = ROWS * H * 4; break;
+    case 2: *ptr = c->s.kc; *bytes = kv; break;
+    case 3: *ptr = c->s.vc; *bytes = kv; break;
+    case 4: *ptr = c->s.pval; *bytes = pv; break;
+    case 5: *ptr = c->s.pidx; *bytes = pv; break;
+    default: return fail(VP_ERR_ARG, "unknown buffer");
+  }
+  return VP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,211 @@
+"""VerifyEngine: host side of the verification pass, mirroring the reference's Engine operator
+surface (Sources/Engine/Engine.swift) on top of the C ABI (include/vpass.h).
+
+    Engine.init(modelPath:...)          -> VerifyEngine(weights, max_ctx=..., max_steps=...)
+    generate() state init  (:937-964)   -> begin(cached, max_new, eos)
+    encodePrefill          (:588-601)   -> prefill(tokens)
+    encodeWidePass         (:567-579)   -> verify(tree) / verify_chain(drafts)
+    encodeCommitSpec       (:484-497)   -> commit()
+    wide pass + commit as one unit      -> pass_(tree)    (CUDA graph replay)
+    generate()             (:922-1038)  -> generate(prompt, max_new, tree_fn)
+
+PyTorch only provides device memory and the stream; all compute is the CUDA library.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import FMT, MAT_GATEUP, MAT_PLAIN, MAT_QKV, VpConfig, VpState, VpWeights, check
+from .synth import STOP_IDS, TREE_INTS, tree_to_buffer
+
+
+class _DevArray:
+    """Zero-copy torch view of a raw device pointer (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2}
+
+
+def _np_to_dev(a: np.ndarray, device) -> torch.Tensor:
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.float16:
+        a = a.view(np.uint16)
+    return torch.from_numpy(a.view(np.uint8).reshape(-1)).to(device)
+
+
+class VerifyEngine:
+    def __init__(self, weights: dict, max_ctx: int = 4096, max_steps: int = 4096, device: int = 0):
+        self.lib = _lib.load()
+        self.device = torch.device("cuda", device)
+        torch.cuda.set_device(self.device)
+        self.fmt = weights["fmt"]
+        if self.fmt not in FMT:
+            raise ValueError(f"the GPU path runs q4, q8 or f16 weights, not {self.fmt}")
+        self.n_layers = weights["n_layers"]
+        self.vocab = weights["vocab"]
+        self.max_ctx, self.max_steps = max_ctx, max_steps
+        self._keep = []
+        self._staging = []
+        self.stream = torch.cuda.current_stream(self.device)
+        w = VpWeights()
+        w.embed = self._pack(weights["embed"], MAT_PLAIN)
+        w.final_norm = self._vec(weights["final_norm"])
+        for l, L in enumerate(weights["layers"]):
+            w.wqkv[l] = self._pack(L["wqkv"], MAT_QKV)
+            w.bqkv[l] = self._vec(L["bqkv"])
+            w.wo[l] = self._pack(L["wo"], MAT_PLAIN)
+            w.wgu[l] = self._pack(L["wgu"], MAT_GATEUP)
+            w.wd[l] = self._pack(L["wd"], MAT_PLAIN)
+            w.ln1[l] = self._vec(L["ln1"])
+            w.ln2[l] = self._vec(L["ln2"])
+        torch.cuda.synchronize(self.device)
+        self._staging = []  # standard-layout uploads are no longer needed
+        cfg = VpConfig(FMT[self.fmt], self.n_layers, self.vocab, max_ctx, max_steps, device)
+        ctx = ctypes.c_void_p()
+        check(self.lib.vp_create(ctypes.byref(cfg), ctypes.byref(ctx)), "vp_create")
+        self.ctx = ctx
+        check(self.lib.vp_set_weights(self.ctx, ctypes.byref(w)), "vp_set_weights")
+        self._weights_struct = w
+        self._prompt = torch.empty(max_ctx, dtype=torch.int32, device=self.device)
+        self._tree_host = torch.empty(TREE_INTS, dtype=torch.int32).pin_memory()
+
+    # ---- weights ----
+    def _pack(self, m: dict, kind: int) -> int:
+        fmt = FMT[self.fmt]
+        if m["fmt"] != self.fmt:
+            raise ValueError("mixed weight formats")
+        if self.fmt == "f16":
+            rows, cols = m["w"].shape
+            codes, scales = _np_to_dev(m["w"], self.device), None
+        else:
+            rows = m["codes"].shape[0]
+            cols = m["codes"].shape[1] * (2 if self.fmt == "q4" else 1)
+            codes = _np_to_dev(m["codes"], self.device)
+            scales = _np_to_dev(m["scales"], self.device)
+        nbytes = self.lib.vp_packed_bytes(fmt, rows, cols)
+        out = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        check(self.lib.vp_pack_matrix(fmt, kind, rows, cols, codes.data_ptr(),
+                                      scales.data_ptr() if scales is not None else None,
+                                      out.data_ptr(), self.stream.cuda_stream), "vp_pack_matrix")
+        self._keep.append(out)
+        self._staging.append((codes, scales))  # released once the pack kernels have run
+        return out.data_ptr()
+
+    def _vec(self, a: np.ndarray) -> int:
+        t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.device)
+        self._keep.append(t)
+        return t.data_ptr()
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None):
+            self.lib.vp_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- operator surface ----
+    @property
+    def _s(self):
+        return self.stream.cuda_stream
+
+    def begin(self, cached: int, max_new: int, eos=STOP_IDS) -> None:
+        check(self.lib.vp_begin(self.ctx, cached, max_new, eos[0], eos[1], self._s), "vp_begin")
+
+    def prefill(self, tokens) -> None:
+        toks = torch.as_tensor(np.asarray(tokens, dtype=np.int32))
+        n = int(toks.numel())
+        self._prompt[:n].copy_(toks, non_blocking=False)
+        check(self.lib.vp_prefill(self.ctx, self._prompt.data_ptr(), n, self._s), "vp_prefill")
+
+    def _tree_ptr(self, tree) -> int:
+        buf = tree if isinstance(tree, np.ndarray) else tree_to_buffer(tree)
+        self.stream.synchronize()  # the pinned staging buffer is reused
+        self._tree_host.copy_(torch.from_numpy(np.asarray(buf, dtype=np.int32)))
+        return self._tree_host.data_ptr()
+
+    def verify(self, tree) -> None:
+        check(self.lib.vp_verify(self.ctx, self._tree_ptr(tree), self._s), "vp_verify")
+
+    def verify_chain(self, drafts) -> None:
+        d = torch.as_tensor(np.asarray(drafts, dtype=np.int32)).to(self.device)
+        self._keep_chain = d
+        check(self.lib.vp_verify_chain(self.ctx, d.data_ptr() if d.numel() else None, int(d.numel()),
+                                       self._s), "vp_verify_chain")
+
+    def commit(self) -> None:
+        check(self.lib.vp_commit(self.ctx, self._s), "vp_commit")
+
+    def pass_(self, tree) -> None:
+        check(self.lib.vp_pass(self.ctx, self._tree_ptr(tree), self._s), "vp_pass")
+
+    def pass_device(self, tree_dev: torch.Tensor) -> None:
+        """Graph pass with a device-resident tree buffer (no host round trip)."""
+        check(self.lib.vp_pass(self.ctx, tree_dev.data_ptr(), self._s), "vp_pass")
+
+    # ---- results ----
+    def state(self) -> dict:
+        st = VpState()
+        rc = self.lib.vp_read_state(self.ctx, ctypes.byref(st), self._s)
+        d = st.as_dict()
+        if rc not in (0, -5):
+            check(rc, "vp_read_state")
+        return d
+
+    def tokens(self, count: Optional[int] = None) -> list:
+        st = self.state()
+        count = st["step"] if count is None else count
+        out = np.empty(count, np.int32)
+        if count:
+            check(self.lib.vp_read_tokens(self.ctx, out.ctypes.data, count, self._s), "vp_read_tokens")
+        return out.tolist()
+
+    def buffer(self, which: int, shape, dtype: str) -> torch.Tensor:
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+        check(self.lib.vp_buffer(self.ctx, which, ctypes.byref(ptr), ctypes.byref(nbytes)), "vp_buffer")
+        return torch.as_tensor(_DevArray(ptr.value, shape, dtype), device=self.device)
+
+    def kv(self):
+        shape = (self.n_layers, 2, self.max_ctx, 64)
+        return self.buffer(2, shape, "<f2"), self.buffer(3, shape, "<f2")
+
+    def logits(self) -> torch.Tensor:
+        """fp32 logits [16, vocab] of the rows of the last pass (parity helper)."""
+        out = torch.empty((16, self.vocab), dtype=torch.float32, device=self.device)
+        check(self.lib.vp_debug_logits(self.ctx, out.data_ptr(), self._s), "vp_debug_logits")
+        return out
+
+    # ---- generate (Engine.generate, Engine.swift:922-1038) ----
+    def generate(self, prompt, max_new: int, tree_fn: Optional[Callable] = None, eos=STOP_IDS,
+                 use_graph: bool = True) -> dict:
+        """Prefill `prompt`, then verify passes until max_new tokens or a stop token. tree_fn(out)
+        returns the next pass's tree given the tokens committed so far (None: 1-row passes, i.e.
+        plain greedy decoding through the same kernels, the reference's noDraft run)."""
+        from .synth import root_tree
+
+        self.begin(0, max_new, eos)
+        self.prefill(prompt)
+        st = self.state()
+        passes = 0
+        while not st["done"]:
+            out = self.tokens(st["step"])
+            tree = tree_fn(out) if tree_fn else root_tree()
+            if use_graph:
+                self.pass_(tree)
+            else:
+                self.verify(tree)
+                self.commit()
+            passes += 1
+            st = self.state()
+            if st["err"]:
+                raise _lib.VpError(f"device error bits {st['err']}")
+        return {"tokens": self.tokens(st["step"]), "passes": passes, "state": st}
