@@ -1,0 +1,383 @@
+#!/usr/bin/env python3
+"""Benchmark of the q4 16-row tree-verify pass on 1..8 B200s.
+
+One step = one 16-row tree verify pass + greedy accept/commit of one request (prefill of a
+256-token prompt happens before timing, so the prefix is cached). Trees follow BASELINE config 2:
+root + 15 drafts, parents uniform among earlier nodes of depth < 8, drafts equal to the parent's
+true argmax with p = 0.6. The "true argmax" comes from a prior sequential run of the same request
+through the same kernels (1-row passes), and the committed tokens of the timed tree passes are
+checked against it (tree == sequential) at the end of the run.
+
+value  = accepted (committed) tokens per second over all ranks, inputs resident in HBM.
+e2e    = the same through the C ABI with the tree in pinned host memory and the committed
+         state / tokens read back to the host every step.
+N > 1  = one independent request per rank (request-level sharding, weak scaling, no collective on
+         the data path; torch.distributed is used only for the barrier and the max-time reduce).
+
+--impl reference times the reference's CPU path (the numpy fp32 restatement in oracle/, a port of
+tools/reference/qwen_ref.py: the Swift/Metal engine cannot run here) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "q4 16-row tree-verify pass µs & accepted tok/s; HBM GB/s vs B200 peak"
+PREFIX = 256
+ROWS = 16
+L2_NOTE = "weights (278 MB/pass) exceed the 126 MB L2: no flush needed"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+# workload
+
+
+def plan_trees(y_full, start: int, n_steps: int, seed: int):
+    """Trees for n_steps passes starting after y_full[:start] is committed. Returns (tree buffers,
+    committed counts, expected token stream)."""
+    from instantllm_b200 import synth
+    from oracle import accept as A
+
+    rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, 4242])))
+    pos, bufs, counts = start, [], []
+    for _ in range(n_steps):
+        y = y_full[pos:pos + 9]
+        if len(y) < 9:
+            raise RuntimeError("sequential run too short for the tree plan")
+        tree = synth.seeded_tree(rng, y, n=ROWS)
+        parents, tokens = A.to_python_numbering(tree)
+        a = A.accept_tree(parents, tokens, list(y), 0)
+        bufs.append(synth.tree_to_buffer(tree))
+        counts.append(a + 1)
+        pos += a + 1
+    return np.stack(bufs), counts, pos
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    from instantllm_b200 import synth
+    from instantllm_b200.engine import VerifyEngine
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    t_setup = time.time()
+    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    n_steps = args.warmup + args.steps
+    seq_len = min(4096 - PREFIX - 64, n_steps * 9 + 16)
+    eng = VerifyEngine(w, max_ctx=4096, max_steps=4096, device=local)
+    prompt = synth.make_prompt(PREFIX, seed=1000 + rank)
+    no_eos = (-1, -1)
+
+    # 1) sequential reference run (1-row passes through the same kernels), untimed
+    eng.begin(0, seq_len, no_eos)
+    eng.prefill(prompt)
+    tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
+    for _ in range(seq_len - 1):
+        eng.pass_device(tree1)
+    y_full = eng.tokens(seq_len)
+
+    # 2) tree plan for warm-up + timed passes
+    trees, counts, _ = plan_trees(y_full, 1, n_steps, args.seed + rank)
+    trees_dev = torch.tensor(trees, device=dev)
+    n_tok_timed = int(sum(counts[args.warmup:]))
+
+    eng.begin(0, seq_len, no_eos)
+    eng.prefill(prompt)
+    for i in range(args.warmup):
+        eng.pass_device(trees_dev[i])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    s = eng.stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.warmup, n_steps):
+        eng.pass_device(trees_dev[i])
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    st = eng.state()
+    got = eng.tokens(st["step"])
+    ok = got == y_full[:len(got)] and st["step"] == 1 + sum(counts)
+
+    # 3) end to end through the C ABI: host tree in, state + tokens out every step
+    eng.begin(0, seq_len, no_eos)
+    eng.prefill(prompt)
+    for i in range(args.warmup):
+        eng.pass_(trees[i])
+        eng.state()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_tok = 0
+    for i in range(args.warmup, n_steps):
+        eng.pass_(trees[i])  # pinned host tree -> device inside vp_pass
+        stt = eng.state()
+        _ = eng.tokens(stt["step"]) if i == n_steps - 1 else None
+        e2e_tok += counts[i]
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    return dict(ms=ms, tok=n_tok_timed, ok=ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,
+                setup_s=time.time() - t_setup, eng=eng, w=w, prompt=prompt, y=y_full, trees=trees,
+                counts=counts)
+
+
+def cpu_baseline(w, prompt, y_full, trees, seconds: float) -> dict:
+    """The oracle (numpy fp32 port of the reference CPU path) on a bounded sample of the same
+    workload: tree passes over the same trees after the same 256-token prefix."""
+    from oracle import accept as A
+    from oracle import qwen_oracle as Q
+
+    m = Q.model_from_weights(w)
+    cache = Q.KVCache(len(m.layers), 4096)
+    logits = Q.forward_causal(m, cache, list(prompt), 0)
+    last = int(np.argmax(logits))
+    pos, step, tok, passes = PREFIX, 1, 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds and passes < len(trees):
+        tb = trees[passes]
+        n = int(tb[0])
+        tree = {"n": n, "depth": list(tb[1:17]), "parent": list(tb[17:33]), "tok": list(tb[33:49])}
+        lg = Q.tree_pass(m, cache, pos, last, tree)
+        g = lg.argmax(axis=1)
+        res = A.commit(tree, g, pos, step, 1 << 30, eos=())
+        for src, dst in res["moves"]:
+            for li in range(len(m.layers)):
+                cache.k[li][:, dst] = cache.k[li][:, src]
+                cache.v[li][:, dst] = cache.v[li][:, src]
+        pos, step = res["pos"], res["step"]
+        last = res["tokens"][-1]
+        tok += len(res["tokens"])
+        passes += 1
+    dt = time.perf_counter() - t0
+    threads = os.cpu_count()
+    return {"value": tok / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{passes} q4 16-row tree passes (fp32 numpy, dequantised weights) after a "
+                      f"{PREFIX}-token prefix, {dt:.1f} s", "pass_ms": 1000 * dt / max(passes, 1)}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (numpy fp32 port) times the same workload."""
+    from instantllm_b200 import synth
+    from oracle import accept as A
+    from oracle import qwen_oracle as Q
+
+    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    m = Q.model_from_weights(w)
+    prompt = synth.make_prompt(PREFIX, seed=1000)
+    n_steps = args.warmup + args.steps
+    cache = Q.KVCache(len(m.layers), 4096)
+    logits = Q.forward_causal(m, cache, list(prompt), 0)
+    # true continuation for the tree plan: the CPU model's own sequential greedy run
+    y, pos = [int(np.argmax(logits))], PREFIX
+    seq_cache = cache.copy()
+    need = 9 * min(n_steps, 12) + 9  # extended lazily below
+    while len(y) < need:
+        lg = Q.forward_causal(m, seq_cache, [y[-1]], pos)
+        y.append(int(np.argmax(lg)))
+        pos += 1
+    rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([args.seed, 4242])))
+    last, pos, step, ypos = y[0], PREFIX, 1, 1
+    times, toks = [], []
+    for i in range(n_steps):
+        while len(y) < ypos + 9:
+            lg = Q.forward_causal(m, seq_cache, [y[-1]], PREFIX + len(y) - 1)
+            y.append(int(np.argmax(lg)))
+        tree = synth.seeded_tree(rng, y[ypos:ypos + 9], n=ROWS)
+        t0 = time.perf_counter()
+        lg = Q.tree_pass(m, cache, pos, last, tree)
+        res = A.commit(tree, lg.argmax(axis=1), pos, step, 1 << 30, eos=())
+        for src, dst in res["moves"]:
+            for li in range(len(m.layers)):
+                cache.k[li][:, dst] = cache.k[li][:, src]
+                cache.v[li][:, dst] = cache.v[li][:, src]
+        dt = time.perf_counter() - t0
+        pos, step, last = res["pos"], res["step"], res["tokens"][-1]
+        ypos += len(res["tokens"])
+        if i >= args.warmup:
+            times.append(dt)
+            toks.append(len(res["tokens"]))
+    total = sum(times)
+    v = sum(toks) / total
+    line = {
+        "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * total / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2: q4 16-row tree verify + commit, 256-token cached prefix",
+                   "rows": ROWS, "prefix": PREFIX, "layers": args.layers},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{len(times)} tree passes on the numpy fp32 port of "
+                                   "tools/reference/qwen_ref.py (the Swift/Metal engine needs an Apple GPU)"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+    import torch
+
+    from instantllm_b200 import synth
+
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=__import__("datetime").timedelta(seconds=300))
+    r = run_ours(args, rank, world, local)
+    ms, tok = r["ms"], r["tok"]
+    e2e_s, e2e_tok = r["e2e_s"], r["e2e_tok"]
+    ok = 1.0 if r["ok"] else 0.0
+    if world > 1:
+        t = torch.tensor([ms, float(tok), e2e_s, float(e2e_tok), ok], device="cuda", dtype=torch.float64)
+        mx = t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        sm = t.clone()
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        mn = t.clone()
+        torch.distributed.all_reduce(mn, op=torch.distributed.ReduceOp.MIN)
+        ms, tok, e2e_s, e2e_tok = mx[0].item(), sm[1].item(), mx[2].item(), sm[3].item()
+        ok = mn[4].item()
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        wbytes = synth.weight_bytes("q4", args.layers)
+        pass_ms = r["ms"] / args.steps
+        avg_L = PREFIX + 1 + (np.mean(np.cumsum(r["counts"])[args.warmup:]) if args.steps else 0)
+        kv_bytes = 12288 * avg_L * args.layers / 24 + 12288 * ROWS * args.layers / 24
+        alg = wbytes + kv_bytes
+        achieved = alg / (pass_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": tok / (ms * 1e-3),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q4 weights, fp16 activations, fp32 accumulate",
+            "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
+            "config": {"workload": "BASELINE config 2: q4 16-row tree verify + greedy commit, "
+                                   "256-token cached prefix, one request per GPU",
+                       "rows": ROWS, "prefix": PREFIX, "layers": args.layers, "l2": L2_NOTE,
+                       "parallelism": f"request sharding x{world}"},
+            "pass_us": 1000 * pass_ms,
+            "tokens_per_pass": tok / max(1, args.steps * world),
+            "hbm_gbs": achieved,
+            "tree_equals_sequential": bool(ok),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None,
+                         "kernel": "whole verify pass (CUDA graph, rank 0)",
+                         "bytes_per_launch": alg, "peak_kind": peak_kind},
+            "e2e": {"value": e2e_tok / e2e_s, "unit": "tok/s",
+                    "h2d_bytes_per_step": 65 * 4, "d2h_bytes_per_step": 64},
+            "gpu_launches": 123 * args.steps,
+            "clocks": r["clocks"],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(r["w"], r["prompt"], r["y"], r["trees"], args.cpu_seconds)
+        else:
+            line["cpu_baseline"] = None
+        print(json.dumps(line), flush=True)
+    r["eng"].close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -124,6 +124,8 @@ class VerifyEngine:
     def prefill(self, tokens) -> None:
         toks = torch.as_tensor(np.asarray(tokens, dtype=np.int32))
         n = int(toks.numel())
+        if n > self._prompt.numel():  # the device checks the context bound, not this buffer
+            self._prompt = torch.empty(n, dtype=torch.int32, device=self.device)
         self._prompt[:n].copy_(toks, non_blocking=False)
         check(self.lib.vp_prefill(self.ctx, self._prompt.data_ptr(), n, self._s), "vp_prefill")
 

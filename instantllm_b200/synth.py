@@ -96,12 +96,15 @@ def tree_to_buffer(tree: dict) -> np.ndarray:
         buf[1 + i] = tree["depth"][i]
         buf[17 + i] = tree["parent"][i]
         buf[33 + i] = tree["tok"][i]
-        anc, cur = 0, i
-        while True:
-            anc |= 1 << cur
-            if cur == 0:
+        # ancestor mask incl. the row itself; a malformed parent link only truncates the walk
+        # (the device validates the tree and reports it)
+        anc, cur = 1 << i, i
+        for _ in range(16):
+            par = tree["parent"][cur] if cur > 0 else -1
+            if not 0 <= par < cur:
                 break
-            cur = tree["parent"][cur]
+            anc |= 1 << par
+            cur = par
         buf[49 + i] = anc
     return buf
 

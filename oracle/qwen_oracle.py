@@ -191,11 +191,13 @@ def forward_rows(model: Model, cache: KVCache, tokens, rope_pos, slots, attend, 
 
 
 def forward_causal(model: Model, cache: KVCache, tokens, pos0: int, all_logits=False):
-    """Causal rows at slots/positions pos0.. (qwen_ref.Qwen2Ref.forward, qwen_ref.py:118-194)."""
+    """Causal rows at slots/positions pos0.. (qwen_ref.Qwen2Ref.forward, qwen_ref.py:118-194).
+    Returns logits [n, V] if all_logits else [V] of the last row."""
     n = len(tokens)
     pos = np.arange(pos0, pos0 + n)
     attend = [np.arange(0, p + 1) for p in pos]
-    return forward_rows(model, cache, tokens, pos, pos, attend, all_logits=all_logits)
+    lg = forward_rows(model, cache, tokens, pos, pos, attend, all_logits=all_logits)
+    return lg if all_logits else lg[0]
 
 
 def greedy(model: Model, prompt, max_new: int, stop_ids=(151645, 151643), max_len=None):
