@@ -176,6 +176,26 @@ int vp_debug_logits(vp_ctx* ctx, float* d_out, void* stream);
  * 5 argmax ids int32[16][vocab/16]. */
 int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
 
+/* ---- greedy lm-head argmax that allocates nothing ----
+ * No counterpart in the reference (instantllm always owns its buffers); it exists for callers
+ * that cannot allocate device memory: hosts whose device memory is entirely handed out by their
+ * own pool or budget, and serving loops where a cudaMalloc / cudaFree would stall other work on
+ * the device. tokens[r] = argmax_v of (RMSNorm(x[r]) * final_norm) . E[v] for r < rows (the tied
+ * lm_head; lowest id on ties), the same arithmetic as the pass's own lm_head.
+ *   format  VP_FMT_*; embed is the packed [vocab][896] matrix (vp_pack_matrix, VP_MAT_PLAIN)
+ *   x       fp32 [rows][896] residual rows (device); tokens int32 [rows] (device)
+ *   limits  1 <= rows <= VP_MAX_ROWS; vocab a multiple of 16, <= VP_NOALLOC_MAX_VOCAB;
+ *           larger sizes return VP_ERR_ARG.
+ * Scratch is one static device array inside the library (about 1.4 MiB, held by every GPU that
+ * loads the library until the process exits). The first call on a device looks the array up on
+ * that device (make that first call before any stream capture). All calls share the array:
+ * calls whose work overlaps on the GPU (other streams, other threads) race, so serialise them.
+ * Runs on the current device and `stream`; reports a device-side timeout as token -1. */
+#define VP_NOALLOC_MAX_VOCAB 163840
+int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void* d_embed,
+                           const float* d_final_norm, const float* d_x, int32_t rows,
+                           int32_t* d_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

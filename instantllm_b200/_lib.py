@@ -19,7 +19,7 @@ EXPORTS = (
     "vp_packed_bytes", "vp_pack_matrix", "vp_create", "vp_destroy", "vp_set_weights",
     "vp_last_error", "vp_begin", "vp_prefill", "vp_verify", "vp_verify_chain", "vp_commit",
     "vp_pass", "vp_read_state", "vp_read_tokens", "vp_device_tokens", "vp_device_state",
-    "vp_debug_logits", "vp_buffer",
+    "vp_debug_logits", "vp_buffer", "vp_head_argmax_noalloc",
 )
 
 
@@ -84,6 +84,7 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_device_state": (vp, [vp]),
         "vp_debug_logits": (ctypes.c_int, [vp, vp, vp]),
         "vp_buffer": (ctypes.c_int, [vp, i32, ctypes.POINTER(vp), ctypes.POINTER(sz)]),
+        "vp_head_argmax_noalloc": (ctypes.c_int, [i32, i32, vp, vp, vp, i32, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -497,3 +498,183 @@ int vp_buffer(vp_ctx* c, int32_t which, void** ptr, size_t* bytes) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Greedy lm-head argmax that allocates nothing (vp_head_argmax_noalloc).
+//
+// For callers that cannot call cudaMalloc: its scratch (the fp16 normed rows, the RMSNorm
+// partials, the per-16-row argmax partials and a state / row-info block) is this file-scope
+// device array. Host code must never use `g_noalloc_scratch` itself as a pointer: on the host it
+// is only a stand-in symbol. The device address is looked up once per device with
+// cudaGetSymbolAddress and passed to the kernels.
+
+namespace {
+
+constexpr size_t na_align(size_t v) { return (v + 255) & ~size_t(255); }
+constexpr size_t NA_ACT = na_align(ROWS * H * sizeof(__half));
+constexpr size_t NA_SS = na_align(HRB * ROWS * sizeof(float));
+constexpr size_t NA_ST = na_align(sizeof(vp_state));
+constexpr size_t NA_RI = na_align(sizeof(RowInfo));
+constexpr size_t NA_PART = na_align((size_t)ROWS * (VP_NOALLOC_MAX_VOCAB / 16) * 4);
+constexpr size_t NA_BYTES = NA_ACT + NA_SS + NA_ST + NA_RI + 2 * NA_PART;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+namespace {
+
+// x rows -> half(x * final_norm) act blocks and per-row-block sums of squares, with the same
+// expressions and reduction order as the residual epilogue that feeds the pass's own lm_head.
+__global__ void k_na_prep(const float* x, const float* wnorm, int rows, __half* act, float* ss,
+                          vp_state* st, RowInfo* ri) {
+  const int rb = blockIdx.x, lane = threadIdx.x, gid = lane >> 2, tid4 = lane & 3;
+  const int d0 = rb * 16 + gid, d1 = d0 + 8;
+  const float w0 = wnorm[d0], w1 = wnorm[d1];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = nt * 8 + 2 * tid4 + e;
+      float v0 = 0.f, v1 = 0.f;
+      if (t < rows) {
+        v0 = x[t * H + d0];
+        v1 = x[t * H + d1];
+      }
+      act[act_index(t, d0)] = __float2half_rn(v0 * w0);
+      act[act_index(t, d1)] = __float2half_rn(v1 * w1);
+      float sq = v0 * v0 + v1 * v1;
+      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 16);
+      if (gid == 0) ss[rb * 16 + t] = sq;
+    }
+  if (rb == 0 && lane == 0) {
+    vp_state z = {};
+    *st = z;  // the array keeps the previous call's contents: the error bits must start clear
+    ri->n = rows;
+    ri->pos = 0;
+    ri->mode = 0;
+    ri->live = 1;
+  }
+}
+
+// One CTA per row: max over the per-16-row partials, lowest id on ties.
+__global__ void k_na_argmax(const float* pval, const int* pidx, int nrb, const vp_state* st,
+                            int32_t* tokens) {
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float rv[8];
+  __shared__ int ri_[8];
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < nrb; i += 256) {
+    const float v = pval[(size_t)t * nrb + i];
+    const int id = pidx[(size_t)t * nrb + i];
+    if (v > best || (v == best && id < bi)) { best = v; bi = id; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  if (lane == 0) { rv[warp] = best; ri_[warp] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    best = rv[0];
+    bi = ri_[0];
+    for (int w = 1; w < 8; ++w)
+      if (rv[w] > best || (rv[w] == best && ri_[w] < bi)) { best = rv[w]; bi = ri_[w]; }
+    tokens[t] = st->err ? -1 : bi;
+  }
+}
+
+struct NoAllocDevice {
+  std::once_flag once;
+  void* base = nullptr;
+  int rc = VP_OK;
+  std::string msg;
+};
+NoAllocDevice g_na_dev[64];
+
+template <int FMT>
+cudaError_t na_smem_attr() {
+  const size_t need = make_stage(FMT, 16, H, 1).smem;
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, k_gemm<FMT, MODE_ARGMAX>);
+  if (e != cudaSuccess) return e;
+  if ((size_t)a.maxDynamicSharedSizeBytes >= need) return cudaSuccess;
+  return cudaFuncSetAttribute(k_gemm<FMT, MODE_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)need);
+}
+
+// Once per device, with that device current: the device address of the static scratch array.
+int na_setup(int dev, unsigned char** base) {
+  NoAllocDevice& d = g_na_dev[dev];
+  std::call_once(d.once, [&d]() {
+    cudaError_t e = cudaGetSymbolAddress(&d.base, g_noalloc_scratch);
+    if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q4>();
+    if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q8>();
+    if (e == cudaSuccess) e = na_smem_attr<VP_FMT_F16>();
+    if (e != cudaSuccess) {
+      d.base = nullptr;
+      d.rc = VP_ERR_CUDA;
+      d.msg = std::string("no-alloc set-up: ") + cudaGetErrorString(e);
+    }
+  });
+  if (d.rc != VP_OK) return fail(d.rc, d.msg);
+  *base = static_cast<unsigned char*>(d.base);
+  return VP_OK;
+}
+
+}  // namespace
+
+extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void* d_embed,
+                                      const float* d_final_norm, const float* d_x, int32_t rows,
+                                      int32_t* d_tokens, void* stream) {
+  if (format != VP_FMT_Q4 && format != VP_FMT_Q8 && format != VP_FMT_F16)
+    return fail(VP_ERR_ARG, "format must be q4, q8 or f16");
+  if (vocab < 16 || vocab % 16 || vocab > VP_NOALLOC_MAX_VOCAB)
+    return fail(VP_ERR_ARG, "vocab must be a multiple of 16 and at most VP_NOALLOC_MAX_VOCAB (163840)");
+  if (rows < 1 || rows > ROWS) return fail(VP_ERR_ARG, "rows must be 1..16");
+  if (!d_embed || !d_final_norm || !d_x || !d_tokens) return fail(VP_ERR_ARG, "null buffer");
+  int dev = 0;
+  VP_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(VP_ERR_ARG, "device ordinal above 63");
+  unsigned char* base = nullptr;
+  int r = na_setup(dev, &base);
+  if (r) return r;
+  __half* act = reinterpret_cast<__half*>(base);
+  float* ss = reinterpret_cast<float*>(base + NA_ACT);
+  vp_state* st = reinterpret_cast<vp_state*>(base + NA_ACT + NA_SS);
+  RowInfo* ri = reinterpret_cast<RowInfo*>(base + NA_ACT + NA_SS + NA_ST);
+  float* pval = reinterpret_cast<float*>(base + NA_ACT + NA_SS + NA_ST + NA_RI);
+  int* pidx = reinterpret_cast<int*>(base + NA_ACT + NA_SS + NA_ST + NA_RI + NA_PART);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  k_na_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, act, ss, st, ri);
+  VP_CUDA(cudaGetLastError());
+  StageCfg lm = make_stage(format, vocab, H, 1);
+  lm.cps = 296 < (lm.nrb + 3) / 4 ? 296 : (lm.nrb + 3) / 4;
+  GemmParams p = {};
+  p.w = static_cast<const uint8_t*>(d_embed);
+  p.act = act;
+  p.nrb = lm.nrb;
+  p.ng = lm.ng;
+  p.nsplit = 1;
+  p.cg = lm.cg;
+  p.cps = lm.cps;
+  p.ss_in = ss;
+  p.pval = pval;
+  p.pidx = pidx;
+  p.s.st = st;
+  p.s.ri = ri;
+  switch (format) {
+    case VP_FMT_Q4: VP_CUDA((gemm_launch<VP_FMT_Q4, MODE_ARGMAX>(lm, p, s))); break;
+    case VP_FMT_Q8: VP_CUDA((gemm_launch<VP_FMT_Q8, MODE_ARGMAX>(lm, p, s))); break;
+    default: VP_CUDA((gemm_launch<VP_FMT_F16, MODE_ARGMAX>(lm, p, s))); break;
+  }
+  k_na_argmax<<<rows, 256, 0, s>>>(pval, pidx, lm.nrb, st, d_tokens);
+  VP_CUDA(cudaGetLastError());
+  return VP_OK;
+}
