@@ -361,11 +361,11 @@ def main():
             "tree_equals_sequential": bool(ok),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None,
-                         "kernel": "whole verify pass (CUDA graph, rank 0)",
+                         "kernel": "k_pass: the persistent verify-pass kernel (one launch per pass), rank 0",
                          "bytes_per_launch": alg, "peak_kind": peak_kind},
             "e2e": {"value": e2e_tok / e2e_s, "unit": "tok/s",
                     "h2d_bytes_per_step": 65 * 4, "d2h_bytes_per_step": 64},
-            "gpu_launches": 123 * args.steps,
+            "gpu_launches": args.steps,  # one persistent k_pass launch per verify pass
             "clocks": r["clocks"],
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -172,8 +172,10 @@ vp_state* vp_device_state(vp_ctx* ctx);
  * whose argmax the commit reduces). */
 int vp_debug_logits(vp_ctx* ctx, float* d_out, void* stream);
 /* Raw scratch buffers for tests: 0 x fp32[16][896], 1 q fp32[16][896], 2 KV cache K,
- * 3 KV cache V (half [layers][2][max_ctx][64]), 4 argmax values fp32[16][vocab/16],
- * 5 argmax ids int32[16][vocab/16]. */
+ * 3 KV cache V (half [layers][2][max_ctx][64]), 4 argmax partial values fp32 [16][parts],
+ * 5 argmax partial ids int32 [16][parts] (parts = CTAs of the pass kernel), 6 stage trace of the
+ * last launch: uint64 [256] %globaltimer ns (start, after embed, after each of the 5 stages of
+ * every layer, after the lm_head, end). */
 int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
 
 /* ---- greedy lm-head argmax that allocates nothing ----

@@ -1,20 +1,23 @@
-// Embedding of the pass rows and tree-masked grouped-query attention.
+// Embedding of the pass rows and tree-masked grouped-query attention (device functions of the
+// persistent pass kernel, 512 threads per CTA).
 //
-// k_embed replaces k_embed_prompt (Sources/Engine/Shaders.swift:180-190) and the next-row embed of
-// k_commit_spec (:413-417): it also validates the tree buffer and publishes the pass geometry
-// (RowInfo) that every later kernel reads.
+// embed_row replaces k_embed_prompt (Sources/Engine/Shaders.swift:180-190) and the next-row embed
+// of k_commit_spec (:413-417); it also validates the tree buffer and publishes the pass geometry
+// (RowInfo) that every later stage reads.
 //
-// k_attention replaces k_attention (Shaders.swift:876-958). Row t of a pass attends, in
-// sequential-decode order, to the virtual sequence [cached slots 0..pos-1, then its ancestors in
-// depth order, itself last]: exactly the keys the same token would see if the accepted path had
-// been decoded one token at a time. Work is split into fixed 64-position chunks of that virtual
-// sequence (flash-decoding partials: max, sum, weighted V), combined in chunk order by the last
-// chunk to finish. Chunk boundaries depend only on the virtual length, never on the pass shape,
-// so a row's result is bit-identical in a 16-row tree pass and in a 1-row pass.
+// attn_unit replaces k_attention (Shaders.swift:876-958). Row t of a pass attends, in
+// sequential-decode order, to its virtual sequence [cached slots 0..pos-1, then its ancestors in
+// depth order, itself last]: exactly the keys the same token sees when the accepted path is decoded
+// one token at a time. The sequence is cut into fixed 64-position chunks (flash-decoding partials:
+// max, exp-sum, weighted V), combined in chunk order by the last chunk to finish. Chunk boundaries
+// depend only on the virtual length, never on the pass shape, so a row's result is bit-identical in
+// a 16-row tree pass and in a 1-row pass.
 #pragma once
 #include "vp_common.cuh"
 
 namespace vp {
+
+constexpr int PASS_THREADS = CONS_THREADS;
 
 // Dequantised embedding value of (row tok, column k) read from the packed tile layout.
 template <int FMT>
@@ -41,40 +44,38 @@ __device__ __forceinline__ float embed_value(const uint8_t* E, int tok, int k) {
   }
 }
 
-struct EmbedParams {
+struct EmbedArgs {
   const uint8_t* E;
   const float* ln1;        // layer-0 input_layernorm weight
   const int32_t* prompt;   // prefill: token ids of this chunk (device); null for a verify pass
   int chunk_n;             // prefill: rows of this chunk
   int chunk_start;         // prefill: offset of the chunk in the prompt
   int total_n;             // prefill: prompt length
-  int last_chunk;          // prefill: this chunk ends the prompt (its last row is committed)
-  Scratch s;
 };
 
-// grid (16), 256 threads: CTA t embeds row t (zeros for padding rows); CTA 0 publishes RowInfo.
+// Row t of the pass (t < 16; one CTA per row): validates the tree / prompt, embeds the row into x,
+// writes its layer-0 QKV input (x * ln1 in act-block order) and its RMSNorm partials. The CTA of
+// row 0 publishes RowInfo and the pass fields of the state. Zeros for padding rows.
 template <int FMT>
-__global__ void __launch_bounds__(256) k_embed(EmbedParams p) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const Scratch& s = p.s;
+__device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
   vp_state* st = s.st;
-  const int t = blockIdx.x, tid = threadIdx.x;
-  __shared__ int sTok, sN, sLive, sPos;
+  const int tid = threadIdx.x;
+  __shared__ int sTok, sN, sLive;
   __shared__ int sDepth[ROWS], sPar[ROWS];
+  __shared__ float sPart[HRB];
   if (tid == 0) {
-    int live = st->done == 0, err = 0, n, pos;
+    int live = __ldcg(&st->done) == 0, err = 0, n, pos;
     if (p.prompt) {
       n = p.chunk_n;
-      pos = st->pos + p.chunk_start;
+      pos = __ldcg(&st->pos) + p.chunk_start;
       for (int i = 0; i < ROWS; ++i) { sDepth[i] = i; sPar[i] = i - 1; }
-      sTok = t < n ? p.prompt[t] : 0;
       if (n < 1 || n > ROWS) err |= VP_DEV_ERR_TREE;
       for (int i = 0; i < n && !err; ++i)
         if (p.prompt[i] < 0 || p.prompt[i] >= s.vocab) err |= VP_DEV_ERR_TREE;
+      sTok = (!err && t < n) ? p.prompt[t] : 0;
     } else {
       n = s.tree[VP_TR_N];
-      pos = st->pos;
+      pos = __ldcg(&st->pos);
       if (n < 1 || n > ROWS) err |= VP_DEV_ERR_TREE;
       for (int i = 0; i < ROWS && !err; ++i) {
         sDepth[i] = s.tree[VP_TR_DEPTH + i];
@@ -89,16 +90,20 @@ __global__ void __launch_bounds__(256) k_embed(EmbedParams p) {
           if (tk < 0 || tk >= s.vocab) err |= VP_DEV_ERR_TREE;
         }
       }
-      sTok = t == 0 ? st->last_token : (t < n ? s.tree[VP_TR_TOK + t] : 0);
+      sTok = t == 0 ? __ldcg(&st->last_token) : ((!err && t < n) ? s.tree[VP_TR_TOK + t] : 0);
       if (sTok < 0 || sTok >= s.vocab) err |= VP_DEV_ERR_TREE;
     }
     if (!err && (pos < 0 || pos + n > s.max_ctx)) err |= VP_DEV_ERR_CTX;
     if (err) live = 0;
-    sN = n; sLive = live; sPos = pos;
+    sN = n;
+    sLive = live;
     if (t == 0) {
-      if (err && st->done == 0) set_error(st, err);
+      if (err && __ldcg(&st->done) == 0) set_error(st, err);
       RowInfo* ri = s.ri;
-      ri->n = n; ri->pos = pos; ri->mode = p.prompt ? 1 : 0; ri->live = live;
+      ri->n = n;
+      ri->pos = pos;
+      ri->mode = p.prompt ? 1 : 0;
+      ri->live = live;
       for (int r = 0; r < ROWS; ++r) {
         const int dr = (r < n && !err) ? sDepth[r] : 0;
         ri->depth[r] = dr;
@@ -107,26 +112,18 @@ __global__ void __launch_bounds__(256) k_embed(EmbedParams p) {
       }
       if (live) {
         st->n = n;
-        if (p.prompt) {
-          st->mode = 1;
-          st->nver = 1;
-          st->vrow0 = n - 1;
-          st->advance = p.total_n;
-        } else {
-          st->mode = 0;
-          st->nver = n;
-          st->vrow0 = 0;
-          st->advance = 0;
-        }
+        st->mode = p.prompt ? 1 : 0;
+        st->nver = p.prompt ? 1 : n;
+        st->vrow0 = p.prompt ? n - 1 : 0;
+        st->advance = p.prompt ? p.total_n : 0;
       }
     }
   }
-  __syncthreads();
+  cons_sync();
   if (!sLive) return;
   const int n = sN, tok = sTok;
-  __shared__ float sPart[HRB];
-  // Row t of x, of the layer-0 QKV input (x * ln1 in act-block order) and the RMSNorm partials.
-  for (int rb = tid >> 4; rb < HRB; rb += 16) {
+  // groups of 16 threads take row-blocks of 16 columns; both halves of a warp iterate equally often
+  for (int rb = tid >> 4; rb < HRB; rb += PASS_THREADS / 16) {
     const int k = rb * 16 + (tid & 15);
     float v = 0.f;
     if (t < n) v = embed_value<FMT>(p.E, tok, k);
@@ -137,140 +134,179 @@ __global__ void __launch_bounds__(256) k_embed(EmbedParams p) {
     for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o, 16);
     if ((tid & 15) == 0) sPart[rb] = sq;
   }
-  __syncthreads();
+  cons_sync();
   if (tid < HRB) s.ss[tid * 16 + t] = sPart[tid];
 }
 
 // ---------------------------------------------------------------------------------------------
 // Attention
 
-constexpr int ATT_THREADS = 256;
-constexpr int GQ = NQ / NKV;  // 7 query heads per KV head
-constexpr int ATT_TICKETS = 1024;  // offset of the attention arrival counters in Scratch::tickets
+constexpr int GQ = NQ / NKV;            // 7 query heads per KV head
+constexpr int ATT_TICKETS = 1024;       // offset of the attention arrival counters in tickets
+constexpr int ATT_REC = GQ * (2 + HD);  // partial record of a chunk: per head m, l, o[64]
+constexpr int ATT_SEG = 8;              // chunks per work unit (segment)
 
-struct AttnParams {
-  int layer;
-  int max_chunks;   // chunks per (row, kv head) slot in att_part
-  Scratch s;
+struct AttnSmem {
+  float qs[GQ][HD];
+  float sc[GQ][ATT_CHUNK];
+  __half kv[2][ATT_CHUNK][HD];
+  int slots[ATT_SEG][ATT_CHUNK];
+  float rec[ATT_SEG][ATT_REC];  // this segment's chunk partials
+  int last;
 };
 
-// Partial record of one (row, kv head, chunk): per head m, l, o[64].
-constexpr int ATT_REC = GQ * (2 + HD);
+__device__ __forceinline__ int attn_chunks(const RowInfo* ri, int t, int pos) {
+  return (pos + ri->depth[t] + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
+}
+__device__ __forceinline__ int attn_segs(int nch) { return (nch + ATT_SEG - 1) / ATT_SEG; }
 
-__global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnParams p) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const Scratch& s = p.s;
+// Number of attention work units of a pass: (row, kv head, segment of <= 8 chunks).
+__device__ int attn_units(const RowInfo* ri) {
+  const int n = ri->n, pos = ri->pos;
+  int total = 0;
+  for (int t = 0; t < n; ++t) total += NKV * attn_segs(attn_chunks(ri, t, pos));
+  return total;
+}
+
+// Final output of (row t, kv head g) from the chunk partials in fixed chunk order:
+// M = max m_c, O = sum o_c e^(m_c - M) / sum l_c e^(m_c - M).
+template <bool GLOBAL>
+__device__ __forceinline__ void attn_combine(const Scratch& s, const float* base, int nch, int t,
+                                             int g) {
+  for (int i = threadIdx.x; i < GQ * HD; i += PASS_THREADS) {
+    const int h = i / HD, d = i % HD;
+    auto ld = [&](const float* q) { return GLOBAL ? __ldcg(q) : *q; };
+    float M = -INFINITY;
+    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ld(base + cc * ATT_REC + h * (2 + HD)));
+    float O = 0.f, Ls = 0.f;
+    for (int cc = 0; cc < nch; ++cc) {
+      const float* r = base + cc * ATT_REC + h * (2 + HD);
+      const float w = expf(ld(r) - M);
+      Ls = fmaf(ld(r + 1), w, Ls);
+      O = fmaf(ld(r + 2 + d), w, O);
+    }
+    s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / Ls);
+  }
+}
+
+// One unit with PASS_THREADS threads: the chunks of one segment of (row t, kv head g), each a
+// 64-position window of the row's virtual sequence. A row with one segment (virtual length <= 512)
+// is combined right here; longer rows write chunk records and the segment that completes the row
+// combines all of them (same formula, same chunk order).
+__device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, AttnSmem& sm) {
   const RowInfo* ri = s.ri;
-  if (!ri->live) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = ri->n, pos = ri->pos;
-  __shared__ float qs[GQ][HD];
-  __shared__ float sc[GQ][ATT_CHUNK];
-  __shared__ int slots[ATT_CHUNK];
-  __shared__ float sm[GQ], sl[GQ];
-  __shared__ int sLast;
-
-  // Units ordered by (row, kv head, chunk).
-  int nch[ROWS];
-  int total = 0;
-  for (int t = 0; t < ROWS; ++t) {
-    nch[t] = t < n ? (pos + ri->depth[t] + 1 + ATT_CHUNK - 1) / ATT_CHUNK : 0;
-    total += 2 * nch[t];
+  int t = 0, rem = u, nch = 1, nseg = 1;
+  for (; t < n; ++t) {
+    nch = attn_chunks(ri, t, pos);
+    nseg = attn_segs(nch);
+    if (rem < NKV * nseg) break;
+    rem -= NKV * nseg;
   }
-  for (int u = blockIdx.x; u < total; u += gridDim.x) {
-    int t = 0, rem = u;
-    while (rem >= 2 * nch[t]) { rem -= 2 * nch[t]; ++t; }
-    const int g = rem / nch[t], c = rem % nch[t];
-    const int L = pos + ri->depth[t] + 1;
-    const int j0 = c * ATT_CHUNK, cnt = min(L - j0, ATT_CHUNK);
-    const __half* kb = s.kc + (size_t)(p.layer * NKV + g) * s.max_ctx * HD;
-    const __half* vb = s.vc + (size_t)(p.layer * NKV + g) * s.max_ctx * HD;
-    for (int i = tid; i < GQ * HD; i += ATT_THREADS)
-      qs[i / HD][i % HD] = s.q[t * H + (g * GQ + i / HD) * HD + i % HD];
-    if (tid < ATT_CHUNK) {
-      const int jv = j0 + tid;
-      slots[tid] = jv < pos ? jv : pos + ri->path[t][min(jv - pos, ROWS - 1)];
+  const int g = rem / nseg, seg = rem % nseg;
+  const int c0 = seg * ATT_SEG, c1 = min(nch, c0 + ATT_SEG);
+  const int L = pos + ri->depth[t] + 1;
+  const __half* kb = s.kc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
+  const __half* vb = s.vc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
+  // slots of every position of the segment (virtual position -> KV slot), no memory traffic
+  for (int i = tid; i < (c1 - c0) * ATT_CHUNK; i += PASS_THREADS) {
+    const int jv = c0 * ATT_CHUNK + i;
+    sm.slots[i / ATT_CHUNK][i % ATT_CHUNK] =
+        jv < pos ? jv : pos + ri->path[t][min(max(jv - pos, 0), ROWS - 1)];
+  }
+  cons_sync();
+  // K and V rows of a chunk: 2 x 64 rows x 128 bytes = 1024 16-byte words, two per thread, loaded
+  // into registers one chunk ahead of the compute (q travels with the first chunk)
+  auto load_kv = [&](int ci, int cnt, uint4 (&v)[2]) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * PASS_THREADS;
+      const int which = i / (ATT_CHUNK * 8), r = (i / 8) % ATT_CHUNK, part = i % 8;
+      v[k] = make_uint4(0, 0, 0, 0);
+      if (r < cnt)
+        v[k] = __ldcg(reinterpret_cast<const uint4*>((which ? vb : kb) + (size_t)sm.slots[ci][r] * HD + part * 8));
     }
-    __syncthreads();
-    // Scores: 4 threads per position, 16 dims each, fixed-order combine.
+  };
+  uint4 kvr[2];
+  load_kv(0, min(L - c0 * ATT_CHUNK, ATT_CHUNK), kvr);
+  for (int i = tid; i < GQ * HD; i += PASS_THREADS)
+    sm.qs[i / HD][i % HD] = __ldcg(s.q + t * H + (g * GQ + i / HD) * HD + i % HD);
+  for (int c = c0; c < c1; ++c) {
+    const int ci = c - c0;
+    const int j0 = c * ATT_CHUNK, cnt = min(L - j0, ATT_CHUNK);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * PASS_THREADS;
+      const int which = i / (ATT_CHUNK * 8), r = (i / 8) % ATT_CHUNK, part = i % 8;
+      *reinterpret_cast<uint4*>(&sm.kv[which][r][part * 8]) = kvr[k];
+    }
+    cons_sync();
+    if (c + 1 < c1) load_kv(ci + 1, min(L - (c + 1) * ATT_CHUNK, ATT_CHUNK), kvr);
+    // scores: 8 threads per position, 8 dims each, fixed-order combine
     {
-      const int pp = tid >> 2, part = tid & 3;
+      const int pp = tid >> 3, part = tid & 7;
       float a[GQ];
 #pragma unroll
       for (int h = 0; h < GQ; ++h) a[h] = 0.f;
-      if (pp < cnt) {
-        const __half2* kr = reinterpret_cast<const __half2*>(kb + (size_t)slots[pp] * HD + part * 16);
+      const __half2* kr = reinterpret_cast<const __half2*>(&sm.kv[0][pp][part * 8]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 kv = __half22float2(kr[i]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 kv = __half22float2(kr[i]);
 #pragma unroll
-          for (int h = 0; h < GQ; ++h)
-            a[h] = fmaf(qs[h][part * 16 + 2 * i + 1], kv.y, fmaf(qs[h][part * 16 + 2 * i], kv.x, a[h]));
-        }
+        for (int h = 0; h < GQ; ++h)
+          a[h] = fmaf(sm.qs[h][part * 8 + 2 * i + 1], kv.y, fmaf(sm.qs[h][part * 8 + 2 * i], kv.x, a[h]));
       }
 #pragma unroll
       for (int h = 0; h < GQ; ++h) {
         float v = a[h];
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (part == 0) sc[h][pp] = pp < cnt ? v * ATTN_SCALE : -INFINITY;
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (part == 0) sm.sc[h][pp] = pp < cnt ? v * ATTN_SCALE : -INFINITY;
       }
     }
-    __syncthreads();
-    // Per-head max and exp-sum over the chunk (warp h, two positions per lane).
+    cons_sync();
+    // per-head max and exp-sum over the chunk (warp h, two positions per lane)
     if (warp < GQ) {
-      const float v0 = sc[warp][lane], v1 = sc[warp][lane + 32];
+      const float v0 = sm.sc[warp][lane], v1 = sm.sc[warp][lane + 32];
       const float m = warp_max(fmaxf(v0, v1));
       const float e0 = lane < cnt ? expf(v0 - m) : 0.f;
       const float e1 = lane + 32 < cnt ? expf(v1 - m) : 0.f;
-      sc[warp][lane] = e0;
-      sc[warp][lane + 32] = e1;
+      sm.sc[warp][lane] = e0;
+      sm.sc[warp][lane + 32] = e1;
       const float l = warp_sum(e0 + e1);
-      if (lane == 0) { sm[warp] = m; sl[warp] = l; }
+      if (lane == 0) { sm.rec[ci][warp * (2 + HD)] = m; sm.rec[ci][warp * (2 + HD) + 1] = l; }
     }
-    __syncthreads();
-    // Weighted V: thread (d, head set {hg, hg+4}), positions in order.
+    cons_sync();
+    // weighted V: thread (head, dim), positions in order
     {
-      const int d = tid & 63, hg = tid >> 6;
-      float o0 = 0.f, o1 = 0.f;
-      for (int pp = 0; pp < cnt; ++pp) {
-        const float v = __half2float(vb[(size_t)slots[pp] * HD + d]);
-        o0 = fmaf(sc[hg][pp], v, o0);
-        if (hg + 4 < GQ) o1 = fmaf(sc[hg + 4][pp], v, o1);
-      }
-      float* rec = s.att_part + ((size_t)(t * NKV + g) * p.max_chunks + c) * ATT_REC;
-      rec[hg * (2 + HD) + 2 + d] = o0;
-      if (hg + 4 < GQ) rec[(hg + 4) * (2 + HD) + 2 + d] = o1;
-      if (tid < GQ) {
-        rec[tid * (2 + HD)] = sm[tid];
-        rec[tid * (2 + HD) + 1] = sl[tid];
+      const int d = tid & 63, h = tid >> 6;
+      if (h < GQ) {
+        float o = 0.f;
+        for (int pp = 0; pp < cnt; ++pp) o = fmaf(sm.sc[h][pp], __half2float(sm.kv[1][pp][d]), o);
+        sm.rec[ci][h * (2 + HD) + 2 + d] = o;
       }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sLast = atomicAdd(s.tickets + ATT_TICKETS + t * NKV + g, 1) == nch[t] - 1;
-    __syncthreads();
-    if (sLast) {
-      __threadfence();
-      const float* base = s.att_part + (size_t)(t * NKV + g) * p.max_chunks * ATT_REC;
-      for (int i = tid; i < GQ * HD; i += ATT_THREADS) {
-        const int h = i / HD, d = i % HD;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nch[t]; ++cc) M = fmaxf(M, __ldcg(base + cc * ATT_REC + h * (2 + HD)));
-        float O = 0.f, Ls = 0.f;
-        for (int cc = 0; cc < nch[t]; ++cc) {
-          const float* r = base + cc * ATT_REC + h * (2 + HD);
-          const float w = expf(__ldcg(r) - M);
-          Ls = fmaf(__ldcg(r + 1), w, Ls);
-          O = fmaf(__ldcg(r + 2 + d), w, O);
-        }
-        s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / Ls);
-      }
-      if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
-    }
-    __syncthreads();
+    cons_sync();
   }
+  if (nseg == 1) {
+    attn_combine<false>(s, &sm.rec[0][0], nch, t, g);
+    cons_sync();
+    return;
+  }
+  float* base = s.att_part + (size_t)(t * NKV + g) * max_chunks * ATT_REC;
+  for (int i = tid; i < (c1 - c0) * ATT_REC; i += PASS_THREADS) base[c0 * ATT_REC + i] = (&sm.rec[0][0])[i];
+  __threadfence();
+  cons_sync();
+  if (tid == 0) sm.last = atomicAdd(s.tickets + ATT_TICKETS + t * NKV + g, 1) == nseg - 1;
+  cons_sync();
+  if (sm.last) {
+    __threadfence();
+    attn_combine<true>(s, base, nch, t, g);
+    if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
+  }
+  cons_sync();
 }
 
 }  // namespace vp

@@ -4,15 +4,18 @@
 
 namespace vp {
 
-constexpr int COMMIT_THREADS = 1024;
+constexpr int COMMIT_THREADS = CONS_THREADS;
 
 struct CommitParams {
-  int nrb_lm;   // lm_head row-blocks = vocab / 16 (argmax partials per row)
+  const float* pval;  // [16][nparts] argmax partials (value)
+  const int* pidx;    // [16][nparts] (id, lowest on ties)
+  int nparts;
   Scratch s;
 };
 
-// Greedy accept + commit (k_commit_spec, Shaders.swift:254-365, and k_commit :194-244):
-//  1. g[t] = argmax of pass row vrow0+t over the lm_head partials, lowest id on ties (:281-306).
+// Greedy accept + commit (k_commit_spec, Shaders.swift:254-365, and k_commit :194-244), run by the
+// 512 compute threads of one CTA:
+//  1. g[t] = argmax of pass row vrow0+t over the argmax partials, lowest id on ties (:281-306).
 //  2. Tree: from the root, repeatedly take the first row whose parent is the current row and whose
 //     draft equals the current row's argmax (:311-320). The root's argmax is always committed.
 //  3. Commit g along the path to out_tokens, stopping at EOS or max_steps (:326-333).
@@ -20,28 +23,25 @@ struct CommitParams {
 //  5. KV compaction: accepted row path[k-1] moves from slot pos0+path[k-1] to pos0+k in every
 //     layer; it was already rotated for position pos0+k (its depth is k). Copies run in k order,
 //     which is safe because path rows strictly increase (:351-365).
-__global__ void __launch_bounds__(COMMIT_THREADS) k_commit(CommitParams p) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const Scratch& s = p.s;
+__device__ void commit_body(const Scratch& s, const float* pval, const int* pidx, int nparts) {
   vp_state* st = s.st;
   const RowInfo* ri = s.ri;
-  if (!ri->live || st->done) return;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float rv[32];
-  __shared__ int ri_[32];
+  if (!ri->live || __ldcg(&st->done)) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = CONS_THREADS;
+  const int nwarps = nthr >> 5;
   __shared__ int g[ROWS];
   __shared__ int path[ROWS];
   __shared__ int sNpath, sPos0;
   const int nv = st->nver, r0 = st->vrow0;
-  for (int t = 0; t < nv; ++t) {
-    const float* pv = s.pval + (size_t)(r0 + t) * p.nrb_lm;
-    const int* pi = s.pidx + (size_t)(r0 + t) * p.nrb_lm;
+  // one warp per row: argmax over the partials, lowest id on ties
+  for (int t = warp; t < nv; t += nwarps) {
+    const float* pv = pval + (size_t)(r0 + t) * nparts;
+    const int* pi = pidx + (size_t)(r0 + t) * nparts;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = tid; i < p.nrb_lm; i += COMMIT_THREADS) {
-      const float v = pv[i];
-      const int id = pi[i];
+    for (int i = lane; i < nparts; i += 32) {
+      const float v = __ldcg(pv + i);
+      const int id = __ldcg(pi + i);
       if (v > best || (v == best && id < bi)) { best = v; bi = id; }
     }
 #pragma unroll
@@ -50,21 +50,9 @@ __global__ void __launch_bounds__(COMMIT_THREADS) k_commit(CommitParams p) {
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
     }
-    if (lane == 0) { rv[warp] = best; ri_[warp] = bi; }
-    __syncthreads();
-    if (warp == 0) {
-      best = rv[lane];
-      bi = ri_[lane];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-      }
-      if (lane == 0) g[t] = bi;
-    }
-    __syncthreads();
+    if (lane == 0) g[t] = bi;
   }
+  cons_sync();
   if (tid == 0) {
     int m = 0;
     const bool tree = ri->mode == 0 && nv > 1;
@@ -97,30 +85,33 @@ __global__ void __launch_bounds__(COMMIT_THREADS) k_commit(CommitParams p) {
     st->last_token = last;
     if (stop) st->done = 1;
   }
-  __syncthreads();
+  cons_sync();
   const int np = sNpath, pos0 = sPos0;
   for (int k = 1; k <= np; ++k) {
     const int src = pos0 + path[k - 1], dst = pos0 + k;
     if (src != dst) {
       // 2 caches x layers x 2 KV heads x 64 halves, moved as 16-byte words (8 per row).
       const int words = 2 * s.n_layers * NKV * (HD / 8);
-      for (int w = tid; w < words; w += COMMIT_THREADS) {
+      for (int w = tid; w < words; w += nthr) {
         const int cache = w / (s.n_layers * NKV * 8);
         const int rem = w % (s.n_layers * NKV * 8);
         const int lh = rem / 8, part = rem % 8;
         __half* base = (cache ? s.vc : s.kc) + (size_t)lh * s.max_ctx * HD;
-        const uint4 v = *reinterpret_cast<const uint4*>(base + (size_t)src * HD + part * 8);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(base + (size_t)src * HD + part * 8));
         *reinterpret_cast<uint4*>(base + (size_t)dst * HD + part * 8) = v;
       }
     }
-    __syncthreads();
+    cons_sync();
   }
+}
+
+__global__ void __launch_bounds__(COMMIT_THREADS) k_commit(CommitParams p) {
+  commit_body(p.s, p.pval, p.pidx, p.nparts);
 }
 
 // Request set-up (Engine.generate, Engine.swift:945-964): one thread.
 __global__ void k_begin(vp_state* st, int32_t* out_tokens, int max_steps_cap, int cached,
                         int max_new, int eos0, int eos1, int maxctx, int last_token) {
-  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   for (int j = i; j < max_steps_cap; j += gridDim.x * blockDim.x) out_tokens[j] = -1;
   if (i == 0) {

@@ -111,12 +111,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each try_wait itself suspends for a while), so a
-// lost copy can never hang the GPU. Returns false on timeout.
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every device-side wait gives up after WAIT_NS of wall time (and after a poll cap), so a lost copy
+// or a missing arrival can never hang the GPU: the caller records a timeout and returns.
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s
+
+// Bounded wait on an mbarrier phase. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint32_t limit = 1u << 22) {
-  for (uint32_t i = 0; i < limit; ++i)
+                                                  unsigned long long wait_ns = WAIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && globaltimer() - t0 > wait_ns) return false;
+  }
   return false;
 }
 
@@ -159,6 +172,12 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Barrier of the 512 compute threads of a CTA (named barrier 1). The persistent pass kernel adds a
+// producer warp that never takes part in the compute stages, so stage code never uses
+// __syncthreads.
+constexpr int CONS_THREADS = 512;
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
 __device__ __forceinline__ void set_error(vp_state* st, int bits) {
   atomicOr(&st->err, bits);

@@ -41,6 +41,8 @@ struct GemmParams {
   float* pval;           // ARGMAX
   int* pidx;
   float* dbg;            // ARGMAX: optional full logits [16][nrb*16]
+  float* xs;             // RESID: x[16 tokens][16 dims] of the row-block kept in shared memory by
+                         // the CTA that owns it (persistent kernel), or null to use global x
   Scratch s;
 };
 
@@ -139,8 +141,14 @@ __device__ void gemm_epilogue(const GemmParams& p, int rb, float (&acc)[2][4], c
         const int t = nt * 8 + 2 * tid4 + e;
         float v0 = 0.f, v1 = 0.f;
         if (t < n) {
-          v0 = s.x[t * H + d0] + acc[nt][e];
-          v1 = s.x[t * H + d1] + acc[nt][2 + e];
+          const float x0 = p.xs ? p.xs[t * 16 + gid] : __ldcg(s.x + t * H + d0);
+          const float x1 = p.xs ? p.xs[t * 16 + gid + 8] : __ldcg(s.x + t * H + d1);
+          v0 = x0 + acc[nt][e];
+          v1 = x1 + acc[nt][2 + e];
+          if (p.xs) {
+            p.xs[t * 16 + gid] = v0;
+            p.xs[t * 16 + gid + 8] = v1;
+          }
           s.x[t * H + d0] = v0;
           s.x[t * H + d1] = v1;
         }
@@ -262,7 +270,7 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
     }
     if (MODE != MODE_RESID && threadIdx.x < 16) {
       float sum = 0.f;
-      for (int r = 0; r < HRB; ++r) sum += p.ss_in[r * 16 + threadIdx.x];
+      for (int r = 0; r < HRB; ++r) sum += __ldcg(p.ss_in + r * 16 + threadIdx.x);
       sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
     }
     if (!mbar_wait_bounded(barAct, 0)) sOk = 0;
@@ -394,8 +402,8 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
   }
   // Every copy this warp issued must land before the CTA's shared memory is released.
   for (int ci = n_waited; ci < n_issued; ++ci)
-    mbar_wait_bounded(myBars + ci % GEMM_NST, (ci / GEMM_NST) & 1, 1u << 20);
-  if (threadIdx.x == 0) mbar_wait_bounded(barAct, 0, live ? (1u << 20) : 0u);
+    mbar_wait_bounded(myBars + ci % GEMM_NST, (ci / GEMM_NST) & 1);
+  if (threadIdx.x == 0 && live) mbar_wait_bounded(barAct, 0);
 }
 
 template <int FMT, int MODE>

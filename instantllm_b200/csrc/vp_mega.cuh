@@ -1,0 +1,645 @@
+// Persistent verification-pass kernel: one launch runs embed, 24 layers, lm_head and the commit.
+//
+// Replaces the reference's per-dispatch pass encoder (Engine.encodeWidePass, Engine.swift:567-579:
+// 171 Metal dispatches per pass) with one cooperative kernel, one CTA per SM:
+//  * stages are separated by a grid barrier (64-bit arrival counter, bounded spin);
+//  * a producer warp streams the CTA's weights for the whole pass, in consumption order, as
+//    contiguous pieces of up to 28 KiB (cp.async.bulk) into a 5-slot shared-memory ring with
+//    full / empty mbarriers. Weights never depend on activations, so the stream runs up to the
+//    ring's depth ahead, across stage boundaries, and overlaps the barrier and activation latency
+//    of the dependent chain. Copies are few and large: each bulk-copy issue occupies the SM's copy
+//    path for a few hundred cycles whatever its size;
+//  * each CTA owns a contiguous row-block range of every GEMM, chosen so that all SMs stream about
+//    the same bytes per layer; a row-block's K groups are split into a fixed number of parts that
+//    different consumer warps process and that are summed in part order in shared memory;
+//  * per-row arithmetic is a fixed function of the inputs (fixed parts, fixed group order, fixed
+//    attention chunks), so tree rows reproduce 1-row passes bit for bit.
+#pragma once
+#include "vp_attn.cuh"
+#include "vp_commit.cuh"
+#include "vp_gemm.cuh"
+
+namespace vp {
+
+constexpr int MK_WARPS = 16;                     // consumer warps
+constexpr int MK_CONS = MK_WARPS * 32;           // consumer threads (== PASS_THREADS)
+constexpr int MK_THREADS = MK_CONS + 32;         // + the producer warp
+constexpr int MK_NSLOT = 5;                      // weight ring slots
+constexpr int MK_SLOT = 28672;                   // bytes per slot
+constexpr int MK_PART_SLOTS = 24;                // partial tiles of a stage (1 KiB each)
+constexpr int MK_TRACE = 256;                    // trace slots: start, embed, 5 per layer, lm, end
+static_assert(MK_CONS == PASS_THREADS && MK_CONS == CONS_THREADS, "consumer warps run the stage code");
+
+enum MkStage { MK_QKV = 0, MK_O = 1, MK_GU = 2, MK_DOWN = 3, MK_LM = 4 };
+
+// Parts per row-block (K split across warps of one CTA) and K groups of each GEMM stage.
+__host__ __device__ constexpr int mk_parts(int st) {
+  return st == MK_QKV ? 14 : st == MK_O ? 14 : st == MK_GU ? 3 : st == MK_DOWN ? 16 : 1;
+}
+__host__ __device__ constexpr int mk_groups(int st) { return st == MK_DOWN ? F / GS : H / GS; }
+__host__ __device__ constexpr int mk_chunk_groups(int fmt) {
+  return fmt == VP_FMT_Q4 ? 7 : fmt == VP_FMT_Q8 ? 4 : 2;  // stand-alone k_gemm chunking
+}
+__host__ __device__ constexpr int mk_tiles_per_slot(int fmt) { return MK_SLOT / tile_bytes(fmt); }
+
+// Contiguous row-block range [rb0, rb0 + n) of GEMM stage `st` owned by CTA `cta` of G. Balanced
+// so that every CTA streams about the same weight bytes per layer (q4: ~57 KB): O and down go to
+// CTAs 0..55 (which also keep their slice of x), QKV to the last 72 CTAs, gate/up mostly to the
+// CTAs without O / down, the lm_head in equal contiguous shares.
+__host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
+  rb0 = 0;
+  n = 0;
+  const int nh = H / 16, nq = QKV / 16, ngu = 2 * F / 16;
+  if (st == MK_O || st == MK_DOWN) {
+    if (cta < nh) { rb0 = cta; n = 1; }
+  } else if (st == MK_QKV) {
+    if (cta >= G - nq) { rb0 = cta - (G - nq); n = 1; }
+  } else if (st == MK_GU) {
+    if (cta < nh) { rb0 = cta; n = 1; }
+    else {
+      const int rest = ngu - nh, m = G - nh, c = cta - nh;
+      rb0 = nh + (int)((long long)c * rest / m);
+      n = nh + (int)((long long)(c + 1) * rest / m) - rb0;
+    }
+  } else {
+    rb0 = (int)((long long)cta * nrb_lm / G);
+    n = (int)((long long)(cta + 1) * nrb_lm / G) - rb0;
+  }
+}
+
+__host__ __device__ inline int mk_pieces(int fmt, int st, int nrb) {
+  const int tiles = nrb * mk_groups(st);
+  const int tp = mk_tiles_per_slot(fmt);
+  return (tiles + tp - 1) / tp;
+}
+
+struct MegaParams {
+  Scratch s;
+  const uint8_t* embed;
+  const float* final_norm;
+  const uint8_t* wqkv[VP_MAX_LAYERS];
+  const float* bqkv[VP_MAX_LAYERS];
+  const uint8_t* wo[VP_MAX_LAYERS];
+  const uint8_t* wgu[VP_MAX_LAYERS];
+  const uint8_t* wd[VP_MAX_LAYERS];
+  const float* ln1[VP_MAX_LAYERS];
+  const float* ln2[VP_MAX_LAYERS];
+  int n_layers;
+  int nrb_lm;                 // vocab / 16
+  int max_chunks;             // attention partial records per (row, kv head)
+  unsigned long long* bar;    // grid barrier arrival counter (0 at launch, reset by the last CTA)
+  unsigned* exit_ctr;         // CTAs that finished this launch
+  unsigned long long* trace;  // CTA 0: %globaltimer after each stage (MK_TRACE entries)
+  float* lm_pval;             // [16][gridDim] per-CTA argmax partials
+  int* lm_pidx;
+  // what this launch runs
+  const int32_t* prompt;      // prefill chunk tokens (null: tree verify pass)
+  int chunk_n, chunk_start, total_n;
+  int do_lm, do_commit;
+};
+
+__device__ __forceinline__ const uint8_t* mk_weights(const MegaParams& p, int st, int l) {
+  switch (st) {
+    case MK_QKV: return p.wqkv[l];
+    case MK_O: return p.wo[l];
+    case MK_GU: return p.wgu[l];
+    case MK_DOWN: return p.wd[l];
+    default: return p.embed;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// grid barrier (consumer threads only)
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void mk_sync() { cons_sync(); }
+
+// The CTA's writes before the barrier are ordered before its arrival by bar.sync + the release
+// add (cumulativity); the acquire load orders the other CTAs' writes before what follows.
+__device__ bool grid_barrier(const MegaParams& p, unsigned long long target, int* sAbort) {
+  mk_sync();
+  if (threadIdx.x == 0) {
+    red_release_add_u64(p.bar, 1ull);
+    bool ok = false;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 0; i < (1u << 26); ++i) {
+      if (ld_acquire_u64(p.bar) >= target) { ok = true; break; }
+      if ((i & 63) == 63 && globaltimer() - t0 > WAIT_NS) break;
+      __nanosleep(32);
+    }
+    if (!ok) {
+      set_error(p.s.st, VP_DEV_ERR_TIMEOUT);
+      *sAbort = 1;
+    }
+  }
+  mk_sync();
+  return *(volatile int*)sAbort == 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// shared memory map
+
+constexpr size_t MK_RING_BYTES = (size_t)MK_NSLOT * MK_SLOT;
+constexpr size_t MK_ACT_BYTES = (size_t)(H / GS) * 2048;  // act blocks of a K = 896 GEMM
+constexpr size_t MK_OFF_ACT = MK_RING_BYTES;
+constexpr size_t MK_OFF_X = MK_OFF_ACT + MK_ACT_BYTES;            // 16 x 16 group sums
+constexpr size_t MK_OFF_PART = MK_OFF_X + 16 * 16 * 4;            // partial tiles
+constexpr size_t MK_OFF_RS = MK_OFF_PART + MK_PART_SLOTS * 1024;  // rscale[16]
+constexpr size_t MK_OFF_LMV = MK_OFF_RS + 64;                     // [16 warps][16] best value
+constexpr size_t MK_OFF_LMI = MK_OFF_LMV + 1024;                  // [16 warps][16] best id
+constexpr size_t MK_OFF_RI = MK_OFF_LMI + 1024;                   // RowInfo copy
+constexpr size_t MK_OFF_XRB = MK_OFF_RI + ((sizeof(RowInfo) + 15) & ~size_t(15));  // owned x slice
+constexpr size_t MK_OFF_BAR = (MK_OFF_XRB + 16 * 16 * 4 + 127) & ~size_t(127);
+constexpr size_t MK_SMEM = MK_OFF_BAR + 8 * (2 * MK_NSLOT);
+static_assert(sizeof(AttnSmem) <= MK_OFF_RS - MK_OFF_ACT,
+              "attention scratch overlays the act blocks, group sums and partial tiles");
+
+// Consumer view of the weight ring: pieces are numbered over the whole pass in consumption order.
+struct MkRing {
+  uint8_t* base;
+  uint64_t* full;   // [MK_NSLOT], producer arrive + transaction bytes
+  uint64_t* empty;  // [MK_NSLOT], one arrival per consumer warp
+  int released;     // pieces this warp has released (identical in all lanes)
+  int waited;       // pieces this warp has seen full
+};
+
+// ---------------------------------------------------------------------------------------------
+// producer warp: issues every piece of the pass in order (lane 0)
+
+template <int FMT>
+__device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sStop) {
+  if ((threadIdx.x & 31) != 0) return;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + MK_OFF_BAR);
+  uint64_t* empty = full + MK_NSLOT;
+  const int G = gridDim.x, cta = blockIdx.x;
+  constexpr int TB = tile_bytes(FMT);
+  const int tp = mk_tiles_per_slot(FMT);
+  const uint64_t pol = policy_evict_first();
+  int k = 0;  // pieces issued
+  bool ok = true;
+  const int nst = p.n_layers * 4 + (p.do_lm ? 1 : 0);
+  for (int si = 0; si < nst && ok; ++si) {
+    const int l = si / 4, st = si < p.n_layers * 4 ? si % 4 : MK_LM;
+    int rb0, nrb;
+    mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+    if (nrb == 0) continue;
+    const int ng = mk_groups(st);
+    const int tiles = nrb * ng;
+    const uint8_t* src = mk_weights(p, st, l) + (size_t)rb0 * ng * TB;
+    for (int t0 = 0; t0 < tiles && ok; t0 += tp, ++k) {
+      const int slot = k % MK_NSLOT;
+      if (k >= MK_NSLOT) {
+        // the slot's previous piece must be released by every consumer warp
+        const uint32_t par = ((k / MK_NSLOT) - 1) & 1;
+        bool got = false;
+        const unsigned long long t0 = globaltimer();
+        for (uint32_t i = 0; i < (1u << 26); ++i) {
+          if (mbar_try_wait(empty + slot, par)) { got = true; break; }
+          if ((i & 63) == 63 && (*sStop || globaltimer() - t0 > WAIT_NS)) break;
+        }
+        if (!got) { ok = false; break; }
+      }
+      const uint32_t bytes = (uint32_t)(min(tp, tiles - t0) * TB);
+      mbar_arrive_expect_tx(full + slot, bytes);
+      bulk_g2s(smem + (size_t)slot * MK_SLOT, src + (size_t)t0 * TB, bytes, full + slot, pol);
+    }
+  }
+  // every issued piece lands before the CTA's shared memory is released: only the last piece of
+  // each slot can still be in flight
+  for (int s = 0; s < MK_NSLOT; ++s) {
+    int last = -1;
+    for (int q = s; q < k; q += MK_NSLOT) last = q;
+    if (last >= 0) mbar_wait_bounded(full + s, (last / MK_NSLOT) & 1);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// consumer GEMM stage
+
+__device__ __forceinline__ uint4 act_frag_smem(const uint8_t* sAct, int g, int j, int lane) {
+  return *reinterpret_cast<const uint4*>(sAct + (size_t)g * 2048 + j * 512 + lane * 16);
+}
+
+// acc += NT consecutive tiles (groups g .. g+NT-1 of the row-block) times their activations. The
+// tiles' MMA chains are independent (instruction-level parallelism); their folds into acc run in
+// group order, so the result equals NT single-tile steps.
+template <int FMT, bool GLOBAL_B, int NT>
+__device__ __forceinline__ void mk_tiles(const uint8_t* const (&tile)[NT], int g, const uint8_t* sAct,
+                                         const float* sX, const __half* actg, int lane,
+                                         float (&acc)[2][4]) {
+  const int gid = lane >> 2, tid4 = lane & 3;
+  uint4 bf[NT][4];
+#pragma unroll
+  for (int u = 0; u < NT; ++u)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      bf[u][j] = GLOBAL_B
+          ? __ldcg(reinterpret_cast<const uint4*>(actg + (size_t)(g + u) * 1024 + j * 256 + lane * 8))
+          : act_frag_smem(sAct, g + u, j, lane);
+  if constexpr (FMT == VP_FMT_F16) {
+#pragma unroll
+    for (int u = 0; u < NT; ++u)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t w[4];
+        load_a_frags<FMT>(tile[u], lane, j, w);
+        mma16816(acc[0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
+        mma16816(acc[1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
+      }
+  } else {
+    float ag[NT][2][4];
+    float tx[NT][2][2];
+#pragma unroll
+    for (int u = 0; u < NT; ++u) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ag[u][nt][i] = 0.f;
+      if constexpr (GLOBAL_B) {
+        // group sums from the fragments just loaded: a ones-matrix MMA
+        const uint32_t ONE2 = 0x3C003C00u;
+        float xs[2][4] = {};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, bf[u][j].x, bf[u][j].y);
+          mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, bf[u][j].z, bf[u][j].w);
+        }
+        tx[u][0][0] = xs[0][0]; tx[u][0][1] = xs[0][1]; tx[u][1][0] = xs[1][0]; tx[u][1][1] = xs[1][1];
+      } else {
+        const float* xg = sX + (g + u) * 16;
+        const float2 x0 = *reinterpret_cast<const float2*>(xg + 2 * tid4);
+        const float2 x1 = *reinterpret_cast<const float2*>(xg + 8 + 2 * tid4);
+        tx[u][0][0] = x0.x; tx[u][0][1] = x0.y; tx[u][1][0] = x1.x; tx[u][1][1] = x1.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int u = 0; u < NT; ++u) {
+        uint32_t w[4];
+        load_a_frags<FMT>(tile[u], lane, j, w);
+        mma16816(ag[u][0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
+        mma16816(ag[u][1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
+      }
+#pragma unroll
+    for (int u = 0; u < NT; ++u) {
+      float sf[2], sb[2];
+      load_fold<FMT>(tile[u], gid, sf, sb);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = i >> 1;
+          acc[nt][i] = fmaf(sf[r], ag[u][nt][i], fmaf(sb[r], tx[u][nt][i & 1], acc[nt][i]));
+        }
+    }
+  }
+}
+
+// Wait until piece k is in the ring (bounded); returns its slot base or null on timeout.
+__device__ __forceinline__ const uint8_t* mk_piece(MkRing& rg, int k) {
+  while (rg.waited <= k) {
+    if (!mbar_wait_bounded(rg.full + rg.waited % MK_NSLOT, (rg.waited / MK_NSLOT) & 1)) return nullptr;
+    ++rg.waited;
+  }
+  return rg.base + (size_t)(k % MK_NSLOT) * MK_SLOT;
+}
+// Release every piece below k (this warp is done with them). A piece is released only after it
+// has landed: the slot's empty barrier then counts exactly one arrival per warp per piece, because
+// the producer issues piece r + MK_NSLOT only after every warp released piece r. Returns false on
+// timeout.
+// Pieces are released one at a time, each as soon as it has landed, so a warp never waits for a
+// piece while it still holds an older one (the newer piece may need the older one's slot).
+__device__ __forceinline__ bool mk_release(MkRing& rg, int k, int lane) {
+  for (; rg.released < k; ++rg.released) {
+    if (!mk_piece(rg, rg.released)) return false;
+    __syncwarp();
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(rg.empty + rg.released % MK_NSLOT))
+                   : "memory");
+  }
+  return true;
+}
+
+// One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
+// Returns false if a wait timed out.
+template <int FMT, int MODE>
+__device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
+                        uint8_t* smem, volatile int* sAbort, float (&lmV)[2][2], int (&lmI)[2][2]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tid4 = lane & 3;
+  uint8_t* sAct = smem + MK_OFF_ACT;
+  float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
+  float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
+  float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
+  const int G = gridDim.x, cta = blockIdx.x;
+  int rb0, nrb;
+  mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+  if (nrb == 0) return true;
+  const int P = mk_parts(st), ng = mk_groups(st);
+  const int tp = mk_tiles_per_slot(FMT);
+  constexpr int TB = tile_bytes(FMT);
+  const bool down = st == MK_DOWN;
+  // RMSNorm scale of the input rows and the act blocks (K = 896 stages) in one round trip
+  if (MODE != MODE_RESID && threadIdx.x < 16) {
+    float sum = 0.f;
+    for (int r = 0; r < HRB; ++r) sum += __ldcg(gp.ss_in + r * 16 + threadIdx.x);
+    sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
+  }
+  if (!down) {
+    const uint4* src = reinterpret_cast<const uint4*>(gp.act);
+    uint4* dst = reinterpret_cast<uint4*>(sAct);
+    for (int i = threadIdx.x; i < (int)(MK_ACT_BYTES / 16); i += MK_CONS) dst[i] = __ldcg(src + i);
+  }
+  mk_sync();
+  if (!down && FMT != VP_FMT_F16 && warp < H / GS) {
+    const uint32_t ONE2 = 0x3C003C00u;
+    float xs[2][4] = {};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 b = act_frag_smem(sAct, warp, j, lane);
+      mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
+      mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
+    }
+    if (gid == 0) {
+      sX[warp * 16 + 2 * tid4] = xs[0][0];
+      sX[warp * 16 + 2 * tid4 + 1] = xs[0][1];
+      sX[warp * 16 + 8 + 2 * tid4] = xs[1][0];
+      sX[warp * 16 + 8 + 2 * tid4 + 1] = xs[1][1];
+    }
+  }
+  mk_sync();
+
+  // jobs (row-block i, part q) -> warp (i * P + q) % 16, in increasing tile order per warp
+  const int jobs = nrb * P;
+  const int npieces = (nrb * ng + tp - 1) / tp;
+  bool ok = true;
+  for (int j = warp; j < jobs && ok; j += MK_WARPS) {
+    const int i = j / P, q = j % P;
+    const int ga = q * ng / P, gb = (q + 1) * ng / P;
+    float acc[2][4] = {};
+    for (int g = ga; g < gb; g += 2) {
+      // tiles g and g+1 (if in the part): release the pieces before g's, wait for both
+      const int idx = i * ng + g;
+      const int k = piece0 + idx / tp;
+      if (!mk_release(rg, k, lane)) { ok = false; break; }
+      const uint8_t* base = mk_piece(rg, k);
+      if (!base) { ok = false; break; }
+      const uint8_t* t0 = base + (size_t)(idx % tp) * TB;
+      if (g + 1 < gb) {
+        const int k1 = piece0 + (idx + 1) / tp;
+        const uint8_t* base1 = mk_piece(rg, k1);
+        if (!base1) { ok = false; break; }
+        const uint8_t* const tt[2] = {t0, base1 + (size_t)((idx + 1) % tp) * TB};
+        if (down) mk_tiles<FMT, true, 2>(tt, g, sAct, sX, gp.act, lane, acc);
+        else mk_tiles<FMT, false, 2>(tt, g, sAct, sX, gp.act, lane, acc);
+      } else {
+        const uint8_t* const tt[1] = {t0};
+        if (down) mk_tiles<FMT, true, 1>(tt, g, sAct, sX, gp.act, lane, acc);
+        else mk_tiles<FMT, false, 1>(tt, g, sAct, sX, gp.act, lane, acc);
+      }
+    }
+    if (!ok) break;
+    if (P == 1) {
+      // lm_head: running best (value, lowest id) per token over this warp's row-blocks
+      const int rb = rb0 + i;
+      const int v0 = rb * 16 + gid, v1 = v0 + 8;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = nt * 8 + 2 * tid4 + e;
+          const float l0 = acc[nt][e] * sRs[t], l1 = acc[nt][2 + e] * sRs[t];
+          float bv = l0;
+          int bi = v0;
+          if (l1 > bv) { bv = l1; bi = v1; }
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+          }
+          if (bv > lmV[nt][e] || (bv == lmV[nt][e] && bi < lmI[nt][e])) { lmV[nt][e] = bv; lmI[nt][e] = bi; }
+        }
+    } else {
+      float* part = sPart + j * 256;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          part[(gid + 8 * (r >> 1)) * 16 + nt * 8 + 2 * tid4 + (r & 1)] = acc[nt][r];
+    }
+  }
+  // this warp is done with every piece of the stage
+  if (ok) ok = mk_release(rg, piece0 + npieces, lane);
+  if (!ok) {
+    if (lane == 0) set_error(p.s.st, VP_DEV_ERR_TIMEOUT);
+    *sAbort = 1;
+  }
+  mk_sync();
+  if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
+  if (P > 1) {
+    for (int i = warp; i < nrb; i += MK_WARPS) {
+      float sum[2][4] = {};
+      for (int q = 0; q < P; ++q) {
+        const float* part = sPart + (i * P + q) * 256;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+            sum[nt][r] += part[(gid + 8 * (r >> 1)) * 16 + nt * 8 + 2 * tid4 + (r & 1)];
+      }
+      gemm_epilogue<MODE>(gp, rb0 + i, sum, sRs, lane);
+    }
+  }
+  return true;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int sAbort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + MK_OFF_BAR);
+  uint64_t* empty = full + MK_NSLOT;
+  RowInfo* sRi = reinterpret_cast<RowInfo*>(smem + MK_OFF_RI);
+  AttnSmem& sAtt = *reinterpret_cast<AttnSmem*>(smem + MK_OFF_ACT);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < MK_NSLOT; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, MK_WARPS);
+    }
+    fence_barrier_init();
+    sAbort = 0;
+  }
+  __syncthreads();
+
+  if (warp == MK_WARPS) {
+    mk_producer<FMT>(p, smem, &sAbort);
+    __syncwarp();
+  } else {
+    unsigned long long target = 0;
+    int nstamp = 0;
+    auto stamp = [&]() {
+      if (cta == 0 && threadIdx.x == 0 && p.trace && nstamp < MK_TRACE) p.trace[nstamp] = globaltimer();
+      ++nstamp;
+    };
+    stamp();
+    auto barrier = [&]() -> bool {
+      target += (unsigned long long)G;
+      const bool r = grid_barrier(p, target, &sAbort);
+      stamp();
+      return r;
+    };
+
+    // ---- embed the pass rows, publish RowInfo ----
+    if (cta < ROWS) {
+      EmbedArgs ea;
+      ea.E = p.embed;
+      ea.ln1 = p.ln1[0];
+      ea.prompt = p.prompt;
+      ea.chunk_n = p.chunk_n;
+      ea.chunk_start = p.chunk_start;
+      ea.total_n = p.total_n;
+      embed_row<FMT>(ea, p.s, cta);
+    }
+    bool ok = barrier();
+    if (ok) {
+      const int* src = reinterpret_cast<const int*>(p.s.ri);
+      int* dst = reinterpret_cast<int*>(sRi);
+      for (int i = threadIdx.x; i < (int)(sizeof(RowInfo) / 4); i += MK_CONS) dst[i] = __ldcg(src + i);
+    }
+    // the CTA that owns row-block `cta` of the hidden dimension (O and down epilogues) keeps its
+    // 16 x 16 slice of x in shared memory for the whole pass
+    float* sXrb = reinterpret_cast<float*>(smem + MK_OFF_XRB);
+    const bool own_x = cta < H / 16;
+    if (ok && own_x)
+      for (int i = threadIdx.x; i < 256; i += MK_CONS)
+        sXrb[i] = __ldcg(p.s.x + (i >> 4) * H + cta * 16 + (i & 15));
+    mk_sync();
+    Scratch s = p.s;
+    s.ri = sRi;
+    const bool live = ok && sRi->live != 0;
+    MkRing rg;
+    rg.base = smem;
+    rg.full = full;
+    rg.empty = empty;
+    rg.released = 0;
+    rg.waited = 0;
+    int piece0 = 0;
+    auto pieces = [&](int st) {
+      int rb0, nrb;
+      mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+      return mk_pieces(FMT, st, nrb);
+    };
+    float lmV[2][2];
+    int lmI[2][2];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) { lmV[a][b] = -INFINITY; lmI[a][b] = 0x7fffffff; }
+
+    if (live) {
+      for (int l = 0; l < p.n_layers && ok; ++l) {
+        GemmParams gp = {};
+        gp.s = s;
+        gp.layer = l;
+        // QKV (+ RMSNorm scale, bias, RoPE, KV write)
+        gp.w = p.wqkv[l]; gp.act = s.act_h; gp.nrb = QKV / 16; gp.ng = H / GS;
+        gp.bias = p.bqkv[l]; gp.ss_in = s.ss;
+        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        piece0 += pieces(MK_QKV);
+        if (!ok) break;
+        // attention
+        {
+          const int units = attn_units(sRi);
+          for (int u = cta; u < units; u += G) attn_unit(s, l, p.max_chunks, u, sAtt);
+        }
+        ok = barrier();
+        if (!ok) break;
+        // O + residual
+        gp = GemmParams{};
+        gp.s = s; gp.layer = l;
+        gp.w = p.wo[l]; gp.act = s.act_a; gp.nrb = H / 16; gp.ng = H / GS;
+        gp.wnext = p.ln2[l]; gp.ss_out = s.ss; gp.act_out = s.act_h;
+        gp.xs = own_x ? sXrb : nullptr;
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        piece0 += pieces(MK_O);
+        if (!ok) break;
+        // gate/up + SiLU
+        gp = GemmParams{};
+        gp.s = s; gp.layer = l;
+        gp.w = p.wgu[l]; gp.act = s.act_h; gp.nrb = 2 * F / 16; gp.ng = H / GS;
+        gp.ss_in = s.ss; gp.act_out = s.act_f;
+        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        piece0 += pieces(MK_GU);
+        if (!ok) break;
+        // down + residual
+        gp = GemmParams{};
+        gp.s = s; gp.layer = l;
+        gp.w = p.wd[l]; gp.act = s.act_f; gp.nrb = H / 16; gp.ng = F / GS;
+        gp.wnext = l + 1 < p.n_layers ? p.ln1[l + 1] : p.final_norm;
+        gp.ss_out = s.ss; gp.act_out = s.act_h;
+        gp.xs = own_x ? sXrb : nullptr;
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        piece0 += pieces(MK_DOWN);
+      }
+      if (ok && p.do_lm) {
+        GemmParams gp = {};
+        gp.s = s;
+        gp.w = p.embed; gp.act = s.act_h; gp.nrb = p.nrb_lm; gp.ng = H / GS; gp.ss_in = s.ss;
+        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort, lmV, lmI);
+        // per-CTA best per token: lanes with gid == 0 hold tokens nt*8 + 2*tid4 + e
+        float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
+        int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
+        if ((lane >> 2) == 0) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int t = nt * 8 + 2 * (lane & 3) + e;
+              sLmV[warp * 16 + t] = lmV[nt][e];
+              sLmI[warp * 16 + t] = lmI[nt][e];
+            }
+        }
+        mk_sync();
+        if (threadIdx.x < 16) {
+          const int t = threadIdx.x;
+          float bv = sLmV[t];
+          int bi = sLmI[t];
+          for (int w = 1; w < MK_WARPS; ++w) {
+            const float v = sLmV[w * 16 + t];
+            const int id = sLmI[w * 16 + t];
+            if (v > bv || (v == bv && id < bi)) { bv = v; bi = id; }
+          }
+          p.lm_pval[t * G + cta] = bv;
+          p.lm_pidx[t * G + cta] = bi;
+        }
+        ok = ok && barrier();
+        if (ok && p.do_commit && cta == 0) commit_body(s, p.lm_pval, p.lm_pidx, G);
+      }
+    }
+    if (!live || !ok) sAbort = 1;  // the producer stops waiting for releases
+    stamp();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.exit_ctr, 1u) == (unsigned)G - 1) {
+      *p.bar = 0ull;  // every CTA is past its last barrier: the next launch starts from zero
+      *p.exit_ctr = 0u;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace vp

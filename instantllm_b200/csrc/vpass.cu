@@ -1,9 +1,9 @@
 // C ABI of the verification pass (include/vpass.h): context, weight packing, pass encoder.
 //
 // The pass encoder replaces Engine.encodeWidePass / encodePrefill / encodeCommitSpec
-// (Sources/Engine/Engine.swift:484-601): one verify pass is embed, 24 x (QKV, attention, O,
-// gate/up, down), lm_head, commit = 123 kernels, launched with programmatic dependent launch so
-// each kernel streams its weights while the previous one finishes, and replayed from a CUDA graph.
+// (Sources/Engine/Engine.swift:484-601, 171 Metal dispatches per pass): one verify pass (or one
+// 16-row prefill chunk) is ONE cooperative launch of the persistent pass kernel k_pass
+// (vp_mega.cuh), one CTA per SM, stages separated by grid barriers.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -13,9 +13,9 @@
 #include <string>
 #include <vector>
 
-#include "vp_attn.cuh"
 #include "vp_commit.cuh"
 #include "vp_gemm.cuh"
+#include "vp_mega.cuh"
 
 using namespace vp;
 
@@ -35,6 +35,8 @@ int fail(int code, const std::string& msg) {
       return fail(VP_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));    \
   } while (0)
 
+// Launch geometry of the stand-alone GEMM kernel (k_gemm), used for the full-logits parity helper
+// and the allocation-free argmax.
 struct StageCfg {
   int nrb, ng, nsplit, cg, cps;
   size_t smem;
@@ -46,7 +48,7 @@ StageCfg make_stage(int fmt, int rows, int cols, int nsplit) {
   c.nrb = rows / 16;
   c.ng = cols / GS;
   c.nsplit = nsplit;
-  const int per_chunk = fmt == VP_FMT_Q4 ? 7 : fmt == VP_FMT_Q8 ? 4 : 2;  // ~4 KiB chunks
+  const int per_chunk = mk_chunk_groups(fmt);
   const int ngs = (c.ng + nsplit - 1) / nsplit;
   c.cg = per_chunk < ngs ? per_chunk : ngs;
   c.cps = (c.nrb + GEMM_WARPS - 1) / GEMM_WARPS;
@@ -62,10 +64,14 @@ struct vp_ctx {
   bool have_w = false;
   Scratch s{};
   std::vector<void*> allocs;
-  StageCfg qkv{}, o{}, gu{}, down{}, lm{};
-  int att_grid = 0, max_chunks = 0;
-  cudaStream_t cap = nullptr;
-  cudaGraphExec_t pass_exec = nullptr;
+  StageCfg lm{};          // stand-alone lm_head GEMM (parity helper)
+  int grid = 0;           // CTAs of the pass kernel (one per SM)
+  int max_chunks = 0;
+  unsigned long long* bar = nullptr;
+  unsigned* exit_ctr = nullptr;
+  float* lm_pval = nullptr;  // [16][grid] per-CTA argmax partials of the last pass
+  int* lm_pidx = nullptr;
+  unsigned long long* trace = nullptr;  // stage timestamps of the last pass (ns)
 };
 
 namespace {
@@ -83,15 +89,15 @@ int dalloc(vp_ctx* c, T** p, size_t bytes) {
 }
 
 template <typename Kern, typename... Args>
-cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t st, Args... args) {
+cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t st, bool coop, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = coop ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
@@ -99,136 +105,61 @@ cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t s
 
 template <int FMT, int MODE>
 cudaError_t gemm_launch(const StageCfg& c, const GemmParams& p, cudaStream_t st) {
-  static bool attr_done[2] = {false, false};
-  (void)attr_done;
-  return launch(k_gemm<FMT, MODE>, c.grid(), GEMM_WARPS * 32, c.smem, st, p);
-}
-
-template <int FMT, int MODE>
-int set_smem_attr(size_t smem) {
-  VP_CUDA(cudaFuncSetAttribute(k_gemm<FMT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
-  return VP_OK;
+  return launch(k_gemm<FMT, MODE>, c.grid(), GEMM_WARPS * 32, c.smem, st, false, p);
 }
 
 template <int FMT>
 int set_attrs(vp_ctx* c) {
-  size_t mx = 0;
-  for (const StageCfg* sc : {&c->qkv, &c->o, &c->gu, &c->down, &c->lm}) mx = sc->smem > mx ? sc->smem : mx;
-  int r;
-  if ((r = set_smem_attr<FMT, MODE_QKV>(mx))) return r;
-  if ((r = set_smem_attr<FMT, MODE_RESID>(mx))) return r;
-  if ((r = set_smem_attr<FMT, MODE_SILU>(mx))) return r;
-  if ((r = set_smem_attr<FMT, MODE_ARGMAX>(mx))) return r;
+  VP_CUDA(cudaFuncSetAttribute(k_gemm<FMT, MODE_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)c->lm.smem));
+  VP_CUDA(cudaFuncSetAttribute(k_pass<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+  int per_sm = 0;
+  VP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass<FMT>, MK_THREADS, MK_SMEM));
+  if (per_sm < 1) return fail(VP_ERR_CUDA, "pass kernel does not fit on an SM");
   return VP_OK;
 }
 
-GemmParams base_params(vp_ctx* c, const StageCfg& sc, const void* w, const __half* act, int layer) {
-  GemmParams p = {};
-  p.w = static_cast<const uint8_t*>(w);
-  p.act = act;
-  p.nrb = sc.nrb;
-  p.ng = sc.ng;
-  p.nsplit = sc.nsplit;
-  p.cg = sc.cg;
-  p.cps = sc.cps;
-  p.layer = layer;
+MegaParams mega_params(vp_ctx* c) {
+  MegaParams p = {};
   p.s = c->s;
+  p.embed = static_cast<const uint8_t*>(c->w.embed);
+  p.final_norm = c->w.final_norm;
+  for (int l = 0; l < c->cfg.n_layers; ++l) {
+    p.wqkv[l] = static_cast<const uint8_t*>(c->w.wqkv[l]);
+    p.bqkv[l] = c->w.bqkv[l];
+    p.wo[l] = static_cast<const uint8_t*>(c->w.wo[l]);
+    p.wgu[l] = static_cast<const uint8_t*>(c->w.wgu[l]);
+    p.wd[l] = static_cast<const uint8_t*>(c->w.wd[l]);
+    p.ln1[l] = c->w.ln1[l];
+    p.ln2[l] = c->w.ln2[l];
+  }
+  p.n_layers = c->cfg.n_layers;
+  p.nrb_lm = c->cfg.vocab / 16;
+  p.max_chunks = c->max_chunks;
+  p.bar = c->bar;
+  p.exit_ctr = c->exit_ctr;
+  p.lm_pval = c->lm_pval;
+  p.lm_pidx = c->lm_pidx;
+  p.trace = c->trace;
   return p;
 }
 
-template <int FMT>
-int launch_embed(vp_ctx* c, cudaStream_t st, const int32_t* prompt, int chunk_n, int chunk_start,
-                 int total_n, int last) {
-  EmbedParams ep = {};
-  ep.E = static_cast<const uint8_t*>(c->w.embed);
-  ep.ln1 = c->w.ln1[0];
-  ep.prompt = prompt;
-  ep.chunk_n = chunk_n;
-  ep.chunk_start = chunk_start;
-  ep.total_n = total_n;
-  ep.last_chunk = last;
-  ep.s = c->s;
-  VP_CUDA(launch(k_embed<FMT>, ROWS, 256, 0, st, ep));
-  return VP_OK;
-}
-
-template <int FMT>
-int launch_layers_and_head(vp_ctx* c, cudaStream_t st, bool head) {
-  const vp_weights& w = c->w;
-  const int L = c->cfg.n_layers;
-  for (int l = 0; l < L; ++l) {
-    GemmParams p = base_params(c, c->qkv, w.wqkv[l], c->s.act_h, l);
-    p.bias = w.bqkv[l];
-    p.ss_in = c->s.ss;
-    VP_CUDA((gemm_launch<FMT, MODE_QKV>(c->qkv, p, st)));
-
-    AttnParams ap = {};
-    ap.layer = l;
-    ap.max_chunks = c->max_chunks;
-    ap.s = c->s;
-    VP_CUDA(launch(k_attention, c->att_grid, ATT_THREADS, 0, st, ap));
-
-    p = base_params(c, c->o, w.wo[l], c->s.act_a, l);
-    p.wnext = w.ln2[l];
-    p.ss_out = c->s.ss;
-    p.act_out = c->s.act_h;
-    VP_CUDA((gemm_launch<FMT, MODE_RESID>(c->o, p, st)));
-
-    p = base_params(c, c->gu, w.wgu[l], c->s.act_h, l);
-    p.ss_in = c->s.ss;
-    p.act_out = c->s.act_f;
-    VP_CUDA((gemm_launch<FMT, MODE_SILU>(c->gu, p, st)));
-
-    p = base_params(c, c->down, w.wd[l], c->s.act_f, l);
-    p.wnext = l + 1 < L ? w.ln1[l + 1] : w.final_norm;
-    p.ss_out = c->s.ss;
-    p.act_out = c->s.act_h;
-    VP_CUDA((gemm_launch<FMT, MODE_RESID>(c->down, p, st)));
-  }
-  if (head) {
-    GemmParams p = base_params(c, c->lm, w.embed, c->s.act_h, 0);
-    p.ss_in = c->s.ss;
-    p.pval = c->s.pval;
-    p.pidx = c->s.pidx;
-    VP_CUDA((gemm_launch<FMT, MODE_ARGMAX>(c->lm, p, st)));
+int launch_pass(vp_ctx* c, const MegaParams& p, cudaStream_t st) {
+  switch (c->cfg.format) {
+    case VP_FMT_Q4: VP_CUDA(launch(k_pass<VP_FMT_Q4>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
+    case VP_FMT_Q8: VP_CUDA(launch(k_pass<VP_FMT_Q8>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
+    default: VP_CUDA(launch(k_pass<VP_FMT_F16>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
   }
   return VP_OK;
 }
 
 int launch_commit(vp_ctx* c, cudaStream_t st) {
   CommitParams cp = {};
-  cp.nrb_lm = c->cfg.vocab / 16;
+  cp.pval = c->lm_pval;
+  cp.pidx = c->lm_pidx;
+  cp.nparts = c->grid;
   cp.s = c->s;
-  VP_CUDA(launch(k_commit, 1, COMMIT_THREADS, 0, st, cp));
-  return VP_OK;
-}
-
-template <int FMT>
-int verify_body(vp_ctx* c, cudaStream_t st) {
-  int r = launch_embed<FMT>(c, st, nullptr, 0, 0, 0, 0);
-  if (r) return r;
-  return launch_layers_and_head<FMT>(c, st, true);
-}
-
-int dispatch_verify(vp_ctx* c, cudaStream_t st) {
-  switch (c->cfg.format) {
-    case VP_FMT_Q4: return verify_body<VP_FMT_Q4>(c, st);
-    case VP_FMT_Q8: return verify_body<VP_FMT_Q8>(c, st);
-    default: return verify_body<VP_FMT_F16>(c, st);
-  }
-}
-
-template <int FMT>
-int prefill_body(vp_ctx* c, const int32_t* toks, int n, cudaStream_t st) {
-  for (int c0 = 0; c0 < n; c0 += ROWS) {
-    const int cn = n - c0 < ROWS ? n - c0 : ROWS;
-    const bool last = c0 + cn == n;
-    int r = launch_embed<FMT>(c, st, toks + c0, cn, c0, n, last);
-    if (r) return r;
-    if ((r = launch_layers_and_head<FMT>(c, st, last))) return r;
-    if (last && (r = launch_commit(c, st))) return r;
-  }
+  VP_CUDA(launch(k_commit, 1, COMMIT_THREADS, 0, st, false, cp));
   return VP_OK;
 }
 
@@ -283,17 +214,25 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   if (cfg->max_ctx < ROWS || cfg->max_ctx > (1 << 20)) return fail(VP_ERR_ARG, "max_ctx out of range");
   if (cfg->max_steps < 1 || cfg->max_steps > (1 << 24)) return fail(VP_ERR_ARG, "max_steps out of range");
   VP_CUDA(cudaSetDevice(cfg->device));
+  int sms = 0;
+  VP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device));
+  // every CTA keeps its row-blocks' partial tiles of a stage in MK_PART_SLOTS shared-memory slots,
+  // and QKV / O / down need one CTA per row-block
+  if (sms < QKV / 16) return fail(VP_ERR_DEVICE, "the pass kernel needs at least 72 SMs");
+  for (int st = MK_QKV; st <= MK_DOWN; ++st)
+    for (int cta = 0; cta < sms; ++cta) {
+      int rb0, n;
+      mk_range(st, cta, sms, cfg->vocab / 16, rb0, n);
+      if (n * mk_parts(st) > MK_PART_SLOTS)
+        return fail(VP_ERR_DEVICE, "too few SMs for the pass kernel's work split");
+    }
   vp_ctx* c = new vp_ctx();
   c->cfg = *cfg;
   const int fmt = cfg->format;
-  c->qkv = make_stage(fmt, QKV, H, 7);
-  c->o = make_stage(fmt, H, H, 7);
-  c->gu = make_stage(fmt, 2 * F, H, 1);
-  c->down = make_stage(fmt, H, F, 19);
   c->lm = make_stage(fmt, cfg->vocab, H, 1);
   c->lm.cps = 296 < (c->lm.nrb + 3) / 4 ? 296 : (c->lm.nrb + 3) / 4;
   c->max_chunks = (cfg->max_ctx + ATT_CHUNK - 1) / ATT_CHUNK + 1;
-  c->att_grid = 296;
+  c->grid = sms;
 
   Scratch& s = c->s;
   s.max_ctx = cfg->max_ctx;
@@ -301,9 +240,6 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   s.vocab = cfg->vocab;
   s.n_layers = cfg->n_layers;
   const size_t kv = (size_t)cfg->n_layers * NKV * cfg->max_ctx * HD * sizeof(__half);
-  size_t part_units = 0;
-  for (const StageCfg* sc : {&c->qkv, &c->o, &c->down})
-    part_units = (size_t)sc->nrb * sc->nsplit > part_units ? (size_t)sc->nrb * sc->nsplit : part_units;
   int r = VP_OK;
   if ((r = dalloc(c, &s.st, sizeof(vp_state))) || (r = dalloc(c, &s.ri, sizeof(RowInfo))) ||
       (r = dalloc(c, &s.tree, VP_TREE_INTS * sizeof(int32_t))) ||
@@ -313,13 +249,18 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &s.act_a, ROWS * H * sizeof(__half))) ||
       (r = dalloc(c, &s.act_f, ROWS * F * sizeof(__half))) ||
       (r = dalloc(c, &s.ss, HRB * ROWS * sizeof(float))) ||
-      (r = dalloc(c, &s.part, part_units * 256 * sizeof(float))) ||
+      (r = dalloc(c, &s.part, 256 * sizeof(float))) ||
       (r = dalloc(c, &s.tickets, 2048 * sizeof(int))) ||
       (r = dalloc(c, &s.att_part, (size_t)ROWS * NKV * c->max_chunks * ATT_REC * sizeof(float))) ||
       (r = dalloc(c, &s.kc, kv)) || (r = dalloc(c, &s.vc, kv)) ||
       (r = dalloc(c, &s.rope, (size_t)(cfg->max_ctx + ROWS) * 32 * sizeof(float2))) ||
       (r = dalloc(c, &s.pval, (size_t)ROWS * (cfg->vocab / 16) * sizeof(float))) ||
-      (r = dalloc(c, &s.pidx, (size_t)ROWS * (cfg->vocab / 16) * sizeof(int)))) {
+      (r = dalloc(c, &s.pidx, (size_t)ROWS * (cfg->vocab / 16) * sizeof(int))) ||
+      (r = dalloc(c, &c->bar, sizeof(unsigned long long))) ||
+      (r = dalloc(c, &c->exit_ctr, sizeof(unsigned))) ||
+      (r = dalloc(c, &c->lm_pval, (size_t)ROWS * sms * sizeof(float))) ||
+      (r = dalloc(c, &c->lm_pidx, (size_t)ROWS * sms * sizeof(int))) ||
+      (r = dalloc(c, &c->trace, MK_TRACE * sizeof(unsigned long long)))) {
     vp_destroy(c);
     return r;
   }
@@ -340,8 +281,6 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   else if (fmt == VP_FMT_Q8) r = set_attrs<VP_FMT_Q8>(c);
   else r = set_attrs<VP_FMT_F16>(c);
   if (r) { vp_destroy(c); return r; }
-  cudaError_t e = cudaStreamCreateWithFlags(&c->cap, cudaStreamNonBlocking);
-  if (e != cudaSuccess) { vp_destroy(c); return fail(VP_ERR_CUDA, cudaGetErrorString(e)); }
   *out = c;
   return VP_OK;
 }
@@ -349,8 +288,6 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
 void vp_destroy(vp_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->cfg.device);
-  if (c->pass_exec) cudaGraphExecDestroy(c->pass_exec);
-  if (c->cap) cudaStreamDestroy(c->cap);
   for (void* p : c->allocs) cudaFree(p);
   delete c;
 }
@@ -363,10 +300,6 @@ int vp_set_weights(vp_ctx* c, const vp_weights* w) {
       return fail(VP_ERR_ARG, "layer weight missing");
   c->w = *w;
   c->have_w = true;
-  if (c->pass_exec) {  // pointers are baked into the graph
-    cudaGraphExecDestroy(c->pass_exec);
-    c->pass_exec = nullptr;
-  }
   return VP_OK;
 }
 
@@ -376,9 +309,8 @@ int vp_begin(vp_ctx* c, int32_t cached, int32_t max_new, int32_t eos0, int32_t e
   if (cached + max_new + ROWS > c->cfg.max_ctx) return fail(VP_ERR_ARG, "request exceeds max_ctx");
   VP_CUDA(cudaSetDevice(c->cfg.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int last = 0;
-  launch(k_begin, 64, 256, 0, st, c->s.st, c->s.out_tokens, c->cfg.max_steps, (int)cached,
-         (int)max_new, (int)eos0, (int)eos1, c->cfg.max_ctx, last);
+  k_begin<<<64, 256, 0, st>>>(c->s.st, c->s.out_tokens, c->cfg.max_steps, (int)cached, (int)max_new,
+                              (int)eos0, (int)eos1, c->cfg.max_ctx, 0);
   VP_CUDA(cudaGetLastError());
   return VP_OK;
 }
@@ -388,11 +320,19 @@ int vp_prefill(vp_ctx* c, const int32_t* d_tokens, int32_t n, void* stream) {
   if (r) return r;
   if (!d_tokens || n < 1) return fail(VP_ERR_ARG, "empty prompt");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (c->cfg.format) {
-    case VP_FMT_Q4: return prefill_body<VP_FMT_Q4>(c, d_tokens, n, st);
-    case VP_FMT_Q8: return prefill_body<VP_FMT_Q8>(c, d_tokens, n, st);
-    default: return prefill_body<VP_FMT_F16>(c, d_tokens, n, st);
+  for (int c0 = 0; c0 < n; c0 += ROWS) {
+    const int cn = n - c0 < ROWS ? n - c0 : ROWS;
+    const bool last = c0 + cn == n;
+    MegaParams p = mega_params(c);
+    p.prompt = d_tokens + c0;
+    p.chunk_n = cn;
+    p.chunk_start = c0;
+    p.total_n = n;
+    p.do_lm = last;
+    p.do_commit = last;
+    if ((r = launch_pass(c, p, st))) return r;
   }
+  return VP_OK;
 }
 
 int vp_verify(vp_ctx* c, const int32_t* tree, void* stream) {
@@ -401,7 +341,9 @@ int vp_verify(vp_ctx* c, const int32_t* tree, void* stream) {
   if (!tree) return fail(VP_ERR_ARG, "null tree");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
-  return dispatch_verify(c, st);
+  MegaParams p = mega_params(c);
+  p.do_lm = 1;
+  return launch_pass(c, p, st);
 }
 
 int vp_verify_chain(vp_ctx* c, const int32_t* drafts, int32_t nd, void* stream) {
@@ -411,7 +353,9 @@ int vp_verify_chain(vp_ctx* c, const int32_t* drafts, int32_t nd, void* stream) 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_chain_tree<<<1, 32, 0, st>>>(c->s.tree, drafts, nd);
   VP_CUDA(cudaGetLastError());
-  return dispatch_verify(c, st);
+  MegaParams p = mega_params(c);
+  p.do_lm = 1;
+  return launch_pass(c, p, st);
 }
 
 int vp_commit(vp_ctx* c, void* stream) {
@@ -425,21 +369,11 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
   if (r) return r;
   if (!tree) return fail(VP_ERR_ARG, "null tree");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!c->pass_exec) {
-    cudaGraph_t g = nullptr;
-    VP_CUDA(cudaStreamBeginCapture(c->cap, cudaStreamCaptureModeThreadLocal));
-    r = dispatch_verify(c, c->cap);
-    if (!r) r = launch_commit(c, c->cap);
-    cudaError_t e = cudaStreamEndCapture(c->cap, &g);
-    if (r) { if (g) cudaGraphDestroy(g); return r; }
-    if (e != cudaSuccess) return fail(VP_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&c->pass_exec, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) { c->pass_exec = nullptr; return fail(VP_ERR_CUDA, cudaGetErrorString(e)); }
-  }
   VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
-  VP_CUDA(cudaGraphLaunch(c->pass_exec, st));
-  return VP_OK;
+  MegaParams p = mega_params(c);
+  p.do_lm = 1;
+  p.do_commit = 1;
+  return launch_pass(c, p, st);
 }
 
 int vp_read_state(vp_ctx* c, vp_state* host, void* stream) {
@@ -468,7 +402,15 @@ int vp_debug_logits(vp_ctx* c, float* d_out, void* stream) {
   if (r) return r;
   if (!d_out) return fail(VP_ERR_ARG, "null output");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  GemmParams p = base_params(c, c->lm, c->w.embed, c->s.act_h, 0);
+  GemmParams p = {};
+  p.w = static_cast<const uint8_t*>(c->w.embed);
+  p.act = c->s.act_h;
+  p.nrb = c->lm.nrb;
+  p.ng = c->lm.ng;
+  p.nsplit = 1;
+  p.cg = c->lm.cg;
+  p.cps = c->lm.cps;
+  p.s = c->s;
   p.ss_in = c->s.ss;
   p.pval = c->s.pval;
   p.pidx = c->s.pidx;
@@ -484,14 +426,15 @@ int vp_debug_logits(vp_ctx* c, float* d_out, void* stream) {
 int vp_buffer(vp_ctx* c, int32_t which, void** ptr, size_t* bytes) {
   if (!c || !ptr || !bytes) return fail(VP_ERR_ARG, "null argument");
   const size_t kv = (size_t)c->cfg.n_layers * NKV * c->cfg.max_ctx * HD * sizeof(__half);
-  const size_t pv = (size_t)ROWS * (c->cfg.vocab / 16) * 4;
+  const size_t pv = (size_t)ROWS * c->grid * 4;
   switch (which) {
     case 0: *ptr = c->s.x; *bytes = ROWS * H * 4; break;
     case 1: *ptr = c->s.q; *bytes = ROWS * H * 4; break;
     case 2: *ptr = c->s.kc; *bytes = kv; break;
     case 3: *ptr = c->s.vc; *bytes = kv; break;
-    case 4: *ptr = c->s.pval; *bytes = pv; break;
-    case 5: *ptr = c->s.pidx; *bytes = pv; break;
+    case 4: *ptr = c->lm_pval; *bytes = pv; break;
+    case 5: *ptr = c->lm_pidx; *bytes = pv; break;
+    case 6: *ptr = c->trace; *bytes = MK_TRACE * sizeof(unsigned long long); break;
     default: return fail(VP_ERR_ARG, "unknown buffer");
   }
   return VP_OK;

@@ -176,6 +176,14 @@ class VerifyEngine:
         check(self.lib.vp_buffer(self.ctx, which, ctypes.byref(ptr), ctypes.byref(nbytes)), "vp_buffer")
         return torch.as_tensor(_DevArray(ptr.value, shape, dtype), device=self.device)
 
+    def argmax_partials(self):
+        """Per-CTA argmax partials of the last pass, (value fp32 [16][parts], id int32 [16][parts]):
+        what the commit reduces."""
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+        check(self.lib.vp_buffer(self.ctx, 4, ctypes.byref(ptr), ctypes.byref(nbytes)), "vp_buffer")
+        parts = nbytes.value // (16 * 4)
+        return self.buffer(4, (16, parts), "<f4"), self.buffer(5, (16, parts), "<i4")
+
     def kv(self):
         shape = (self.n_layers, 2, self.max_ctx, 64)
         return self.buffer(2, shape, "<f2"), self.buffer(3, shape, "<f2")

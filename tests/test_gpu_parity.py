@@ -68,7 +68,6 @@ def test_commit_kernel_matches_commit_oracle(small):
     if fmt != "q4":
         pytest.skip("format independent")
     rng = np.random.default_rng(17)
-    nrb = VOCAB_SMALL // 16
     for case in range(25):
         prompt = (synth.make_prompt(20 + case, seed=case) % VOCAB_SMALL).tolist()
         eng.begin(0, 40)
@@ -84,16 +83,16 @@ def test_commit_kernel_matches_commit_oracle(small):
         path = A.walk_tree(tree, [y[tree["depth"][i]] for i in range(n)])
         for k, row in enumerate([0] + path):
             g[row] = int(y[k])
-        pval = eng.buffer(4, (16, nrb), "<f4")
-        pidx = eng.buffer(5, (16, nrb), "<i4")
+        pval, pidx = eng.argmax_partials()
+        parts = pval.shape[1]
         pval.fill_(-1.0)
-        pidx.copy_(torch.arange(nrb, device=pval.device, dtype=torch.int32).mul(16).expand(16, nrb))
+        pidx.copy_(torch.arange(parts, device=pval.device, dtype=torch.int32).mul(16).expand(16, parts))
         for t in range(n):
             # two tied maxima: the lower id must win
-            pval[t, (g[t] + 300) % nrb] = 5.0
-            pidx[t, (g[t] + 300) % nrb] = g[t]
-            pval[t, (g[t] + 301) % nrb] = 5.0
-            pidx[t, (g[t] + 301) % nrb] = g[t] + 1000
+            pval[t, (g[t] + 30) % parts] = 5.0
+            pidx[t, (g[t] + 30) % parts] = g[t]
+            pval[t, (g[t] + 31) % parts] = 5.0
+            pidx[t, (g[t] + 31) % parts] = g[t] + 1000
         k_before, v_before = [b.clone() for b in eng.kv()]
         eng.commit()
         st = eng.state()
