@@ -144,27 +144,40 @@ __device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
 constexpr int GQ = NQ / NKV;            // 7 query heads per KV head
 constexpr int ATT_TICKETS = 1024;       // offset of the attention arrival counters in tickets
 constexpr int ATT_REC = GQ * (2 + HD);  // partial record of a chunk: per head m, l, o[64]
-constexpr int ATT_SEG = 8;              // chunks per work unit (segment)
+constexpr int ATT_SEG = 4;              // at most this many chunks per work unit (segment)
+constexpr int ATT_PAD = 8;              // row padding (halves) against shared-memory bank conflicts
 
 struct AttnSmem {
   float qs[GQ][HD];
-  float sc[GQ][ATT_CHUNK];
-  __half kv[2][ATT_CHUNK][HD];
+  alignas(16) __half qh[2][8][HD + ATT_PAD];   // q * 0.125 as fp16 hi + lo parts, row 7 zero
+  float sc[GQ][ATT_CHUNK + 4];
+  alignas(16) __half kv[2][2][ATT_CHUNK][HD + ATT_PAD];  // [buffer][K, V][position][dim]
   int slots[ATT_SEG][ATT_CHUNK];
   float rec[ATT_SEG][ATT_REC];  // this segment's chunk partials
   int last;
 };
 
+// K/V double buffers double as the staging area of a row's chunk records in the combine.
+constexpr int ATT_MAX_REC_STAGED = (int)(sizeof(__half) * 2 * 2 * ATT_CHUNK * (HD + ATT_PAD) / (ATT_REC * 4));
+
 __device__ __forceinline__ int attn_chunks(const RowInfo* ri, int t, int pos) {
   return (pos + ri->depth[t] + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
 }
-__device__ __forceinline__ int attn_segs(int nch) { return (nch + ATT_SEG - 1) / ATT_SEG; }
+// Chunks per work unit: enough units to occupy `ctas` CTAs, at most ATT_SEG. The chunk records and
+// their combine do not depend on how chunks are grouped into units, so this is free to follow the
+// pass shape.
+__device__ __forceinline__ int attn_segsize(const RowInfo* ri, int ctas) {
+  int total = 0;
+  for (int t = 0; t < ri->n; ++t) total += NKV * attn_chunks(ri, t, ri->pos);
+  return min(ATT_SEG, max(1, (total + ctas - 1) / ctas));
+}
+__device__ __forceinline__ int attn_segs(int nch, int segsz) { return (nch + segsz - 1) / segsz; }
 
-// Number of attention work units of a pass: (row, kv head, segment of <= 8 chunks).
-__device__ int attn_units(const RowInfo* ri) {
+// Number of attention work units of a pass: (row, kv head, segment of <= segsz chunks).
+__device__ int attn_units(const RowInfo* ri, int segsz) {
   const int n = ri->n, pos = ri->pos;
   int total = 0;
-  for (int t = 0; t < n; ++t) total += NKV * attn_segs(attn_chunks(ri, t, pos));
+  for (int t = 0; t < n; ++t) total += NKV * attn_segs(attn_chunks(ri, t, pos), segsz);
   return total;
 }
 
@@ -193,19 +206,26 @@ __device__ __forceinline__ void attn_combine(const Scratch& s, const float* base
 // 64-position window of the row's virtual sequence. A row with one segment (virtual length <= 512)
 // is combined right here; longer rows write chunk records and the segment that completes the row
 // combines all of them (same formula, same chunk order).
-__device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, AttnSmem& sm) {
+__device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, int segsz, AttnSmem& sm,
+                          unsigned long long* trace = nullptr) {
+  int ntr = 0;
+  auto tstamp = [&]() {
+    if (trace && threadIdx.x == 0 && ntr < 40) trace[ntr] = globaltimer();
+    ++ntr;
+  };
+  tstamp();
   const RowInfo* ri = s.ri;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = ri->n, pos = ri->pos;
   int t = 0, rem = u, nch = 1, nseg = 1;
   for (; t < n; ++t) {
     nch = attn_chunks(ri, t, pos);
-    nseg = attn_segs(nch);
+    nseg = attn_segs(nch, segsz);
     if (rem < NKV * nseg) break;
     rem -= NKV * nseg;
   }
   const int g = rem / nseg, seg = rem % nseg;
-  const int c0 = seg * ATT_SEG, c1 = min(nch, c0 + ATT_SEG);
+  const int c0 = seg * segsz, c1 = min(nch, c0 + segsz);
   const int L = pos + ri->depth[t] + 1;
   const __half* kb = s.kc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
   const __half* vb = s.vc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
@@ -216,57 +236,70 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, At
         jv < pos ? jv : pos + ri->path[t][min(max(jv - pos, 0), ROWS - 1)];
   }
   cons_sync();
-  // K and V rows of a chunk: 2 x 64 rows x 128 bytes = 1024 16-byte words, two per thread, loaded
-  // into registers one chunk ahead of the compute (q travels with the first chunk)
-  auto load_kv = [&](int ci, int cnt, uint4 (&v)[2]) {
+  // K and V rows of a chunk: 2 x 64 rows x 128 bytes = 1024 16-byte copies, two per thread, as
+  // cp.async one chunk ahead (barriers do not wait for them); rows past the sequence are zeros.
+  // evict-last keeps the KV cache resident in L2 against the streaming weights.
+  const uint64_t kvpol = policy_evict_last();
+  auto load_kv = [&](int ci, int buf) {
+    const int cnt = min(L - (c0 + ci) * ATT_CHUNK, ATT_CHUNK);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int i = tid + k * PASS_THREADS;
       const int which = i / (ATT_CHUNK * 8), r = (i / 8) % ATT_CHUNK, part = i % 8;
-      v[k] = make_uint4(0, 0, 0, 0);
-      if (r < cnt)
-        v[k] = __ldcg(reinterpret_cast<const uint4*>((which ? vb : kb) + (size_t)sm.slots[ci][r] * HD + part * 8));
+      const int slot = r < cnt ? sm.slots[ci][r] : 0;
+      cp_async16(&sm.kv[buf][which][r][part * 8], (which ? vb : kb) + (size_t)slot * HD + part * 8,
+                 r < cnt ? 16u : 0u, kvpol);
     }
+    cp_async_commit();
   };
-  uint4 kvr[2];
-  load_kv(0, min(L - c0 * ATT_CHUNK, ATT_CHUNK), kvr);
+  load_kv(0, 0);
   for (int i = tid; i < GQ * HD; i += PASS_THREADS)
     sm.qs[i / HD][i % HD] = __ldcg(s.q + t * H + (g * GQ + i / HD) * HD + i % HD);
   for (int c = c0; c < c1; ++c) {
-    const int ci = c - c0;
+    const int ci = c - c0, buf = ci & 1;
     const int j0 = c * ATT_CHUNK, cnt = min(L - j0, ATT_CHUNK);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = tid + k * PASS_THREADS;
-      const int which = i / (ATT_CHUNK * 8), r = (i / 8) % ATT_CHUNK, part = i % 8;
-      *reinterpret_cast<uint4*>(&sm.kv[which][r][part * 8]) = kvr[k];
+    if (c + 1 < c1) {
+      load_kv(ci + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     cons_sync();
-    if (c + 1 < c1) load_kv(ci + 1, min(L - (c + 1) * ATT_CHUNK, ATT_CHUNK), kvr);
-    // scores: 8 threads per position, 8 dims each, fixed-order combine
-    {
-      const int pp = tid >> 3, part = tid & 7;
-      float a[GQ];
-#pragma unroll
-      for (int h = 0; h < GQ; ++h) a[h] = 0.f;
-      const __half2* kr = reinterpret_cast<const __half2*>(&sm.kv[0][pp][part * 8]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 kv = __half22float2(kr[i]);
-#pragma unroll
-        for (int h = 0; h < GQ; ++h)
-          a[h] = fmaf(sm.qs[h][part * 8 + 2 * i + 1], kv.y, fmaf(sm.qs[h][part * 8 + 2 * i], kv.x, a[h]));
+    tstamp();
+    // scores S = (q * 0.125) K^T on the tensor cores: warp w < 8 takes positions 8w..8w+7,
+    // M = heads (7 of 16 rows used), K = 64 dims, q as fp16 hi + lo (near-fp32 product)
+    if (c == c0) {
+      for (int i = tid; i < 8 * HD; i += PASS_THREADS) {
+        const int h = i / HD, d = i % HD;
+        const float v = h < GQ ? sm.qs[h][d] * ATTN_SCALE : 0.f;
+        const __half hi = __float2half_rn(v);
+        sm.qh[0][h][d] = hi;
+        sm.qh[1][h][d] = __float2half_rn(v - __half2float(hi));
       }
+      cons_sync();
+    }
+    if (warp < 8) {
+      const int gid = lane >> 2, t4 = lane & 3;
+      float acc[2][4] = {};  // hi and lo parts of q: two independent chains, added at the end
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {
-        float v = a[h];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (part == 0) sm.sc[h][pp] = pp < cnt ? v * ATTN_SCALE : -INFINITY;
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sm.kv[buf][0][warp * 8 + gid][ks * 16 + 2 * t4]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sm.kv[buf][0][warp * 8 + gid][ks * 16 + 2 * t4 + 8]);
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&sm.qh[part][gid][ks * 16 + 2 * t4]);
+          const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&sm.qh[part][gid][ks * 16 + 2 * t4 + 8]);
+          mma16816(acc[part], a0, 0u, a2, 0u, b0, b1);
+        }
+      }
+      if (gid < GQ) {
+        const int p0 = warp * 8 + 2 * t4;
+        sm.sc[gid][p0] = p0 < cnt ? acc[0][0] + acc[1][0] : -INFINITY;
+        sm.sc[gid][p0 + 1] = p0 + 1 < cnt ? acc[0][1] + acc[1][1] : -INFINITY;
       }
     }
     cons_sync();
+    tstamp();
     // per-head max and exp-sum over the chunk (warp h, two positions per lane)
     if (warp < GQ) {
       const float v0 = sm.sc[warp][lane], v1 = sm.sc[warp][lane + 32];
@@ -279,20 +312,49 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, At
       if (lane == 0) { sm.rec[ci][warp * (2 + HD)] = m; sm.rec[ci][warp * (2 + HD) + 1] = l; }
     }
     cons_sync();
-    // weighted V: thread (head, dim), positions in order
-    {
-      const int d = tid & 63, h = tid >> 6;
-      if (h < GQ) {
-        float o = 0.f;
-        for (int pp = 0; pp < cnt; ++pp) o = fmaf(sm.sc[h][pp], __half2float(sm.kv[1][pp][d]), o);
-        sm.rec[ci][h * (2 + HD) + 2 + d] = o;
+    tstamp();
+    // weighted V: O = P V on the tensor cores: warp w < 8 takes dims 8w..8w+7, M = heads,
+    // K = the chunk's 64 positions, P as fp16 hi + lo
+    if (warp < 8) {
+      const int gid = lane >> 2, t4 = lane & 3;
+      float acc2[2][4] = {};  // hi and lo parts of P: two independent chains
+      const int d = warp * 8 + gid;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          uint32_t a[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int pp = ks * 16 + 2 * t4 + 8 * hh;
+            float e0 = 0.f, e1 = 0.f;
+            if (gid < GQ) { e0 = sm.sc[gid][pp]; e1 = sm.sc[gid][pp + 1]; }
+            __half h0 = __float2half_rn(e0), h1 = __float2half_rn(e1);
+            if (part) {
+              h0 = __float2half_rn(e0 - __half2float(h0));
+              h1 = __float2half_rn(e1 - __half2float(h1));
+            }
+            a[hh] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          }
+          const int pb = ks * 16 + 2 * t4;
+          const uint32_t b0 = (uint32_t)__half_as_ushort(sm.kv[buf][1][pb][d]) |
+                              ((uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 1][d]) << 16);
+          const uint32_t b1 = (uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 8][d]) |
+                              ((uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 9][d]) << 16);
+          mma16816(acc2[part], a[0], 0u, a[1], 0u, b0, b1);
+        }
+      if (gid < GQ) {
+        sm.rec[ci][gid * (2 + HD) + 2 + warp * 8 + 2 * t4] = acc2[0][0] + acc2[1][0];
+        sm.rec[ci][gid * (2 + HD) + 2 + warp * 8 + 2 * t4 + 1] = acc2[0][1] + acc2[1][1];
       }
     }
     cons_sync();
   }
+  tstamp();
   if (nseg == 1) {
     attn_combine<false>(s, &sm.rec[0][0], nch, t, g);
     cons_sync();
+    tstamp();
     return;
   }
   float* base = s.att_part + (size_t)(t * NKV + g) * max_chunks * ATT_REC;
@@ -303,7 +365,16 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, At
   cons_sync();
   if (sm.last) {
     __threadfence();
-    attn_combine<true>(s, base, nch, t, g);
+    // all chunk records of the row into shared memory in one coalesced round trip (they fit: the
+    // K/V buffers are free now), then the combine reads shared memory only
+    if (nch <= ATT_MAX_REC_STAGED) {
+      float* recs = reinterpret_cast<float*>(&sm.kv[0][0][0][0]);
+      for (int i = tid; i < nch * ATT_REC; i += PASS_THREADS) recs[i] = __ldcg(base + i);
+      cons_sync();
+      attn_combine<false>(s, recs, nch, t, g);
+    } else {
+      attn_combine<true>(s, base, nch, t, g);  // long rows: read the records in place
+    }
     if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
   }
   cons_sync();

@@ -156,6 +156,17 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// 16-byte cp.async global -> shared (bypasses L1); src_bytes 0 fills zeros. CTA barriers do not
+// wait for these copies, so they can run ahead across barriers (unlike ordinary loads).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(src_bytes), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // D += A * B, m16n8k16, fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {

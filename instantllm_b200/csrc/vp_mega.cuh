@@ -561,8 +561,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         if (!ok) break;
         // attention
         {
-          const int units = attn_units(sRi);
-          for (int u = cta; u < units; u += G) attn_unit(s, l, p.max_chunks, u, sAtt);
+          const int segsz = attn_segsize(sRi, G);
+          const int units = attn_units(sRi, segsz);
+          for (int u = cta; u < units; u += G)
+            attn_unit(s, l, p.max_chunks, u, segsz, sAtt,
+                      (p.trace && cta == 0 && l == 5 && u == 0) ? p.trace + 200 : nullptr);
         }
         ok = barrier();
         if (!ok) break;
