@@ -138,62 +138,59 @@ __device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
   if (tid < HRB) s.ss[tid * 16 + t] = sPart[tid];
 }
 
-// ---------------------------------------------------------------------------------------------
 // Attention
+//
+// Records: the virtual sequence of row t is cut into fixed 32-position sub-chunks; each
+// (row, query head, sub-chunk) gets a record (max, exp-sum, unnormalised o[64]) and the output is
+// the combine of the row's records in sub-chunk order. Sub-chunk boundaries depend only on virtual
+// positions, so a row's output is bit-identical in a 16-row tree pass and in a 1-row pass.
+//
+// Work split: one unit (CTA) per (row t, kv head g, segment of <= ATT_SEGSUB sub-chunks). Warp w
+// stages sub-chunk w of the segment (its 32 K and V rows, coalesced cp.async into its own
+// XOR-swizzled buffer), loads the 7 query heads as fp16 hi + lo A fragments meanwhile, and computes
+// S = (q/8) K^T, the masked softmax and O = P V on the tensor cores (K and V B fragments by
+// ldmatrix). Its record replaces its K rows in shared memory and the CTA combines the records. A
+// row longer than one segment writes its records to global memory; the segment that arrives last
+// combines them all.
 
 constexpr int GQ = NQ / NKV;            // 7 query heads per KV head
 constexpr int ATT_TICKETS = 1024;       // offset of the attention arrival counters in tickets
-constexpr int ATT_REC = GQ * (2 + HD);  // partial record of a chunk: per head m, l, o[64]
-constexpr int ATT_SEG = 4;              // at most this many chunks per work unit (segment)
-constexpr int ATT_PAD = 8;              // row padding (halves) against shared-memory bank conflicts
+constexpr int ATT_REC = GQ * (2 + HD);  // records of a (row, kv head, sub-chunk): per head m, l, o[64]
+constexpr int ATT_SEGSUB = 10;          // sub-chunks per unit (one per warp; shared-memory bound)
 
 struct AttnSmem {
-  float qs[GQ][HD];
-  alignas(16) __half qh[2][8][HD + ATT_PAD];   // q * 0.125 as fp16 hi + lo parts, row 7 zero
-  float sc[GQ][ATT_CHUNK + 4];
-  alignas(16) __half kv[2][2][ATT_CHUNK][HD + ATT_PAD];  // [buffer][K, V][position][dim]
-  int slots[ATT_SEG][ATT_CHUNK];
-  float rec[ATT_SEG][ATT_REC];  // this segment's chunk partials
+  // [warp][K, V][position][dim] staging; the warp's record overwrites its K rows once S is done
+  alignas(128) __half kv[ATT_SEGSUB][2][ATT_SUB][HD];
   int last;
 };
+constexpr int ATT_REC_STRIDE = 2 * ATT_SUB * HD / 2;  // floats between the records of two warps
+static_assert(ATT_REC * 4 <= ATT_SUB * HD * 2, "a record fits in the K rows of its buffer");
 
-// K/V double buffers double as the staging area of a row's chunk records in the combine.
-constexpr int ATT_MAX_REC_STAGED = (int)(sizeof(__half) * 2 * 2 * ATT_CHUNK * (HD + ATT_PAD) / (ATT_REC * 4));
-
-__device__ __forceinline__ int attn_chunks(const RowInfo* ri, int t, int pos) {
-  return (pos + ri->depth[t] + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
+__device__ __forceinline__ int attn_subs(const RowInfo* ri, int t) {
+  return (ri->pos + ri->depth[t] + 1 + ATT_SUB - 1) / ATT_SUB;
 }
-// Chunks per work unit: enough units to occupy `ctas` CTAs, at most ATT_SEG. The chunk records and
-// their combine do not depend on how chunks are grouped into units, so this is free to follow the
-// pass shape.
-__device__ __forceinline__ int attn_segsize(const RowInfo* ri, int ctas) {
-  int total = 0;
-  for (int t = 0; t < ri->n; ++t) total += NKV * attn_chunks(ri, t, ri->pos);
-  return min(ATT_SEG, max(1, (total + ctas - 1) / ctas));
-}
-__device__ __forceinline__ int attn_segs(int nch, int segsz) { return (nch + segsz - 1) / segsz; }
+__device__ __forceinline__ int attn_segs(int nsub) { return (nsub + ATT_SEGSUB - 1) / ATT_SEGSUB; }
 
-// Number of attention work units of a pass: (row, kv head, segment of <= segsz chunks).
-__device__ int attn_units(const RowInfo* ri, int segsz) {
-  const int n = ri->n, pos = ri->pos;
+// Number of attention work units of a pass.
+__device__ __forceinline__ int attn_units(const RowInfo* ri) {
   int total = 0;
-  for (int t = 0; t < n; ++t) total += NKV * attn_segs(attn_chunks(ri, t, pos), segsz);
+  for (int t = 0; t < ri->n; ++t) total += NKV * attn_segs(attn_subs(ri, t));
   return total;
 }
 
-// Final output of (row t, kv head g) from the chunk partials in fixed chunk order:
-// M = max m_c, O = sum o_c e^(m_c - M) / sum l_c e^(m_c - M).
+// Final output of (row t, kv head g) from its records in sub-chunk order (record cc at
+// base + cc * stride): M = max m_c, O = sum o_c e^(m_c - M) / sum l_c e^(m_c - M).
 template <bool GLOBAL>
-__device__ __forceinline__ void attn_combine(const Scratch& s, const float* base, int nch, int t,
-                                             int g) {
+__device__ __forceinline__ void attn_combine(const Scratch& s, const float* base, int stride, int nsub,
+                                             int t, int g) {
+  auto ld = [&](const float* q) { return GLOBAL ? __ldcg(q) : *q; };
   for (int i = threadIdx.x; i < GQ * HD; i += PASS_THREADS) {
     const int h = i / HD, d = i % HD;
-    auto ld = [&](const float* q) { return GLOBAL ? __ldcg(q) : *q; };
     float M = -INFINITY;
-    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ld(base + cc * ATT_REC + h * (2 + HD)));
+    for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, ld(base + cc * stride + h * (2 + HD)));
     float O = 0.f, Ls = 0.f;
-    for (int cc = 0; cc < nch; ++cc) {
-      const float* r = base + cc * ATT_REC + h * (2 + HD);
+    for (int cc = 0; cc < nsub; ++cc) {
+      const float* r = base + cc * stride + h * (2 + HD);
       const float w = expf(ld(r) - M);
       Ls = fmaf(ld(r + 1), w, Ls);
       O = fmaf(ld(r + 2 + d), w, O);
@@ -202,182 +199,196 @@ __device__ __forceinline__ void attn_combine(const Scratch& s, const float* base
   }
 }
 
-// One unit with PASS_THREADS threads: the chunks of one segment of (row t, kv head g), each a
-// 64-position window of the row's virtual sequence. A row with one segment (virtual length <= 512)
-// is combined right here; longer rows write chunk records and the segment that completes the row
-// combines all of them (same formula, same chunk order).
-__device__ void attn_unit(const Scratch& s, int layer, int max_chunks, int u, int segsz, AttnSmem& sm,
+// fp16 hi + lo split of two values: hi = rn(v), lo = rn(v - hi).
+__device__ __forceinline__ void split_half2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+  lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+// Byte offset of 16-byte chunk k (dims 8k..8k+7) of staged row r: XOR swizzle, so that the 8 rows
+// of an 8x8 ldmatrix block fall in distinct bank groups.
+__device__ __forceinline__ uint32_t kv_off(int r, int k) { return (uint32_t)(r * HD * 2 + ((k ^ (r & 7)) << 4)); }
+
+// One warp: sub-chunk c (virtual positions 32c..32c+31) of row t, kv head g, staged in buf
+// (K rows then V rows). Writes the record to rec (the K rows of buf).
+// kc, vc: the (layer, kv head) K and V caches; q: query row t (all heads).
+__device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, const __half* vc,
+                                       const RowInfo* ri, int t, int g, int c, __half* buf, float* rec,
+                                       unsigned long long* tr) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
+  if (tr && lane == 0) tr[0] = globaltimer();
+  const int pos = ri->pos, L = pos + ri->depth[t] + 1;
+  // stage the K and V rows: lane copies 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8,
+  // of both K and V; positions past the row are zeros
+  {
+    const uint64_t pol = policy_evict_last();
+    const int ch = lane & 7;
+    uint8_t* dk = reinterpret_cast<uint8_t*>(buf);
+#pragma unroll 2
+    for (int k = 0; k < 8; ++k) {
+      const int r = (lane >> 3) + 4 * k, jv = c * ATT_SUB + r;
+      const bool valid = jv < L;
+      const int slot = !valid ? 0 : jv < pos ? jv : pos + ri->path[t][min(jv - pos, ROWS - 1)];
+      const size_t src = (size_t)slot * HD + ch * 8;
+      const uint32_t off = kv_off(r, ch), n = valid ? 16u : 0u;
+      cp_async16(dk + off, kc + src, n, pol);
+      cp_async16(dk + ATT_SUB * HD * 2 + off, vc + src, n, pol);
+    }
+    cp_async_commit();
+  }
+  // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero)
+  uint32_t qa[4][2][2];  // [k-step][hi, lo][a0, a2]
+  {
+    const float* q = qrow + (g * GQ + min(gid, GQ - 1)) * HD;
+    const float z = gid < GQ ? ATTN_SCALE : 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float2 x0 = __ldcg(reinterpret_cast<const float2*>(q + ks * 16 + 2 * t4));
+      const float2 x2 = __ldcg(reinterpret_cast<const float2*>(q + ks * 16 + 2 * t4 + 8));
+      split_half2(x0.x * z, x0.y * z, qa[ks][0][0], qa[ks][1][0]);
+      split_half2(x2.x * z, x2.y * z, qa[ks][0][1], qa[ks][1][1]);
+    }
+  }
+  if (tr && lane == 0) tr[1] = globaltimer_after(__uint_as_float(qa[3][1][1]));
+  cp_async_wait<0>();
+  __syncwarp();
+  if (tr && lane == 0) tr[2] = globaltimer();
+  const uint32_t sK = smem_u32(buf), sV = sK + ATT_SUB * HD * 2;
+  const int mi = lane >> 3, ri8 = lane & 7;  // ldmatrix: this lane addresses row ri8 of block mi
+  // S = q K^T: n-tile j = positions 8j..8j+7; one x4 load gives the B fragments of two k-steps
+  float sacc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sacc[j][i] = 0.f;
+    uint32_t kb[4][2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+      ldsm_x4(sK + kv_off(8 * j + ri8, 4 * hh + mi), kb[2 * hh][0], kb[2 * hh][1], kb[2 * hh + 1][0],
+              kb[2 * hh + 1][1]);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+        mma16816(sacc[j], qa[ks][part][0], 0u, qa[ks][part][1], 0u, kb[ks][0], kb[ks][1]);
+  }
+  if (tr && lane == 0) tr[3] = globaltimer_after(sacc[3][0]);
+  // masked softmax of query head gid over the 32 positions (position 8j + 2*t4 + e)
+  const int cnt = L - c * ATT_SUB;
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sacc[j][e] = 8 * j + 2 * t4 + e < cnt ? sacc[j][e] : -INFINITY;
+      m = fmaxf(m, sacc[j][e]);
+    }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  float l = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sacc[j][e] = expf(sacc[j][e] - m);
+      l += sacc[j][e];
+    }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  // P as the A operand: k-step kk = positions 16kk..16kk+15 = n-tiles 2kk (a0) and 2kk+1 (a2)
+  uint32_t pa[2][2][2];  // [kk][hi, lo][a0, a2]
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    split_half2(sacc[2 * kk][0], sacc[2 * kk][1], pa[kk][0][0], pa[kk][1][0]);
+    split_half2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1], pa[kk][0][1], pa[kk][1][1]);
+  }
+  // O = P V: n-tile nd = dims 8nd..8nd+7; V B fragments by transposed ldmatrix, two n-tiles per x4.
+  // The K rows are dead: the record goes there.
+  float* r = rec + min(gid, GQ - 1) * (2 + HD);
+#pragma unroll
+  for (int np = 0; np < 4; ++np) {
+    float oacc[2][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t b00, b01, b10, b11;  // [n-tile 2np + x][b0, b1]
+      ldsm_x4_trans(sV + kv_off(16 * kk + 8 * (mi & 1) + ri8, 2 * np + (mi >> 1)), b00, b01, b10, b11);
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        mma16816(oacc[0], pa[kk][part][0], 0u, pa[kk][part][1], 0u, b00, b01);
+        mma16816(oacc[1], pa[kk][part][0], 0u, pa[kk][part][1], 0u, b10, b11);
+      }
+    }
+    if (gid < GQ) {
+#pragma unroll
+      for (int x = 0; x < 2; ++x)
+        *reinterpret_cast<float2*>(r + 2 + (2 * np + x) * 8 + 2 * t4) = make_float2(oacc[x][0], oacc[x][1]);
+    }
+    __syncwarp();
+  }
+  if (gid < GQ && t4 == 0) { r[0] = m; r[1] = l; }
+  __syncwarp();
+  if (tr && lane == 0) tr[4] = globaltimer();
+}
+
+// One unit with PASS_THREADS threads: segment seg of (row t, kv head g).
+__device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, AttnSmem& sm,
                           unsigned long long* trace = nullptr) {
   int ntr = 0;
   auto tstamp = [&]() {
-    if (trace && threadIdx.x == 0 && ntr < 40) trace[ntr] = globaltimer();
+    if (trace && threadIdx.x == 0 && ntr < 8) trace[ntr] = globaltimer();
     ++ntr;
   };
   tstamp();
   const RowInfo* ri = s.ri;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = ri->n, pos = ri->pos;
-  int t = 0, rem = u, nch = 1, nseg = 1;
-  for (; t < n; ++t) {
-    nch = attn_chunks(ri, t, pos);
-    nseg = attn_segs(nch, segsz);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  int t = 0, rem = u, nsub = 1, nseg = 1;
+  for (; t < ri->n; ++t) {
+    nsub = attn_subs(ri, t);
+    nseg = attn_segs(nsub);
     if (rem < NKV * nseg) break;
     rem -= NKV * nseg;
   }
   const int g = rem / nseg, seg = rem % nseg;
-  const int c0 = seg * segsz, c1 = min(nch, c0 + segsz);
-  const int L = pos + ri->depth[t] + 1;
-  const __half* kb = s.kc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
-  const __half* vb = s.vc + (size_t)(layer * NKV + g) * s.max_ctx * HD;
-  // slots of every position of the segment (virtual position -> KV slot), no memory traffic
-  for (int i = tid; i < (c1 - c0) * ATT_CHUNK; i += PASS_THREADS) {
-    const int jv = c0 * ATT_CHUNK + i;
-    sm.slots[i / ATT_CHUNK][i % ATT_CHUNK] =
-        jv < pos ? jv : pos + ri->path[t][min(max(jv - pos, 0), ROWS - 1)];
+  const int c0 = seg * ATT_SEGSUB, c1 = min(nsub, c0 + ATT_SEGSUB);
+  float* rec0 = reinterpret_cast<float*>(&sm.kv[0][0][0][0]);
+  if (c0 + warp < c1) {
+    const size_t cache = (size_t)(layer * NKV + g) * s.max_ctx * HD;
+    attn_warp(s.q + t * H, s.kc + cache, s.vc + cache, ri, t, g, c0 + warp, &sm.kv[warp][0][0][0],
+              rec0 + warp * ATT_REC_STRIDE, trace ? trace + 8 + 8 * warp : nullptr);
   }
   cons_sync();
-  // K and V rows of a chunk: 2 x 64 rows x 128 bytes = 1024 16-byte copies, two per thread, as
-  // cp.async one chunk ahead (barriers do not wait for them); rows past the sequence are zeros.
-  // evict-last keeps the KV cache resident in L2 against the streaming weights.
-  const uint64_t kvpol = policy_evict_last();
-  auto load_kv = [&](int ci, int buf) {
-    const int cnt = min(L - (c0 + ci) * ATT_CHUNK, ATT_CHUNK);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = tid + k * PASS_THREADS;
-      const int which = i / (ATT_CHUNK * 8), r = (i / 8) % ATT_CHUNK, part = i % 8;
-      const int slot = r < cnt ? sm.slots[ci][r] : 0;
-      cp_async16(&sm.kv[buf][which][r][part * 8], (which ? vb : kb) + (size_t)slot * HD + part * 8,
-                 r < cnt ? 16u : 0u, kvpol);
-    }
-    cp_async_commit();
-  };
-  load_kv(0, 0);
-  for (int i = tid; i < GQ * HD; i += PASS_THREADS)
-    sm.qs[i / HD][i % HD] = __ldcg(s.q + t * H + (g * GQ + i / HD) * HD + i % HD);
-  for (int c = c0; c < c1; ++c) {
-    const int ci = c - c0, buf = ci & 1;
-    const int j0 = c * ATT_CHUNK, cnt = min(L - j0, ATT_CHUNK);
-    if (c + 1 < c1) {
-      load_kv(ci + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    cons_sync();
-    tstamp();
-    // scores S = (q * 0.125) K^T on the tensor cores: warp w < 8 takes positions 8w..8w+7,
-    // M = heads (7 of 16 rows used), K = 64 dims, q as fp16 hi + lo (near-fp32 product)
-    if (c == c0) {
-      for (int i = tid; i < 8 * HD; i += PASS_THREADS) {
-        const int h = i / HD, d = i % HD;
-        const float v = h < GQ ? sm.qs[h][d] * ATTN_SCALE : 0.f;
-        const __half hi = __float2half_rn(v);
-        sm.qh[0][h][d] = hi;
-        sm.qh[1][h][d] = __float2half_rn(v - __half2float(hi));
-      }
-      cons_sync();
-    }
-    if (warp < 8) {
-      const int gid = lane >> 2, t4 = lane & 3;
-      float acc[2][4] = {};  // hi and lo parts of q: two independent chains, added at the end
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sm.kv[buf][0][warp * 8 + gid][ks * 16 + 2 * t4]);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sm.kv[buf][0][warp * 8 + gid][ks * 16 + 2 * t4 + 8]);
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&sm.qh[part][gid][ks * 16 + 2 * t4]);
-          const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&sm.qh[part][gid][ks * 16 + 2 * t4 + 8]);
-          mma16816(acc[part], a0, 0u, a2, 0u, b0, b1);
-        }
-      }
-      if (gid < GQ) {
-        const int p0 = warp * 8 + 2 * t4;
-        sm.sc[gid][p0] = p0 < cnt ? acc[0][0] + acc[1][0] : -INFINITY;
-        sm.sc[gid][p0 + 1] = p0 + 1 < cnt ? acc[0][1] + acc[1][1] : -INFINITY;
-      }
-    }
-    cons_sync();
-    tstamp();
-    // per-head max and exp-sum over the chunk (warp h, two positions per lane)
-    if (warp < GQ) {
-      const float v0 = sm.sc[warp][lane], v1 = sm.sc[warp][lane + 32];
-      const float m = warp_max(fmaxf(v0, v1));
-      const float e0 = lane < cnt ? expf(v0 - m) : 0.f;
-      const float e1 = lane + 32 < cnt ? expf(v1 - m) : 0.f;
-      sm.sc[warp][lane] = e0;
-      sm.sc[warp][lane + 32] = e1;
-      const float l = warp_sum(e0 + e1);
-      if (lane == 0) { sm.rec[ci][warp * (2 + HD)] = m; sm.rec[ci][warp * (2 + HD) + 1] = l; }
-    }
-    cons_sync();
-    tstamp();
-    // weighted V: O = P V on the tensor cores: warp w < 8 takes dims 8w..8w+7, M = heads,
-    // K = the chunk's 64 positions, P as fp16 hi + lo
-    if (warp < 8) {
-      const int gid = lane >> 2, t4 = lane & 3;
-      float acc2[2][4] = {};  // hi and lo parts of P: two independent chains
-      const int d = warp * 8 + gid;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-          uint32_t a[2];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int pp = ks * 16 + 2 * t4 + 8 * hh;
-            float e0 = 0.f, e1 = 0.f;
-            if (gid < GQ) { e0 = sm.sc[gid][pp]; e1 = sm.sc[gid][pp + 1]; }
-            __half h0 = __float2half_rn(e0), h1 = __float2half_rn(e1);
-            if (part) {
-              h0 = __float2half_rn(e0 - __half2float(h0));
-              h1 = __float2half_rn(e1 - __half2float(h1));
-            }
-            a[hh] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-          }
-          const int pb = ks * 16 + 2 * t4;
-          const uint32_t b0 = (uint32_t)__half_as_ushort(sm.kv[buf][1][pb][d]) |
-                              ((uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 1][d]) << 16);
-          const uint32_t b1 = (uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 8][d]) |
-                              ((uint32_t)__half_as_ushort(sm.kv[buf][1][pb + 9][d]) << 16);
-          mma16816(acc2[part], a[0], 0u, a[1], 0u, b0, b1);
-        }
-      if (gid < GQ) {
-        sm.rec[ci][gid * (2 + HD) + 2 + warp * 8 + 2 * t4] = acc2[0][0] + acc2[1][0];
-        sm.rec[ci][gid * (2 + HD) + 2 + warp * 8 + 2 * t4 + 1] = acc2[0][1] + acc2[1][1];
-      }
-    }
-    cons_sync();
-  }
   tstamp();
   if (nseg == 1) {
-    attn_combine<false>(s, &sm.rec[0][0], nch, t, g);
+    attn_combine<false>(s, rec0, ATT_REC_STRIDE, nsub, t, g);
     cons_sync();
     tstamp();
     return;
   }
-  float* base = s.att_part + (size_t)(t * NKV + g) * max_chunks * ATT_REC;
-  for (int i = tid; i < (c1 - c0) * ATT_REC; i += PASS_THREADS) base[c0 * ATT_REC + i] = (&sm.rec[0][0])[i];
+  float* base = s.att_part + (size_t)(t * NKV + g) * max_subs * ATT_REC;
+  for (int i = tid; i < (c1 - c0) * ATT_REC; i += PASS_THREADS)
+    base[(c0 + i / ATT_REC) * ATT_REC + i % ATT_REC] = rec0[(i / ATT_REC) * ATT_REC_STRIDE + i % ATT_REC];
   __threadfence();
   cons_sync();
   if (tid == 0) sm.last = atomicAdd(s.tickets + ATT_TICKETS + t * NKV + g, 1) == nseg - 1;
   cons_sync();
   if (sm.last) {
     __threadfence();
-    // all chunk records of the row into shared memory in one coalesced round trip (they fit: the
-    // K/V buffers are free now), then the combine reads shared memory only
-    if (nch <= ATT_MAX_REC_STAGED) {
-      float* recs = reinterpret_cast<float*>(&sm.kv[0][0][0][0]);
-      for (int i = tid; i < nch * ATT_REC; i += PASS_THREADS) recs[i] = __ldcg(base + i);
-      cons_sync();
-      attn_combine<false>(s, recs, nch, t, g);
-    } else {
-      attn_combine<true>(s, base, nch, t, g);  // long rows: read the records in place
-    }
+    attn_combine<true>(s, base, ATT_REC, nsub, t, g);
     if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
   }
   cons_sync();
+  tstamp();
 }
 
 }  // namespace vp

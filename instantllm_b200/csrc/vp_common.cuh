@@ -27,7 +27,7 @@ constexpr int GS = VP_GROUP;
 constexpr int HRB = H / 16;        // 56 row-blocks of a hidden-sized output
 constexpr float EPS = 1e-6f;
 constexpr float ATTN_SCALE = 0.125f;  // 64^-0.5, exact
-constexpr int ATT_CHUNK = 64;         // virtual positions per attention split (fixed: shape-invariant)
+constexpr int ATT_SUB = 32;           // virtual positions per attention record (fixed: shape-invariant)
 
 // Bytes of one packed 16x64 tile per format: codes then per-row scale data.
 __host__ __device__ constexpr int tile_bytes(int fmt) {
@@ -154,6 +154,15 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// %globaltimer read issued only once `dep` is available (for timing a dependent chain).
+__device__ __forceinline__ unsigned long long globaltimer_after(float dep) {
+  unsigned long long t;
+  asm volatile("{\n .reg .f32 z;\n add.f32 z, %1, 0f00000000;\n mov.u64 %0, %%globaltimer;\n}\n"
+               : "=l"(t)
+               : "f"(dep));
+  return t;
 }
 
 // 16-byte cp.async global -> shared (bypasses L1); src_bytes 0 fills zeros. CTA barriers do not

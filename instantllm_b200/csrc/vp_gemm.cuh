@@ -269,8 +269,12 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
       bulk_g2s(sAct, p.act + (size_t)g0 * 1024, bytes, barAct, policy_evict_last());
     }
     if (MODE != MODE_RESID && threadIdx.x < 16) {
+      float v[HRB];  // all loads in flight at once, summed in fixed order
+#pragma unroll
+      for (int r = 0; r < HRB; ++r) v[r] = __ldcg(p.ss_in + r * 16 + threadIdx.x);
       float sum = 0.f;
-      for (int r = 0; r < HRB; ++r) sum += __ldcg(p.ss_in + r * 16 + threadIdx.x);
+#pragma unroll
+      for (int r = 0; r < HRB; ++r) sum += v[r];
       sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
     }
     if (!mbar_wait_bounded(barAct, 0)) sOk = 0;

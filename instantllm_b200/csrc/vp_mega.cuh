@@ -27,14 +27,27 @@ constexpr int MK_THREADS = MK_CONS + 32;         // + the producer warp
 constexpr int MK_NSLOT = 5;                      // weight ring slots
 constexpr int MK_SLOT = 28672;                   // bytes per slot
 constexpr int MK_PART_SLOTS = 24;                // partial tiles of a stage (1 KiB each)
-constexpr int MK_TRACE = 256;                    // trace slots: start, embed, 5 per layer, lm, end
+constexpr int MK_TRACE = 2048;  // trace slots: [0, 256) stage ends of CTA 0; the rest detail stamps
 static_assert(MK_CONS == PASS_THREADS && MK_CONS == CONS_THREADS, "consumer warps run the stage code");
 
 enum MkStage { MK_QKV = 0, MK_O = 1, MK_GU = 2, MK_DOWN = 3, MK_LM = 4 };
 
-// Parts per row-block (K split across warps of one CTA) and K groups of each GEMM stage.
-__host__ __device__ constexpr int mk_parts(int st) {
-  return st == MK_QKV ? 14 : st == MK_O ? 14 : st == MK_GU ? 3 : st == MK_DOWN ? 16 : 1;
+// Detail timeline for performance work (compiled in only with -DVP_TRACE_DETAIL): CTA 0 stamps the
+// steps of each GEMM stage of layer 5 and of the lm_head stage at trace[256 + 8 * stage + step],
+// and every CTA stamps its grid-barrier arrivals of layer 5 at trace[512 + 148 * k + cta].
+#ifdef VP_TRACE_DETAIL
+#define MK_DSTAMP(p, cond, idx) \
+  do { if ((p).trace && blockIdx.x == 0 && threadIdx.x == 0 && (cond)) (p).trace[(idx)] = globaltimer(); } while (0)
+#else
+#define MK_DSTAMP(p, cond, idx) do {} while (0)
+#endif
+
+// Parts per row-block (K split across the warps of one CTA) of a GEMM stage whose CTA owns nrb
+// row-blocks, and K groups of each GEMM stage. Gate/up fills the 16 warps once: 4 row-blocks x 4
+// parts or 5 x 3.
+__host__ __device__ constexpr int mk_parts(int st, int nrb) {
+  return st == MK_QKV ? 14 : st == MK_O ? 14 : st == MK_DOWN ? 16
+       : st == MK_GU ? (nrb >= 16 ? 1 : nrb <= 1 ? 14 : 16 / nrb) : 1;
 }
 __host__ __device__ constexpr int mk_groups(int st) { return st == MK_DOWN ? F / GS : H / GS; }
 __host__ __device__ constexpr int mk_chunk_groups(int fmt) {
@@ -42,10 +55,10 @@ __host__ __device__ constexpr int mk_chunk_groups(int fmt) {
 }
 __host__ __device__ constexpr int mk_tiles_per_slot(int fmt) { return MK_SLOT / tile_bytes(fmt); }
 
-// Contiguous row-block range [rb0, rb0 + n) of GEMM stage `st` owned by CTA `cta` of G. Balanced
-// so that every CTA streams about the same weight bytes per layer (q4: ~57 KB): O and down go to
-// CTAs 0..55 (which also keep their slice of x), QKV to the last 72 CTAs, gate/up mostly to the
-// CTAs without O / down, the lm_head in equal contiguous shares.
+// Contiguous row-block range [rb0, rb0 + n) of GEMM stage `st` owned by CTA `cta` of G. O and down
+// go to CTAs 0..55 (which also keep their slice of x), QKV to the last 72 CTAs, gate/up and the
+// lm_head in equal contiguous shares over every CTA. Weights stream ahead of the stages that use
+// them, so the split balances each stage's work rather than each CTA's bytes.
 __host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
   rb0 = 0;
   n = 0;
@@ -55,15 +68,13 @@ __host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int
   } else if (st == MK_QKV) {
     if (cta >= G - nq) { rb0 = cta - (G - nq); n = 1; }
   } else if (st == MK_GU) {
-    if (cta < nh) { rb0 = cta; n = 1; }
-    else {
-      const int rest = ngu - nh, m = G - nh, c = cta - nh;
-      rb0 = nh + (int)((long long)c * rest / m);
-      n = nh + (int)((long long)(c + 1) * rest / m) - rb0;
+    {
+      rb0 = cta * ngu / G;  // < 2^31: 148 x 608
+      n = (cta + 1) * ngu / G - rb0;
     }
   } else {
-    rb0 = (int)((long long)cta * nrb_lm / G);
-    n = (int)((long long)(cta + 1) * nrb_lm / G) - rb0;
+    rb0 = cta * nrb_lm / G;  // < 2^31 for every vocab the context accepts
+    n = (cta + 1) * nrb_lm / G - rb0;
   }
 }
 
@@ -86,7 +97,7 @@ struct MegaParams {
   const float* ln2[VP_MAX_LAYERS];
   int n_layers;
   int nrb_lm;                 // vocab / 16
-  int max_chunks;             // attention partial records per (row, kv head)
+  int max_chunks;             // attention records (32-position sub-chunks) per (row, kv head)
   unsigned long long* bar;    // grid barrier arrival counter (0 at launch, reset by the last CTA)
   unsigned* exit_ctr;         // CTAs that finished this launch
   unsigned long long* trace;  // CTA 0: %globaltimer after each stage (MK_TRACE entries)
@@ -151,15 +162,19 @@ constexpr size_t MK_ACT_BYTES = (size_t)(H / GS) * 2048;  // act blocks of a K =
 constexpr size_t MK_OFF_ACT = MK_RING_BYTES;
 constexpr size_t MK_OFF_X = MK_OFF_ACT + MK_ACT_BYTES;            // 16 x 16 group sums
 constexpr size_t MK_OFF_PART = MK_OFF_X + 16 * 16 * 4;            // partial tiles
-constexpr size_t MK_OFF_RS = MK_OFF_PART + MK_PART_SLOTS * 1024;  // rscale[16]
+// attention scratch overlays the act blocks, group sums and partial tiles (and extends past them)
+constexpr size_t MK_OVERLAY = sizeof(AttnSmem) > MK_ACT_BYTES + 16 * 16 * 4 + MK_PART_SLOTS * 1024
+                                  ? ((sizeof(AttnSmem) + 127) & ~size_t(127))
+                                  : MK_ACT_BYTES + 16 * 16 * 4 + MK_PART_SLOTS * 1024;
+constexpr size_t MK_OFF_RS = MK_OFF_ACT + MK_OVERLAY;              // rscale[16]
 constexpr size_t MK_OFF_LMV = MK_OFF_RS + 64;                     // [16 warps][16] best value
 constexpr size_t MK_OFF_LMI = MK_OFF_LMV + 1024;                  // [16 warps][16] best id
 constexpr size_t MK_OFF_RI = MK_OFF_LMI + 1024;                   // RowInfo copy
 constexpr size_t MK_OFF_XRB = MK_OFF_RI + ((sizeof(RowInfo) + 15) & ~size_t(15));  // owned x slice
 constexpr size_t MK_OFF_BAR = (MK_OFF_XRB + 16 * 16 * 4 + 127) & ~size_t(127);
 constexpr size_t MK_SMEM = MK_OFF_BAR + 8 * (2 * MK_NSLOT);
-static_assert(sizeof(AttnSmem) <= MK_OFF_RS - MK_OFF_ACT,
-              "attention scratch overlays the act blocks, group sums and partial tiles");
+static_assert(sizeof(AttnSmem) <= MK_OFF_RS - MK_OFF_ACT, "attention scratch fits its overlay");
+static_assert(MK_SMEM <= 232448, "dynamic shared memory of the pass kernel fits one sm_100 CTA");
 
 // Consumer view of the weight ring: pieces are numbered over the whole pass in consumption order.
 struct MkRing {
@@ -230,19 +245,12 @@ __device__ __forceinline__ uint4 act_frag_smem(const uint8_t* sAct, int g, int j
 // acc += NT consecutive tiles (groups g .. g+NT-1 of the row-block) times their activations. The
 // tiles' MMA chains are independent (instruction-level parallelism); their folds into acc run in
 // group order, so the result equals NT single-tile steps.
+// GLOBAL_B: the activations come from global memory (down projection: K = 4864 does not fit in
+// shared memory) and the group sums are formed from the fragments; otherwise both are in smem.
 template <int FMT, bool GLOBAL_B, int NT>
-__device__ __forceinline__ void mk_tiles(const uint8_t* const (&tile)[NT], int g, const uint8_t* sAct,
-                                         const float* sX, const __half* actg, int lane,
-                                         float (&acc)[2][4]) {
+__device__ __forceinline__ void mk_tiles_bf(const uint8_t* const (&tile)[NT], int g, const uint4 (&bf)[NT][4],
+                                            const float* sX, int lane, float (&acc)[2][4]) {
   const int gid = lane >> 2, tid4 = lane & 3;
-  uint4 bf[NT][4];
-#pragma unroll
-  for (int u = 0; u < NT; ++u)
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      bf[u][j] = GLOBAL_B
-          ? __ldcg(reinterpret_cast<const uint4*>(actg + (size_t)(g + u) * 1024 + j * 256 + lane * 8))
-          : act_frag_smem(sAct, g + u, j, lane);
   if constexpr (FMT == VP_FMT_F16) {
 #pragma unroll
     for (int u = 0; u < NT; ++u)
@@ -303,6 +311,25 @@ __device__ __forceinline__ void mk_tiles(const uint8_t* const (&tile)[NT], int g
   }
 }
 
+template <int FMT, int NT>
+__device__ __forceinline__ void mk_tiles(const uint8_t* const (&tile)[NT], int g, const uint8_t* sAct,
+                                         const float* sX, int lane, float (&acc)[2][4]) {
+  uint4 bf[NT][4];
+#pragma unroll
+  for (int u = 0; u < NT; ++u)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bf[u][j] = act_frag_smem(sAct, g + u, j, lane);
+  mk_tiles_bf<FMT, false, NT>(tile, g, bf, sX, lane, acc);
+}
+static_assert(mk_parts(MK_DOWN, 1) * 1024 + (MK_WARPS - H / GS) * 2048 <= MK_PART_SLOTS * 1024,
+              "down-projection staging buffers of warps 14 and 15 sit past the 16 partial tiles");
+// Down projection: per-warp 2 KiB staging buffer of one act block. The act blocks area is free
+// in that stage (14 buffers); warps 14 and 15 use the partial-tile area past the 16 partials.
+__device__ __forceinline__ uint8_t* mk_down_stage(uint8_t* sAct, float* sPart, int warp) {
+  return warp < H / GS ? sAct + (size_t)warp * 2048
+                       : reinterpret_cast<uint8_t*>(sPart) + (size_t)(16 + 2 * (warp - H / GS)) * 1024;
+}
+
 // Wait until piece k is in the ring (bounded); returns its slot base or null on timeout.
 __device__ __forceinline__ const uint8_t* mk_piece(MkRing& rg, int k) {
   while (rg.waited <= k) {
@@ -328,82 +355,85 @@ __device__ __forceinline__ bool mk_release(MkRing& rg, int k, int lane) {
   return true;
 }
 
-// One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
-// Returns false if a wait timed out.
-template <int FMT, int MODE>
-__device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
-                        uint8_t* smem, volatile int* sAbort, float (&lmV)[2][2], int (&lmI)[2][2]) {
+// The job loop of a GEMM stage for one warp. Writes the partial tile of each job to the
+// partial-tile area, or (lm_head, one part) folds it into this warp's running argmax in shared
+// memory.
+struct MkJobs {
+  int piece0, rb0, nrb, P, ng;
+  int down;              // activations from global memory (down projection)
+  const __half* actg;    // down projection: act blocks of the SiLU output
+};
+
+// The ring state travels by value (registers) and comes back updated: x = pieces released (or -1
+// after a timeout), y = pieces seen full.
+template <int FMT>
+__device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid4 = lane & 3;
   uint8_t* sAct = smem + MK_OFF_ACT;
   float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
   float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
-  float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
-  const int G = gridDim.x, cta = blockIdx.x;
-  int rb0, nrb;
-  mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
-  if (nrb == 0) return true;
-  const int P = mk_parts(st), ng = mk_groups(st);
+  const float* sRs = reinterpret_cast<const float*>(smem + MK_OFF_RS);
+  float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
+  int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
+  const int piece0 = J.piece0, rb0 = J.rb0, nrb = J.nrb, P = J.P, ng = J.ng;
+  const bool down = J.down != 0;
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
-  const bool down = st == MK_DOWN;
-  // RMSNorm scale of the input rows and the act blocks (K = 896 stages) in one round trip
-  if (MODE != MODE_RESID && threadIdx.x < 16) {
-    float sum = 0.f;
-    for (int r = 0; r < HRB; ++r) sum += __ldcg(gp.ss_in + r * 16 + threadIdx.x);
-    sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
-  }
-  if (!down) {
-    const uint4* src = reinterpret_cast<const uint4*>(gp.act);
-    uint4* dst = reinterpret_cast<uint4*>(sAct);
-    for (int i = threadIdx.x; i < (int)(MK_ACT_BYTES / 16); i += MK_CONS) dst[i] = __ldcg(src + i);
-  }
-  mk_sync();
-  if (!down && FMT != VP_FMT_F16 && warp < H / GS) {
-    const uint32_t ONE2 = 0x3C003C00u;
-    float xs[2][4] = {};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 b = act_frag_smem(sAct, warp, j, lane);
-      mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
-      mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
-    }
-    if (gid == 0) {
-      sX[warp * 16 + 2 * tid4] = xs[0][0];
-      sX[warp * 16 + 2 * tid4 + 1] = xs[0][1];
-      sX[warp * 16 + 8 + 2 * tid4] = xs[1][0];
-      sX[warp * 16 + 8 + 2 * tid4 + 1] = xs[1][1];
-    }
-  }
-  mk_sync();
-
   // jobs (row-block i, part q) -> warp (i * P + q) % 16, in increasing tile order per warp
   const int jobs = nrb * P;
-  const int npieces = (nrb * ng + tp - 1) / tp;
   bool ok = true;
   for (int j = warp; j < jobs && ok; j += MK_WARPS) {
     const int i = j / P, q = j % P;
     const int ga = q * ng / P, gb = (q + 1) * ng / P;
     float acc[2][4] = {};
-    for (int g = ga; g < gb; g += 2) {
-      // tiles g and g+1 (if in the part): release the pieces before g's, wait for both
-      const int idx = i * ng + g;
-      const int k = piece0 + idx / tp;
-      if (!mk_release(rg, k, lane)) { ok = false; break; }
-      const uint8_t* base = mk_piece(rg, k);
-      if (!base) { ok = false; break; }
-      const uint8_t* t0 = base + (size_t)(idx % tp) * TB;
-      if (g + 1 < gb) {
-        const int k1 = piece0 + (idx + 1) / tp;
-        const uint8_t* base1 = mk_piece(rg, k1);
-        if (!base1) { ok = false; break; }
-        const uint8_t* const tt[2] = {t0, base1 + (size_t)((idx + 1) % tp) * TB};
-        if (down) mk_tiles<FMT, true, 2>(tt, g, sAct, sX, gp.act, lane, acc);
-        else mk_tiles<FMT, false, 2>(tt, g, sAct, sX, gp.act, lane, acc);
-      } else {
-        const uint8_t* const tt[1] = {t0};
-        if (down) mk_tiles<FMT, true, 1>(tt, g, sAct, sX, gp.act, lane, acc);
-        else mk_tiles<FMT, false, 1>(tt, g, sAct, sX, gp.act, lane, acc);
+    if (down) {
+      // one tile per step, software-pipelined: the act block of tile g + 1 streams from L2 into
+      // this warp's 2 KiB staging buffer (cp.async, each lane its own fragments) while tile g
+      // computes; the first copy overlaps the wait for the weights
+      uint8_t* sB = mk_down_stage(sAct, sPart, warp);
+      const uint64_t pol = policy_evict_last();
+      auto fetch = [&](int g) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          cp_async16(sB + j * 512 + lane * 16, J.actg + (size_t)g * 1024 + j * 256 + lane * 8, 16u, pol);
+        cp_async_commit();
+      };
+      if (ga < gb) fetch(ga);
+      for (int g = ga; g < gb; ++g) {
+        const int idx = i * ng + g;
+        const int k = piece0 + idx / tp;
+        if (!mk_release(rg, k, lane)) { ok = false; break; }
+        const uint8_t* base = mk_piece(rg, k);
+        if (!base) { ok = false; break; }
+        cp_async_wait<0>();
+        uint4 bf[1][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bf[0][j] = *reinterpret_cast<const uint4*>(sB + j * 512 + lane * 16);
+        if (g + 1 < gb) fetch(g + 1);
+        const uint8_t* const tt[1] = {base + (size_t)(idx % tp) * TB};
+        mk_tiles_bf<FMT, true, 1>(tt, g, bf, sX, lane, acc);
+      }
+      cp_async_wait<0>();
+    } else {
+      for (int g = ga; g < gb; g += 2) {
+        // tiles g and g+1 (if in the part): release the pieces before g's, wait for both
+        const int idx = i * ng + g;
+        const int k = piece0 + idx / tp;
+        if (!mk_release(rg, k, lane)) { ok = false; break; }
+        const uint8_t* base = mk_piece(rg, k);
+        if (!base) { ok = false; break; }
+        const uint8_t* t0 = base + (size_t)(idx % tp) * TB;
+        if (g + 1 < gb) {
+          const int k1 = piece0 + (idx + 1) / tp;
+          const uint8_t* base1 = mk_piece(rg, k1);
+          if (!base1) { ok = false; break; }
+          const uint8_t* const tt[2] = {t0, base1 + (size_t)((idx + 1) % tp) * TB};
+          mk_tiles<FMT, 2>(tt, g, sAct, sX, lane, acc);
+        } else {
+          const uint8_t* const tt[1] = {t0};
+          mk_tiles<FMT, 1>(tt, g, sAct, sX, lane, acc);
+        }
       }
     }
     if (!ok) break;
@@ -426,7 +456,11 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
           }
-          if (bv > lmV[nt][e] || (bv == lmV[nt][e] && bi < lmI[nt][e])) { lmV[nt][e] = bv; lmI[nt][e] = bi; }
+          if (gid == 0) {  // this warp's running best of token t (shared memory, warp-private)
+            float& mv = sLmV[warp * 16 + t];
+            int& mi = sLmI[warp * 16 + t];
+            if (bv > mv || (bv == mv && bi < mi)) { mv = bv; mi = bi; }
+          }
         }
     } else {
       float* part = sPart + j * 256;
@@ -437,6 +471,80 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
           part[(gid + 8 * (r >> 1)) * 16 + nt * 8 + 2 * tid4 + (r & 1)] = acc[nt][r];
     }
   }
+  return make_int2(ok ? rg.released : -1, rg.waited);
+}
+
+// One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
+// Returns false if a wait timed out.
+template <int FMT, int MODE>
+__device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
+                        uint8_t* smem, volatile int* sAbort) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tid4 = lane & 3;
+  uint8_t* sAct = smem + MK_OFF_ACT;
+  float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
+  float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
+  float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
+  const int G = gridDim.x, cta = blockIdx.x;
+  int rb0, nrb;
+  mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+  if (nrb == 0) return true;
+  const int P = mk_parts(st, nrb), ng = mk_groups(st);
+  const int tp = mk_tiles_per_slot(FMT);
+  constexpr int TB = tile_bytes(FMT);
+  const bool down = st == MK_DOWN;
+#ifdef VP_TRACE_DETAIL
+  const bool dtr = gp.layer == 5 || MODE == MODE_ARGMAX;
+#endif
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 0);
+  // the act blocks (K = 896 stages) and the RMSNorm scale of the input rows in one round trip: the
+  // act copies are in flight while the partial sums load (all 56 at once, summed in fixed order)
+  // (the partials land in the partial-tile area, which is free until the jobs start)
+  float* sSs = sPart;
+  {
+    const uint64_t pol = policy_evict_last();
+    if (!down)
+      for (int i = threadIdx.x; i < (int)(MK_ACT_BYTES / 16); i += MK_CONS)
+        cp_async16(sAct + (size_t)i * 16, reinterpret_cast<const uint4*>(gp.act) + i, 16u, pol);
+    if (MODE != MODE_RESID && threadIdx.x < HRB * 16 / 4)
+      cp_async16(sSs + threadIdx.x * 4, gp.ss_in + threadIdx.x * 4, 16u, pol);
+    cp_async_commit();
+    cp_async_wait<0>();
+  }
+  mk_sync();
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 1);
+  if (MODE != MODE_RESID && warp == MK_WARPS - 1 && lane < 16) {
+    float sum = 0.f;
+    for (int r = 0; r < HRB; ++r) sum += sSs[r * 16 + lane];
+    sRs[lane] = 1.f / sqrtf(sum / (float)H + EPS);
+  }
+  if (!down && FMT != VP_FMT_F16 && warp < H / GS) {
+    const uint32_t ONE2 = 0x3C003C00u;
+    float xs[2][4] = {};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 b = act_frag_smem(sAct, warp, j, lane);
+      mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
+      mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
+    }
+    if (gid == 0) {
+      sX[warp * 16 + 2 * tid4] = xs[0][0];
+      sX[warp * 16 + 2 * tid4 + 1] = xs[0][1];
+      sX[warp * 16 + 8 + 2 * tid4] = xs[1][0];
+      sX[warp * 16 + 8 + 2 * tid4 + 1] = xs[1][1];
+    }
+  }
+  mk_sync();
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 2);
+
+  const int npieces = (nrb * ng + tp - 1) / tp;
+  MkJobs J;
+  J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.down = down ? 1 : 0; J.actg = gp.act;
+  const int2 rs2 = mk_jobs<FMT>(J, rg, smem);
+  bool ok = rs2.x >= 0;
+  if (ok) rg.released = rs2.x;
+  rg.waited = rs2.y;
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 3);
   // this warp is done with every piece of the stage
   if (ok) ok = mk_release(rg, piece0 + npieces, lane);
   if (!ok) {
@@ -444,6 +552,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
     *sAbort = 1;
   }
   mk_sync();
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
   if (P > 1) {
     for (int i = warp; i < nrb; i += MK_WARPS) {
@@ -459,6 +568,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
       gemm_epilogue<MODE>(gp, rb0 + i, sum, sRs, lane);
     }
   }
+  MK_DSTAMP(p, dtr, 256 + 8 * st + 5);
   return true;
 }
 
@@ -495,6 +605,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
     };
     stamp();
     auto barrier = [&]() -> bool {
+#ifdef VP_TRACE_DETAIL
+      if (p.trace && threadIdx.x == 0) {
+        const int k = nstamp >= 27 && nstamp < 32 ? nstamp - 27 : nstamp == 2 + 5 * p.n_layers ? 5 : -1;
+        if (k >= 0 && G <= 148) p.trace[512 + 148 * k + cta] = globaltimer();
+      }
+#endif
       target += (unsigned long long)G;
       const bool r = grid_barrier(p, target, &sAbort);
       stamp();
@@ -541,12 +657,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
       mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
       return mk_pieces(FMT, st, nrb);
     };
-    float lmV[2][2];
-    int lmI[2][2];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < 2; ++b) { lmV[a][b] = -INFINITY; lmI[a][b] = 0x7fffffff; }
 
     if (live) {
       for (int l = 0; l < p.n_layers && ok; ++l) {
@@ -556,16 +666,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         // QKV (+ RMSNorm scale, bias, RoPE, KV write)
         gp.w = p.wqkv[l]; gp.act = s.act_h; gp.nrb = QKV / 16; gp.ng = H / GS;
         gp.bias = p.bqkv[l]; gp.ss_in = s.ss;
-        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_QKV);
         if (!ok) break;
         // attention
         {
-          const int segsz = attn_segsize(sRi, G);
-          const int units = attn_units(sRi, segsz);
+          const int units = attn_units(sRi);
           for (int u = cta; u < units; u += G)
-            attn_unit(s, l, p.max_chunks, u, segsz, sAtt,
-                      (p.trace && cta == 0 && l == 5 && u == 0) ? p.trace + 200 : nullptr);
+            attn_unit(s, l, p.max_chunks, u, sAtt,
+#ifdef VP_TRACE_DETAIL
+                      (p.trace && cta == 0 && l == 5 && u == 0) ? p.trace + 300 : nullptr);
+#else
+                      nullptr);
+#endif
         }
         ok = barrier();
         if (!ok) break;
@@ -575,7 +688,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.w = p.wo[l]; gp.act = s.act_a; gp.nrb = H / 16; gp.ng = H / GS;
         gp.wnext = p.ln2[l]; gp.ss_out = s.ss; gp.act_out = s.act_h;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_O);
         if (!ok) break;
         // gate/up + SiLU
@@ -583,7 +696,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.s = s; gp.layer = l;
         gp.w = p.wgu[l]; gp.act = s.act_h; gp.nrb = 2 * F / 16; gp.ng = H / GS;
         gp.ss_in = s.ss; gp.act_out = s.act_f;
-        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_GU);
         if (!ok) break;
         // down + residual
@@ -593,27 +706,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.wnext = l + 1 < p.n_layers ? p.ln1[l + 1] : p.final_norm;
         gp.ss_out = s.ss; gp.act_out = s.act_h;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, lmV, lmI) && barrier();
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_DOWN);
       }
       if (ok && p.do_lm) {
         GemmParams gp = {};
         gp.s = s;
         gp.w = p.embed; gp.act = s.act_h; gp.nrb = p.nrb_lm; gp.ng = H / GS; gp.ss_in = s.ss;
-        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort, lmV, lmI);
-        // per-CTA best per token: lanes with gid == 0 hold tokens nt*8 + 2*tid4 + e
+        if (lane < 16) {  // every warp's running best starts empty
+          reinterpret_cast<float*>(smem + MK_OFF_LMV)[warp * 16 + lane] = -INFINITY;
+          reinterpret_cast<int*>(smem + MK_OFF_LMI)[warp * 16 + lane] = 0x7fffffff;
+        }
+        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort);
+        // per-CTA best per token from the warps' running bests
         float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
         int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
-        if ((lane >> 2) == 0) {
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int t = nt * 8 + 2 * (lane & 3) + e;
-              sLmV[warp * 16 + t] = lmV[nt][e];
-              sLmI[warp * 16 + t] = lmI[nt][e];
-            }
-        }
         mk_sync();
         if (threadIdx.x < 16) {
           const int t = threadIdx.x;

@@ -211,6 +211,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
     return fail(VP_ERR_ARG, "format must be q4, q8 or f16");
   if (cfg->n_layers < 1 || cfg->n_layers > VP_MAX_LAYERS) return fail(VP_ERR_ARG, "n_layers out of range");
   if (cfg->vocab < 16 || cfg->vocab % 16) return fail(VP_ERR_ARG, "vocab must be a positive multiple of 16");
+  if (cfg->vocab > (1 << 24)) return fail(VP_ERR_ARG, "vocab above 2^24");
   if (cfg->max_ctx < ROWS || cfg->max_ctx > (1 << 20)) return fail(VP_ERR_ARG, "max_ctx out of range");
   if (cfg->max_steps < 1 || cfg->max_steps > (1 << 24)) return fail(VP_ERR_ARG, "max_steps out of range");
   VP_CUDA(cudaSetDevice(cfg->device));
@@ -223,7 +224,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
     for (int cta = 0; cta < sms; ++cta) {
       int rb0, n;
       mk_range(st, cta, sms, cfg->vocab / 16, rb0, n);
-      if (n * mk_parts(st) > MK_PART_SLOTS)
+      if (n * mk_parts(st, n) > MK_PART_SLOTS)
         return fail(VP_ERR_DEVICE, "too few SMs for the pass kernel's work split");
     }
   vp_ctx* c = new vp_ctx();
@@ -231,7 +232,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   const int fmt = cfg->format;
   c->lm = make_stage(fmt, cfg->vocab, H, 1);
   c->lm.cps = 296 < (c->lm.nrb + 3) / 4 ? 296 : (c->lm.nrb + 3) / 4;
-  c->max_chunks = (cfg->max_ctx + ATT_CHUNK - 1) / ATT_CHUNK + 1;
+  c->max_chunks = (cfg->max_ctx + ATT_SUB - 1) / ATT_SUB + 1;
   c->grid = sms;
 
   Scratch& s = c->s;
