@@ -58,6 +58,21 @@ def dist_env():
     return rank, world, local
 
 
+PROFILE = ROOT / "profiles" / "k_pass_q4_config2.md"
+
+
+def ncu_traffic():
+    """DRAM bytes (read + write) of one k_pass launch of this workload from the committed ncu
+    summary (line 'dram_bytes_per_launch: N'), or None."""
+    import re
+
+    if PROFILE.exists():
+        m = re.search(r"dram_bytes_per_launch:\s*(\d+)", PROFILE.read_text())
+        if m:
+            return int(m.group(1))
+    return None
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -67,49 +82,70 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 5 ms through NVML in a background
+    thread; stop() keeps the samples taken inside the timed region (mark_start .. stop)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu: int):
+        import threading
+
         self.gpu = gpu
-        self.proc = None
+        self.samples = []  # (t, sm_mhz, reasons bitmask)
+        self.t0 = None
+        self.err = None
+        self.max_mhz = None
+        self.run = threading.Event()
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+
+    def _loop(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            while self.run.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except AttributeError:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((time.perf_counter(), float(sm), int(rs)))
+                time.sleep(0.005)
+            nv.nvmlShutdown()
+        except Exception as e:  # no NVML: report it instead of clocks
+            self.err = f"{type(e).__name__}: {e}"
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        self.run.set()
+        self.thread.start()
+        for _ in range(400):  # sampling is running before the timed region starts
+            if self.samples or self.err:
+                break
+            time.sleep(0.005)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        t1 = time.perf_counter()
+        self.run.clear()
+        self.thread.join(timeout=5)
+        if self.err:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"NVML unavailable ({self.err})"],
+                    "samples": 0}
+        inside = [x for x in self.samples if self.t0 is None or self.t0 <= x[0] <= t1]
+        if not inside and self.samples:  # region shorter than one sampling period
+            inside = [min(self.samples, key=lambda x: abs(x[0] - t1))]
+        mask = 0
+        for x in inside:
+            mask |= x[2]
+        return {"sm_mhz": float(np.median([x[1] for x in inside])) if inside else None,
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(k for k, v in self.REASONS.items() if mask & v),
+                "samples": len(inside)}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -178,6 +214,7 @@ def run_ours(args, rank, world, local):
     clocks.start()
     s = eng.stream
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
     e0.record(s)
     for i in range(args.warmup, n_steps):
         eng.pass_device(trees_dev[i])
@@ -360,7 +397,7 @@ def main():
             "hbm_gbs": achieved,
             "tree_equals_sequential": bool(ok),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None,
+                         "frac": achieved / hbm_peak, "traffic": ncu_traffic(),
                          "kernel": "k_pass: the persistent verify-pass kernel (one launch per pass), rank 0",
                          "bytes_per_launch": alg, "peak_kind": peak_kind},
             "e2e": {"value": e2e_tok / e2e_s, "unit": "tok/s",

@@ -158,7 +158,7 @@ int vp_verify_chain(vp_ctx* ctx, const int32_t* drafts, int32_t nd, void* stream
  * KV compaction of the accepted rows. */
 int vp_commit(vp_ctx* ctx, void* stream);
 
-/* ---- whole pass: verify + commit replayed from one CUDA graph (the pass encoder) ---- */
+/* ---- whole pass: verify + commit as one persistent-kernel launch (the pass encoder) ---- */
 int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
 
 /* ---- results ---- */

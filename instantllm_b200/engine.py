@@ -6,7 +6,7 @@ surface (Sources/Engine/Engine.swift) on top of the C ABI (include/vpass.h).
     encodePrefill          (:588-601)   -> prefill(tokens)
     encodeWidePass         (:567-579)   -> verify(tree) / verify_chain(drafts)
     encodeCommitSpec       (:484-497)   -> commit()
-    wide pass + commit as one unit      -> pass_(tree)    (CUDA graph replay)
+    wide pass + commit as one unit      -> pass_(tree)    (one persistent-kernel launch)
     generate()             (:922-1038)  -> generate(prompt, max_new, tree_fn)
 
 PyTorch only provides device memory and the stream; all compute is the CUDA library.
@@ -196,10 +196,11 @@ class VerifyEngine:
 
     # ---- generate (Engine.generate, Engine.swift:922-1038) ----
     def generate(self, prompt, max_new: int, tree_fn: Optional[Callable] = None, eos=STOP_IDS,
-                 use_graph: bool = True) -> dict:
+                 fused: bool = True) -> dict:
         """Prefill `prompt`, then verify passes until max_new tokens or a stop token. tree_fn(out)
         returns the next pass's tree given the tokens committed so far (None: 1-row passes, i.e.
-        plain greedy decoding through the same kernels, the reference's noDraft run)."""
+        plain greedy decoding through the same kernels, the reference's noDraft run). fused=False
+        runs each pass as verify + a separate commit launch instead of one pass launch."""
         from .synth import root_tree
 
         self.begin(0, max_new, eos)
@@ -209,7 +210,7 @@ class VerifyEngine:
         while not st["done"]:
             out = self.tokens(st["step"])
             tree = tree_fn(out) if tree_fn else root_tree()
-            if use_graph:
+            if fused:
                 self.pass_(tree)
             else:
                 self.verify(tree)

@@ -168,14 +168,14 @@ def test_tree_equals_sequential_200_prompts(full_q4):
     assert passes_tree < 0.7 * passes_seq
 
 
-def test_graph_pass_equals_separate_launches(full_q4):
-    """vp_pass (graph replay of verify + commit) and vp_verify + vp_commit give the same tokens."""
+def test_fused_pass_equals_separate_launches(full_q4):
+    """vp_pass (verify + commit in one launch) and vp_verify + vp_commit give the same tokens."""
     w, eng = full_q4
     prompt = synth.make_prompt(40, seed=77).tolist()
     seq = eng.generate(prompt, 20)
     a = eng.generate(prompt, 20, tree_fn=_tree_fn(seq["tokens"], np.random.default_rng(1)))
     b = eng.generate(prompt, 20, tree_fn=_tree_fn(seq["tokens"], np.random.default_rng(1)),
-                     use_graph=False)
+                     fused=False)
     assert a["tokens"] == b["tokens"] == seq["tokens"]
     assert a["passes"] == b["passes"]
 
