@@ -163,6 +163,11 @@ int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
 
 /* ---- results ---- */
 int vp_read_state(vp_ctx* ctx, vp_state* host, void* stream);       /* syncs `stream` */
+/* The host fills State (Engine.swift:937-964 writes the shared State buffer before a pass):
+ * copies `state` (host memory, or device memory when from_device != 0) into the context's device
+ * state, stream-ordered. Writing back a snapshot taken after a prefill replays later passes over
+ * the same cached prefix: passes only write KV slots at or above the state's pos. */
+int vp_write_state(vp_ctx* ctx, const vp_state* state, int32_t from_device, void* stream);
 int vp_read_tokens(vp_ctx* ctx, int32_t* host, int32_t count, void* stream); /* syncs `stream` */
 int32_t* vp_device_tokens(vp_ctx* ctx);   /* out_tokens, int32[max_steps], -1 = not yet written */
 vp_state* vp_device_state(vp_ctx* ctx);

@@ -133,6 +133,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Warp-uniform bounded wait: every lane probes the phase (each try_wait acquires for its own
+// lane) and the warp leaves on a vote, so all 32 lanes leave together and the tensor-core
+// instructions that follow (mma.sync.aligned) run converged. Returns the same value in every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if ((i & 63) == 63 && __any_sync(0xffffffffu, globaltimer() - t0 > WAIT_NS)) return false;
+  }
+  return false;
+}
+
 // One bulk copy global -> this CTA's shared memory, completing on `bar` (16-byte aligned, size a
 // multiple of 16). Streaming weights are read once per pass: evict-first keeps them from pushing
 // the activations and KV cache out of L2.
@@ -197,7 +210,18 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // producer warp that never takes part in the compute stages, so stage code never uses
 // __syncthreads.
 constexpr int CONS_THREADS = 512;
-__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+// barrier.sync without .aligned: lanes of a warp may arrive from divergent code (a conditional
+// store just before the barrier), which the .aligned form (bar.sync) leaves undefined; the
+// __syncwarp reconverges the warp first.
+__device__ __forceinline__ void cons_sync() {
+  __syncwarp();
+  asm volatile("barrier.sync 1, 512;" ::: "memory");
+}
+// Whole-CTA barrier after possibly divergent code (same reasoning as cons_sync).
+__device__ __forceinline__ void cta_sync() {
+  __syncwarp();
+  __syncthreads();
+}
 
 __device__ __forceinline__ void set_error(vp_state* st, int bits) {
   atomicOr(&st->err, bits);

@@ -233,7 +233,7 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
     fence_barrier_init();
     sOk = 1;
   }
-  __syncthreads();
+  cta_sync();
 
   // This warp's row-blocks: cin*4 + warp, then strided by all warps of the split.
   const int rb_first = cin * GEMM_WARPS + warp, rb_stride = p.cps * GEMM_WARPS;
@@ -277,10 +277,12 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
       for (int r = 0; r < HRB; ++r) sum += v[r];
       sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
     }
-    if (!mbar_wait_bounded(barAct, 0)) sOk = 0;
+    // every warp waits (warp-uniform) for the act blocks; a timeout is recorded, not acted on per lane
+    const bool act_ok = mbar_wait_warp(barAct, 0);
+    if (!act_ok && lane == 0) sOk = 0;
     // Group sums X[g][t] = sum of the group's 64 fp16 inputs of token t (exact products, fp32
     // accumulation) via a ones-matrix MMA.
-    if (FMT != VP_FMT_F16 && mbar_try_wait(barAct, 0)) {
+    if (FMT != VP_FMT_F16 && act_ok) {
       const uint32_t ONE2 = 0x3C003C00u;
       for (int g = warp; g < g1 - g0; g += GEMM_WARPS) {
         float xs[2][4] = {};
@@ -300,7 +302,7 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
       }
     }
   }
-  __syncthreads();
+  cta_sync();
   bool ok = live && sOk != 0;
   if (live && !ok && threadIdx.x == 0) set_error(p.s.st, VP_DEV_ERR_TIMEOUT);
 
@@ -308,7 +310,7 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
   int n_waited = 0;
   for (int ci = 0; ok && ci < total_chunks; ++ci) {
     const int slot = ci % GEMM_NST;
-    if (!mbar_wait_bounded(myBars + slot, (ci / GEMM_NST) & 1)) {
+    if (!mbar_wait_warp(myBars + slot, (ci / GEMM_NST) & 1)) {
       if (lane == 0) set_error(p.s.st, VP_DEV_ERR_TIMEOUT);
       ok = false;
       break;

@@ -132,7 +132,7 @@ __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsig
 }
 __device__ __forceinline__ void mk_sync() { cons_sync(); }
 
-// The CTA's writes before the barrier are ordered before its arrival by bar.sync + the release
+// The CTA's writes before the barrier are ordered before its arrival by the CTA barrier + the release
 // add (cumulativity); the acquire load orders the other CTAs' writes before what follows.
 __device__ bool grid_barrier(const MegaParams& p, unsigned long long target, int* sAbort) {
   mk_sync();
@@ -171,7 +171,9 @@ constexpr size_t MK_OFF_LMV = MK_OFF_RS + 64;                     // [16 warps][
 constexpr size_t MK_OFF_LMI = MK_OFF_LMV + 1024;                  // [16 warps][16] best id
 constexpr size_t MK_OFF_RI = MK_OFF_LMI + 1024;                   // RowInfo copy
 constexpr size_t MK_OFF_XRB = MK_OFF_RI + ((sizeof(RowInfo) + 15) & ~size_t(15));  // owned x slice
-constexpr size_t MK_OFF_BAR = (MK_OFF_XRB + 16 * 16 * 4 + 127) & ~size_t(127);
+constexpr size_t MK_OFF_EPC = MK_OFF_XRB + 16 * 16 * 4;  // epilogue constants: 16 bias / norm weights,
+                                                         // 128 (cos, sin) pairs
+constexpr size_t MK_OFF_BAR = (MK_OFF_EPC + (16 + 256) * 4 + 127) & ~size_t(127);
 constexpr size_t MK_SMEM = MK_OFF_BAR + 8 * (2 * MK_NSLOT);
 static_assert(sizeof(AttnSmem) <= MK_OFF_RS - MK_OFF_ACT, "attention scratch fits its overlay");
 static_assert(MK_SMEM <= 232448, "dynamic shared memory of the pass kernel fits one sm_100 CTA");
@@ -333,7 +335,7 @@ __device__ __forceinline__ uint8_t* mk_down_stage(uint8_t* sAct, float* sPart, i
 // Wait until piece k is in the ring (bounded); returns its slot base or null on timeout.
 __device__ __forceinline__ const uint8_t* mk_piece(MkRing& rg, int k) {
   while (rg.waited <= k) {
-    if (!mbar_wait_bounded(rg.full + rg.waited % MK_NSLOT, (rg.waited / MK_NSLOT) & 1)) return nullptr;
+    if (!mbar_wait_warp(rg.full + rg.waited % MK_NSLOT, (rg.waited / MK_NSLOT) & 1)) return nullptr;
     ++rg.waited;
   }
   return rg.base + (size_t)(k % MK_NSLOT) * MK_SLOT;
@@ -407,6 +409,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
         const uint8_t* base = mk_piece(rg, k);
         if (!base) { ok = false; break; }
         cp_async_wait<0>();
+        __syncwarp();  // converged before the warp-collective MMAs
         uint4 bf[1][4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) bf[0][j] = *reinterpret_cast<const uint4*>(sB + j * 512 + lane * 16);
@@ -474,6 +477,83 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
   return make_int2(ok ? rg.released : -1, rg.waited);
 }
 
+// Fused epilogue of a GEMM stage, element-parallel over the CTA's 512 compute threads: thread
+// (row-block i, token t, row pair rp) sums the K parts of output rows rp and rp + 8 (the RoPE pair
+// of QKV, gate and up of gate/up, two dims of O / down) in part order and applies the stage's
+// epilogue. The 8 lanes of a token sit in one warp (RMSNorm partial of the down / O output).
+template <int MODE>
+__device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int nrb, int P, const float* sPart,
+                                            const float* rs, const float* sEpc) {
+  const Scratch& s = gp.s;
+  const RowInfo* ri = s.ri;
+  const int n = ri->n;
+  for (int e = threadIdx.x; e < nrb * 128; e += MK_CONS) {
+    const int i = e >> 7, lt = e & 127, t = lt >> 3, rp = lt & 7, rb = rb0 + i;
+    float s0 = 0.f, s1 = 0.f;
+    const float* part = sPart + i * P * 256;
+    for (int q = 0; q < P; ++q) {
+      s0 += part[q * 256 + rp * 16 + t];
+      s1 += part[q * 256 + (rp + 8) * 16 + t];
+    }
+    if constexpr (MODE == MODE_QKV) {
+      const int head = rb >> 2, d = (rb & 3) * 8 + rp;
+      if (t < n) {
+        // nrb == 1 for QKV (one CTA per row-block): bias and rotations are in shared memory
+        float a = s0 * rs[t] + sEpc[rp];
+        float b = s1 * rs[t] + sEpc[8 + rp];
+        if (head < NQ + NKV) {
+          const float2 cs = reinterpret_cast<const float2*>(sEpc + 16)[lt];
+          const float a2 = a * cs.x - b * cs.y;
+          const float b2 = b * cs.x + a * cs.y;
+          a = a2; b = b2;
+        }
+        if (head < NQ) {
+          s.q[t * H + head * HD + d] = a;
+          s.q[t * H + head * HD + d + 32] = b;
+        } else {
+          const int kvh = head < NQ + NKV ? head - NQ : head - NQ - NKV;
+          __half* c = head < NQ + NKV ? s.kc : s.vc;
+          __half* row = c + ((size_t)(gp.layer * NKV + kvh) * s.max_ctx + ri->pos + t) * HD;
+          row[d] = __float2half_rn(a);
+          row[d + 32] = __float2half_rn(b);
+        }
+      }
+    } else if constexpr (MODE == MODE_RESID) {
+      const int d0 = rb * 16 + rp, d1 = d0 + 8;
+      float v0 = 0.f, v1 = 0.f;
+      if (t < n) {
+        const float x0 = gp.xs ? gp.xs[t * 16 + rp] : __ldcg(s.x + t * H + d0);
+        const float x1 = gp.xs ? gp.xs[t * 16 + rp + 8] : __ldcg(s.x + t * H + d1);
+        v0 = x0 + s0;
+        v1 = x1 + s1;
+        if (gp.xs) {
+          gp.xs[t * 16 + rp] = v0;
+          gp.xs[t * 16 + rp + 8] = v1;
+        }
+        s.x[t * H + d0] = v0;
+        s.x[t * H + d1] = v1;
+      }
+      const float w0 = nrb == 1 ? sEpc[rp] : gp.wnext[d0], w1 = nrb == 1 ? sEpc[rp + 8] : gp.wnext[d1];
+      gp.act_out[act_index(t, d0)] = __float2half_rn(v0 * w0);
+      gp.act_out[act_index(t, d1)] = __float2half_rn(v1 * w1);
+      float sq = v0 * v0 + v1 * v1;
+      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+      if (rp == 0) gp.ss_out[rb * 16 + t] = sq;
+    } else {  // MODE_SILU
+      const int f = rb * 8 + rp;
+      float h = 0.f;
+      if (t < n) {
+        const float g = s0 * rs[t];
+        const float u = s1 * rs[t];
+        h = g / (1.f + expf(-g)) * u;
+      }
+      gp.act_out[act_index(t, f)] = __float2half_rn(h);
+    }
+  }
+}
+
 // One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
 // Returns false if a wait timed out.
 template <int FMT, int MODE>
@@ -501,6 +581,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   // act copies are in flight while the partial sums load (all 56 at once, summed in fixed order)
   // (the partials land in the partial-tile area, which is free until the jobs start)
   float* sSs = sPart;
+  float* sEpc = reinterpret_cast<float*>(smem + MK_OFF_EPC);
   {
     const uint64_t pol = policy_evict_last();
     if (!down)
@@ -509,6 +590,20 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
     if (MODE != MODE_RESID && threadIdx.x < HRB * 16 / 4)
       cp_async16(sSs + threadIdx.x * 4, gp.ss_in + threadIdx.x * 4, 16u, pol);
     cp_async_commit();
+    // constants of the epilogue (QKV bias and RoPE rotations, the next RMSNorm's weights) load
+    // while the copies are in flight, so the epilogue does not wait on a global round trip
+    if constexpr (MODE == MODE_QKV) {  // one row-block per CTA
+      const RowInfo* ri = gp.s.ri;
+      const int head = rb0 >> 2, tid = threadIdx.x;
+      if (tid < 16) sEpc[tid] = gp.bias[head * HD + (rb0 & 3) * 8 + (tid & 7) + (tid >> 3) * 32];
+      if (head < NQ + NKV && tid >= 32 && tid < 32 + 128) {
+        const int lt = tid - 32, t = lt >> 3, d = (rb0 & 3) * 8 + (lt & 7);
+        if (t < ri->n)
+          reinterpret_cast<float2*>(sEpc + 16)[lt] = gp.s.rope[(ri->pos + ri->depth[t]) * 32 + d];
+      }
+    } else if constexpr (MODE == MODE_RESID) {
+      if (nrb == 1 && threadIdx.x < 16) sEpc[threadIdx.x] = gp.wnext[rb0 * 16 + threadIdx.x];
+    }
     cp_async_wait<0>();
   }
   mk_sync();
@@ -554,20 +649,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   mk_sync();
   MK_DSTAMP(p, dtr, 256 + 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
-  if (P > 1) {
-    for (int i = warp; i < nrb; i += MK_WARPS) {
-      float sum[2][4] = {};
-      for (int q = 0; q < P; ++q) {
-        const float* part = sPart + (i * P + q) * 256;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int r = 0; r < 4; ++r)
-            sum[nt][r] += part[(gid + 8 * (r >> 1)) * 16 + nt * 8 + 2 * tid4 + (r & 1)];
-      }
-      gemm_epilogue<MODE>(gp, rb0 + i, sum, sRs, lane);
-    }
-  }
+  if (P > 1) mk_epilogue<MODE>(gp, rb0, nrb, P, sPart, sRs, sEpc);
   MK_DSTAMP(p, dtr, 256 + 8 * st + 5);
   return true;
 }
@@ -591,7 +673,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
     fence_barrier_init();
     sAbort = 0;
   }
-  __syncthreads();
+  cta_sync();
 
   if (warp == MK_WARPS) {
     mk_producer<FMT>(p, smem, &sAbort);
@@ -741,7 +823,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
     if (!live || !ok) sAbort = 1;  // the producer stops waiting for releases
     stamp();
   }
-  __syncthreads();
+  cta_sync();
   if (threadIdx.x == 0) {
     __threadfence();
     if (atomicAdd(p.exit_ctr, 1u) == (unsigned)G - 1) {

@@ -386,6 +386,15 @@ int vp_read_state(vp_ctx* c, vp_state* host, void* stream) {
   return host->err ? VP_ERR_DEVICE : VP_OK;
 }
 
+int vp_write_state(vp_ctx* c, const vp_state* state, int32_t from_device, void* stream) {
+  if (!c || !state) return fail(VP_ERR_ARG, "null argument");
+  VP_CUDA(cudaSetDevice(c->cfg.device));
+  VP_CUDA(cudaMemcpyAsync(c->s.st, state, sizeof(vp_state),
+                          from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                          static_cast<cudaStream_t>(stream)));
+  return VP_OK;
+}
+
 int vp_read_tokens(vp_ctx* c, int32_t* host, int32_t count, void* stream) {
   if (!c || !host || count < 0 || count > c->cfg.max_steps) return fail(VP_ERR_ARG, "bad argument");
   VP_CUDA(cudaSetDevice(c->cfg.device));
@@ -523,7 +532,7 @@ __global__ void k_na_argmax(const float* pval, const int* pidx, int nrb, const v
     if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
   }
   if (lane == 0) { rv[warp] = best; ri_[warp] = bi; }
-  __syncthreads();
+  cta_sync();
   if (tid == 0) {
     best = rv[0];
     bi = ri_[0];

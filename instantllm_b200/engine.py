@@ -163,6 +163,25 @@ class VerifyEngine:
             check(rc, "vp_read_state")
         return d
 
+    def snapshot(self):
+        """The device state as (host VpState, device int32[16] copy), e.g. right after a prefill."""
+        st = VpState()
+        rc = self.lib.vp_read_state(self.ctx, ctypes.byref(st), self._s)
+        if rc not in (0, -5):
+            check(rc, "vp_read_state")
+        dev = torch.tensor([getattr(st, n) for n in _lib.STATE_FIELDS], dtype=torch.int32,
+                           device=self.device)
+        return st, dev
+
+    def restore(self, snap, on_device: bool = True):
+        """Write a snapshot back into the device state (stream-ordered): the next pass runs from
+        that point over the same cached prefix."""
+        st, dev = snap
+        if on_device:
+            check(self.lib.vp_write_state(self.ctx, dev.data_ptr(), 1, self._s), "vp_write_state")
+        else:
+            check(self.lib.vp_write_state(self.ctx, ctypes.addressof(st), 0, self._s), "vp_write_state")
+
     def tokens(self, count: Optional[int] = None) -> list:
         st = self.state()
         count = st["step"] if count is None else count
