@@ -63,34 +63,45 @@ __device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
   __shared__ int sTok, sN, sLive;
   __shared__ int sDepth[ROWS], sPar[ROWS];
   __shared__ float sPart[HRB];
+  __shared__ int sIn[VP_TREE_INTS + 3];  // the tree buffer (or the prompt chunk), done, pos, last token
+  // every input in one parallel round trip; the validation below then reads shared memory only
+  if (p.prompt) {
+    if (tid < p.chunk_n && tid < ROWS) sIn[tid] = p.prompt[tid];
+  } else if (tid < VP_TREE_INTS) {
+    sIn[tid] = s.tree[tid];
+  }
+  if (tid == VP_TREE_INTS) sIn[tid] = __ldcg(&st->done);
+  if (tid == VP_TREE_INTS + 1) sIn[tid] = __ldcg(&st->pos);
+  if (tid == VP_TREE_INTS + 2) sIn[tid] = __ldcg(&st->last_token);
+  cons_sync();
   if (tid == 0) {
-    int live = __ldcg(&st->done) == 0, err = 0, n, pos;
+    int live = sIn[VP_TREE_INTS] == 0, err = 0, n, pos;
     if (p.prompt) {
       n = p.chunk_n;
-      pos = __ldcg(&st->pos) + p.chunk_start;
+      pos = sIn[VP_TREE_INTS + 1] + p.chunk_start;
       for (int i = 0; i < ROWS; ++i) { sDepth[i] = i; sPar[i] = i - 1; }
       if (n < 1 || n > ROWS) err |= VP_DEV_ERR_TREE;
       for (int i = 0; i < n && !err; ++i)
-        if (p.prompt[i] < 0 || p.prompt[i] >= s.vocab) err |= VP_DEV_ERR_TREE;
-      sTok = (!err && t < n) ? p.prompt[t] : 0;
+        if (sIn[i] < 0 || sIn[i] >= s.vocab) err |= VP_DEV_ERR_TREE;
+      sTok = (!err && t < n) ? sIn[t] : 0;
     } else {
-      n = s.tree[VP_TR_N];
-      pos = __ldcg(&st->pos);
+      n = sIn[VP_TR_N];
+      pos = sIn[VP_TREE_INTS + 1];
       if (n < 1 || n > ROWS) err |= VP_DEV_ERR_TREE;
       for (int i = 0; i < ROWS && !err; ++i) {
-        sDepth[i] = s.tree[VP_TR_DEPTH + i];
-        sPar[i] = s.tree[VP_TR_PARENT + i];
+        sDepth[i] = sIn[VP_TR_DEPTH + i];
+        sPar[i] = sIn[VP_TR_PARENT + i];
       }
       if (!err) {
         if (sDepth[0] != 0) err |= VP_DEV_ERR_TREE;
         for (int i = 1; i < n; ++i) {
           const int pa = sPar[i];
           if (pa < 0 || pa >= i || sDepth[i] != sDepth[pa] + 1) err |= VP_DEV_ERR_TREE;
-          const int tk = s.tree[VP_TR_TOK + i];
+          const int tk = sIn[VP_TR_TOK + i];
           if (tk < 0 || tk >= s.vocab) err |= VP_DEV_ERR_TREE;
         }
       }
-      sTok = t == 0 ? __ldcg(&st->last_token) : ((!err && t < n) ? s.tree[VP_TR_TOK + t] : 0);
+      sTok = t == 0 ? sIn[VP_TREE_INTS + 2] : ((!err && t < n) ? sIn[VP_TR_TOK + t] : 0);
       if (sTok < 0 || sTok >= s.vocab) err |= VP_DEV_ERR_TREE;
     }
     if (!err && (pos < 0 || pos + n > s.max_ctx)) err |= VP_DEV_ERR_CTX;

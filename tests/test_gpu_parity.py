@@ -131,6 +131,30 @@ def test_device_errors_set_flags_without_hanging(small):
     eng2.close()
 
 
+def test_write_state_replays_a_pass(small):
+    """vp_write_state: a state snapshot written back (from device and from host memory) replays the
+    same pass over the same cached prefix: same committed tokens, same state, same KV rows."""
+    fmt, w, m, eng = small
+    if fmt != "q4":
+        pytest.skip("format independent")
+    prompt = (synth.make_prompt(21, seed=5) % VOCAB_SMALL).tolist()
+    eng.begin(0, 40)
+    eng.prefill(prompt)
+    snap = eng.snapshot()
+    first = eng.tokens(1)[0]
+    tree = synth.seeded_tree(np.random.default_rng(9), [first] * 9, n=12, vocab=VOCAB_SMALL)
+    eng.pass_(tree)
+    st1, tok1 = eng.state(), eng.tokens()
+    k1, v1 = (x.clone() for x in eng.kv())
+    for on_device in (True, False):
+        eng.restore(snap, on_device=on_device)
+        assert eng.state()["step"] == 1
+        eng.pass_(tree)
+        assert eng.state() == st1 and eng.tokens() == tok1
+        k2, v2 = eng.kv()
+        assert torch.equal(k1, k2) and torch.equal(v1, v2)
+
+
 # ---------------------------------------------------------------------------------------------
 # full-size model
 
