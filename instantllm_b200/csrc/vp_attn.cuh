@@ -240,22 +240,28 @@ __device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, cons
   const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
   if (tr && lane == 0) tr[0] = globaltimer();
   const int pos = ri->pos, L = pos + ri->depth[t] + 1;
-  // stage the K and V rows: lane copies 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8,
-  // of both K and V; positions past the row are zeros
+  // stage the K rows, then the V rows (two cp.async groups: S starts once K has landed, V keeps
+  // arriving behind it): lane copies 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8;
+  // positions past the row are zeros
   {
     const uint64_t pol = policy_evict_last();
     const int ch = lane & 7;
     uint8_t* dk = reinterpret_cast<uint8_t*>(buf);
-#pragma unroll 2
+    size_t src[8];
+    uint32_t nb[8];
+#pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int r = (lane >> 3) + 4 * k, jv = c * ATT_SUB + r;
       const bool valid = jv < L;
       const int slot = !valid ? 0 : jv < pos ? jv : pos + ri->path[t][min(jv - pos, ROWS - 1)];
-      const size_t src = (size_t)slot * HD + ch * 8;
-      const uint32_t off = kv_off(r, ch), n = valid ? 16u : 0u;
-      cp_async16(dk + off, kc + src, n, pol);
-      cp_async16(dk + ATT_SUB * HD * 2 + off, vc + src, n, pol);
+      src[k] = (size_t)slot * HD + ch * 8;
+      nb[k] = valid ? 16u : 0u;
+      cp_async16(dk + kv_off(r, ch), kc + src[k], nb[k], pol);
     }
+    cp_async_commit();
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      cp_async16(dk + ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch), vc + src[k], nb[k], pol);
     cp_async_commit();
   }
   // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero)
@@ -272,7 +278,7 @@ __device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, cons
     }
   }
   if (tr && lane == 0) tr[1] = globaltimer_after(__uint_as_float(qa[3][1][1]));
-  cp_async_wait<0>();
+  cp_async_wait<1>();  // the K rows (this lane's copies; __syncwarp makes the warp's visible)
   __syncwarp();
   if (tr && lane == 0) tr[2] = globaltimer();
   const uint32_t sK = smem_u32(buf), sV = sK + ATT_SUB * HD * 2;
@@ -317,6 +323,8 @@ __device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, cons
     }
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
+  cp_async_wait<0>();  // the V rows
+  __syncwarp();
   // P as the A operand: k-step kk = positions 16kk..16kk+15 = n-tiles 2kk (a0) and 2kk+1 (a2)
   uint32_t pa[2][2][2];  // [kk][hi, lo][a0, a2]
 #pragma unroll
