@@ -51,7 +51,9 @@ extern "C" {
 #define VP_TR_TOK 33
 #define VP_TR_ANC 49
 
-enum vp_format { VP_FMT_F16 = 0, VP_FMT_Q8 = 1, VP_FMT_Q4 = 2 };
+/* VP_FMT_Q8 is int8 with one scale per 64 columns; VP_FMT_Q8G32 is the
+ * reference's own q8 layout, one scale per 32 columns (Convert.swift:254-282). */
+enum vp_format { VP_FMT_F16 = 0, VP_FMT_Q8 = 1, VP_FMT_Q4 = 2, VP_FMT_Q8G32 = 3 };
 
 /* Matrix roles for vp_pack_matrix: the packer applies the row order the fused epilogues need. */
 enum vp_matrix_kind {
@@ -124,6 +126,8 @@ typedef struct {
  *   q4:  codes uint8 [rows][cols/2], weight 2j in the low nibble of byte j (Convert.swift:317);
  *        scales half2 [rows][cols/64] = (scale, min); w = scale*q + min (Convert.swift:290-317).
  *   q8:  codes int8 [rows][cols]; scales half [rows][cols/64]; w = scale*q (group 64).
+ *   q8g32: codes int8 [rows][cols]; scales half [rows][cols/32]; w = scale*q (group 32, the
+ *        reference's quantizeQ8 output, Convert.swift:254-282).
  *   f16: half [rows][cols]; scales NULL.
  * vp_pack_matrix rewrites one matrix into the kernel layout (16-row x 64-column tiles in
  * tensor-core fragment order). Both buffers are device memory. */

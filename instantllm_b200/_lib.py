@@ -11,7 +11,7 @@ LIB_PATH = PKG / "libvpass.so"
 
 MAX_LAYERS = 24
 TREE_INTS = 65
-FMT = {"f16": 0, "q8": 1, "q4": 2}
+FMT = {"f16": 0, "q8": 1, "q4": 2, "q8g32": 3}
 MAT_PLAIN, MAT_QKV, MAT_GATEUP = 0, 1, 2
 
 # every symbol include/vpass.h declares

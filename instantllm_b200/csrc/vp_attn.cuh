@@ -38,6 +38,12 @@ __device__ __forceinline__ float embed_value(const uint8_t* E, int tok, int k) {
                                                       (a & 1) * 2 + hi);
     const float s = __half2float(*reinterpret_cast<const __half*>(tile + 1024 + (g * 2 + upper) * 2));
     return __fmul_rn(s, (float)q);
+  } else if constexpr (FMT == VP_FMT_Q8G32) {
+    const int8_t q = *reinterpret_cast<const int8_t*>(tile + lane * 32 + j * 8 + (a >> 1) * 4 +
+                                                      (a & 1) * 2 + hi);
+    const int half = kk >> 5;  // scale of the 32-column half
+    const float s = __half2float(*reinterpret_cast<const __half*>(tile + 1024 + (g * 4 + half * 2 + upper) * 2));
+    return __fmul_rn(s, (float)q);
   } else {
     return __half2float(
         *reinterpret_cast<const __half*>(tile + lane * 64 + j * 16 + a * 4 + hi * 2));

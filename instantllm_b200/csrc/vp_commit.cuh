@@ -175,6 +175,11 @@ __global__ void k_pack(int kind, int rows, int cols, const uint8_t* codes, const
       } else if (FMT == VP_FMT_Q8) {
         const uint16_t v = reinterpret_cast<const uint16_t*>(scales)[(size_t)sr * ng + G];
         reinterpret_cast<uint16_t*>(tile + 1024)[g * 2 + upper] = v;
+      } else if (FMT == VP_FMT_Q8G32) {  // scales [rows][cols/32]: both halves of the tile
+        for (int h = 0; h < 2; ++h) {
+          const uint16_t v = reinterpret_cast<const uint16_t*>(scales)[(size_t)sr * (2 * ng) + 2 * G + h];
+          reinterpret_cast<uint16_t*>(tile + 1024)[g * 4 + h * 2 + upper] = v;
+        }
       }
     }
     return;
@@ -193,7 +198,7 @@ __global__ void k_pack(int kind, int rows, int cols, const uint8_t* codes, const
           w |= q << ((hi ? 16 : 0) + 4 * a);
         }
       reinterpret_cast<uint32_t*>(tile + lane * 16)[j] = w;
-    } else if (FMT == VP_FMT_Q8) {
+    } else if (fmt_is_q8(FMT)) {
       uint8_t bytes[8];
       for (int a = 0; a < 4; ++a)
         for (int hi = 0; hi < 2; ++hi) {

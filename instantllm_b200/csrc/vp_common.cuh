@@ -29,12 +29,20 @@ constexpr float EPS = 1e-6f;
 constexpr float ATTN_SCALE = 0.125f;  // 64^-0.5, exact
 constexpr int ATT_SUB = 32;           // virtual positions per attention record (fixed: shape-invariant)
 
-// Bytes of one packed 16x64 tile per format: codes then per-row scale data.
+// Bytes of one packed 16x64 tile per format: codes then per-row scale data (q8g32: two scales
+// per row, one per 32-column half).
 __host__ __device__ constexpr int tile_bytes(int fmt) {
-  return fmt == VP_FMT_Q4 ? 512 + 64 : fmt == VP_FMT_Q8 ? 1024 + 32 : 2048;
+  return fmt == VP_FMT_Q4 ? 512 + 64 : fmt == VP_FMT_Q8 ? 1024 + 32 : fmt == VP_FMT_Q8G32 ? 1024 + 64 : 2048;
 }
 __host__ __device__ constexpr int tile_code_bytes(int fmt) {
-  return fmt == VP_FMT_Q4 ? 512 : fmt == VP_FMT_Q8 ? 1024 : 2048;
+  return fmt == VP_FMT_Q4 ? 512 : (fmt == VP_FMT_Q8 || fmt == VP_FMT_Q8G32) ? 1024 : 2048;
+}
+__host__ __device__ constexpr bool fmt_is_q8(int fmt) { return fmt == VP_FMT_Q8 || fmt == VP_FMT_Q8G32; }
+// Formats whose 64-column tile carries one scale per 32-column half: the group sums and the fold
+// are kept per half.
+__host__ __device__ constexpr bool fmt_halves(int fmt) { return fmt == VP_FMT_Q8G32; }
+__host__ __device__ constexpr bool fmt_valid(int fmt) {
+  return fmt == VP_FMT_F16 || fmt == VP_FMT_Q8 || fmt == VP_FMT_Q4 || fmt == VP_FMT_Q8G32;
 }
 
 // Half index of activation (token t, column k) in B-fragment order (see file comment).

@@ -48,7 +48,8 @@ struct GemmParams {
 
 __host__ inline size_t gemm_smem_bytes(int fmt, int ng, int nsplit, int cg) {
   const int ngs = (ng + nsplit - 1) / nsplit;
-  size_t b = (size_t)ngs * 2048 + (size_t)ngs * 16 * 4 + 16 * 4;   // act blocks, group sums, rscale
+  size_t b = (size_t)ngs * 2048 + (size_t)ngs * 16 * 4 * (fmt_halves(fmt) ? 2 : 1) + 16 * 4;
+  // act blocks, group sums (per 32-column half for q8g32), rscale
   b = (b + 127) & ~size_t(127);
   b += (size_t)GEMM_WARPS * GEMM_NST * cg * tile_bytes(fmt);
   b += 8 * (1 + GEMM_WARPS * GEMM_NST) + 128;
@@ -64,7 +65,7 @@ __device__ __forceinline__ void load_a_frags(const uint8_t* tile, int lane, int 
     a[1] = v & 0x00F000F0u;   // row gid+8, codes * 2^-20
     a[2] = v8 & 0x000F000Fu;
     a[3] = v8 & 0x00F000F0u;
-  } else if constexpr (FMT == VP_FMT_Q8) {
+  } else if constexpr (fmt_is_q8(FMT)) {
     const uint2 v = reinterpret_cast<const uint2*>(tile + lane * 32)[j];
     const uint32_t u0 = v.x ^ 0x80808080u, u1 = v.y ^ 0x80808080u;  // q + 128 in 1..255
     a[0] = __byte_perm(u0, 0u, 0x5150);   // bytes 0,1 -> low bytes of two halves
@@ -77,9 +78,22 @@ __device__ __forceinline__ void load_a_frags(const uint8_t* tile, int lane, int 
   }
 }
 
+// Per-row (gid, gid+8) and per-half constants of a q8g32 tile (one scale per 32 columns):
+// y += sf[h] * acc[h] + sb[h] * X[h] for the halves h = 0 (columns 0..31) and 1 (32..63).
+__device__ __forceinline__ void load_fold_halves(const uint8_t* tile, int gid, float (&sf)[2][2], float (&sb)[2][2]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(tile + 1024 + gid * 8);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float2 p = __half22float2(*reinterpret_cast<const __half2*>(h ? &v.y : &v.x));
+    sf[h][0] = p.x * 16777216.f; sb[h][0] = -128.f * p.x;   // (q + 128) * 2^-24, rows gid
+    sf[h][1] = p.y * 16777216.f; sb[h][1] = -128.f * p.y;   // and gid + 8
+  }
+}
+
 // Per-row (gid, gid+8) affine constants of one tile: y += sf * acc + sb * X.
 template <int FMT>
 __device__ __forceinline__ void load_fold(const uint8_t* tile, int gid, float (&sf)[2], float (&sb)[2]) {
+  static_assert(!fmt_halves(FMT), "q8g32 tiles fold per half (load_fold_halves)");
   if constexpr (FMT == VP_FMT_Q4) {
     const uint2 v = *reinterpret_cast<const uint2*>(tile + 512 + gid * 8);
     const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
@@ -217,8 +231,9 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
 
   uint8_t* sAct = smem;
   float* sX = reinterpret_cast<float*>(smem + (size_t)ngs_max * 2048);
-  float* sRs = sX + ngs_max * 16;
-  size_t off = (size_t)ngs_max * 2048 + (size_t)ngs_max * 16 * 4 + 16 * 4;
+  float* sRs = sX + ngs_max * 16 * (fmt_halves(FMT) ? 2 : 1);
+  // same layout as gemm_smem_bytes: act blocks, group sums (two per group for q8g32), rscale
+  size_t off = (size_t)ngs_max * 2048 + (size_t)ngs_max * 16 * 4 * (fmt_halves(FMT) ? 2 : 1) + 16 * 4;
   off = (off + 127) & ~size_t(127);
   uint8_t* ring = smem + off + (size_t)warp * GEMM_NST * p.cg * TB;
   off += (size_t)GEMM_WARPS * GEMM_NST * p.cg * TB;
@@ -285,19 +300,25 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
     if (FMT != VP_FMT_F16 && act_ok) {
       const uint32_t ONE2 = 0x3C003C00u;
       for (int g = warp; g < g1 - g0; g += GEMM_WARPS) {
-        float xs[2][4] = {};
+        constexpr int NH = fmt_halves(FMT) ? 2 : 1;
+        float xs[NH][2][4] = {};
         const uint8_t* ab = sAct + (size_t)g * 2048;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint4 b = *reinterpret_cast<const uint4*>(ab + j * 512 + lane * 16);
-          mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
-          mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
+          const int h = NH == 2 ? (j >> 1) : 0;
+          mma16816(xs[h][0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
+          mma16816(xs[h][1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
         }
         if (gid == 0) {
-          sX[g * 16 + 2 * tid4] = xs[0][0];
-          sX[g * 16 + 2 * tid4 + 1] = xs[0][1];
-          sX[g * 16 + 8 + 2 * tid4] = xs[1][0];
-          sX[g * 16 + 8 + 2 * tid4 + 1] = xs[1][1];
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            float* xo = sX + (g * NH + h) * 16;
+            xo[2 * tid4] = xs[h][0][0];
+            xo[2 * tid4 + 1] = xs[h][0][1];
+            xo[8 + 2 * tid4] = xs[h][1][0];
+            xo[8 + 2 * tid4 + 1] = xs[h][1][1];
+          }
         }
       }
     }
@@ -337,6 +358,33 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
           const uint4 b = *reinterpret_cast<const uint4*>(ab + j * 512 + lane * 16);
           mma16816(acc[0], a[0], a[1], a[2], a[3], b.x, b.y);
           mma16816(acc[1], a[0], a[1], a[2], a[3], b.z, b.w);
+        }
+      } else if constexpr (fmt_halves(FMT)) {
+        // q8g32: the two 32-column halves accumulate and fold separately
+        float ag[2][2][4] = {};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t a[4];
+          load_a_frags<FMT>(tile, lane, j, a);
+          const uint4 b = *reinterpret_cast<const uint4*>(ab + j * 512 + lane * 16);
+          mma16816(ag[j >> 1][0], a[0], a[1], a[2], a[3], b.x, b.y);
+          mma16816(ag[j >> 1][1], a[0], a[1], a[2], a[3], b.z, b.w);
+        }
+        float sf[2][2], sb[2][2];
+        load_fold_halves(tile, gid, sf, sb);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float* xg = sX + ((g - g0) * 2 + h) * 16;
+          const float2 x0 = *reinterpret_cast<const float2*>(xg + 2 * tid4);
+          const float2 x1 = *reinterpret_cast<const float2*>(xg + 8 + 2 * tid4);
+          const float tx[2][2] = {{x0.x, x0.y}, {x1.x, x1.y}};
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = i >> 1;
+              acc[nt][i] = fmaf(sf[h][r], ag[h][nt][i], fmaf(sb[h][r], tx[nt][i & 1], acc[nt][i]));
+            }
         }
       } else {
         float ag[2][4] = {};

@@ -160,12 +160,13 @@ __device__ bool grid_barrier(const MegaParams& p, unsigned long long target, int
 constexpr size_t MK_RING_BYTES = (size_t)MK_NSLOT * MK_SLOT;
 constexpr size_t MK_ACT_BYTES = (size_t)(H / GS) * 2048;  // act blocks of a K = 896 GEMM
 constexpr size_t MK_OFF_ACT = MK_RING_BYTES;
-constexpr size_t MK_OFF_X = MK_OFF_ACT + MK_ACT_BYTES;            // 16 x 16 group sums
-constexpr size_t MK_OFF_PART = MK_OFF_X + 16 * 16 * 4;            // partial tiles
+constexpr size_t MK_OFF_X = MK_OFF_ACT + MK_ACT_BYTES;            // group sums
+constexpr size_t MK_X_BYTES = 2 * 16 * 16 * 4;  // group sums [14 groups][halves][16 tokens]
+constexpr size_t MK_OFF_PART = MK_OFF_X + MK_X_BYTES;            // partial tiles
 // attention scratch overlays the act blocks, group sums and partial tiles (and extends past them)
-constexpr size_t MK_OVERLAY = sizeof(AttnSmem) > MK_ACT_BYTES + 16 * 16 * 4 + MK_PART_SLOTS * 1024
+constexpr size_t MK_OVERLAY = sizeof(AttnSmem) > MK_ACT_BYTES + MK_X_BYTES + MK_PART_SLOTS * 1024
                                   ? ((sizeof(AttnSmem) + 127) & ~size_t(127))
-                                  : MK_ACT_BYTES + 16 * 16 * 4 + MK_PART_SLOTS * 1024;
+                                  : MK_ACT_BYTES + MK_X_BYTES + MK_PART_SLOTS * 1024;
 constexpr size_t MK_OFF_RS = MK_OFF_ACT + MK_OVERLAY;              // rscale[16]
 constexpr size_t MK_OFF_LMV = MK_OFF_RS + 64;                     // [16 warps][16] best value
 constexpr size_t MK_OFF_LMI = MK_OFF_LMV + 1024;                  // [16 warps][16] best id
@@ -264,29 +265,41 @@ __device__ __forceinline__ void mk_tiles_bf(const uint8_t* const (&tile)[NT], in
         mma16816(acc[1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
       }
   } else {
-    float ag[NT][2][4];
-    float tx[NT][2][2];
+    // NH = 2 for q8g32: the two 32-column halves of a tile accumulate, sum and fold separately
+    constexpr int NH = fmt_halves(FMT) ? 2 : 1;
+    float ag[NT][NH][2][4];
+    float tx[NT][NH][2][2];
 #pragma unroll
     for (int u = 0; u < NT; ++u) {
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int h = 0; h < NH; ++h)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ag[u][nt][i] = 0.f;
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ag[u][h][nt][i] = 0.f;
       if constexpr (GLOBAL_B) {
         // group sums from the fragments just loaded: a ones-matrix MMA
         const uint32_t ONE2 = 0x3C003C00u;
-        float xs[2][4] = {};
+        float xs[NH][2][4] = {};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, bf[u][j].x, bf[u][j].y);
-          mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, bf[u][j].z, bf[u][j].w);
+          const int h = NH == 2 ? (j >> 1) : 0;
+          mma16816(xs[h][0], ONE2, ONE2, ONE2, ONE2, bf[u][j].x, bf[u][j].y);
+          mma16816(xs[h][1], ONE2, ONE2, ONE2, ONE2, bf[u][j].z, bf[u][j].w);
         }
-        tx[u][0][0] = xs[0][0]; tx[u][0][1] = xs[0][1]; tx[u][1][0] = xs[1][0]; tx[u][1][1] = xs[1][1];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tx[u][h][0][0] = xs[h][0][0]; tx[u][h][0][1] = xs[h][0][1];
+          tx[u][h][1][0] = xs[h][1][0]; tx[u][h][1][1] = xs[h][1][1];
+        }
       } else {
-        const float* xg = sX + (g + u) * 16;
-        const float2 x0 = *reinterpret_cast<const float2*>(xg + 2 * tid4);
-        const float2 x1 = *reinterpret_cast<const float2*>(xg + 8 + 2 * tid4);
-        tx[u][0][0] = x0.x; tx[u][0][1] = x0.y; tx[u][1][0] = x1.x; tx[u][1][1] = x1.y;
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const float* xg = sX + ((g + u) * NH + h) * 16;
+          const float2 x0 = *reinterpret_cast<const float2*>(xg + 2 * tid4);
+          const float2 x1 = *reinterpret_cast<const float2*>(xg + 8 + 2 * tid4);
+          tx[u][h][0][0] = x0.x; tx[u][h][0][1] = x0.y; tx[u][h][1][0] = x1.x; tx[u][h][1][1] = x1.y;
+        }
       }
     }
 #pragma unroll
@@ -295,20 +308,24 @@ __device__ __forceinline__ void mk_tiles_bf(const uint8_t* const (&tile)[NT], in
       for (int u = 0; u < NT; ++u) {
         uint32_t w[4];
         load_a_frags<FMT>(tile[u], lane, j, w);
-        mma16816(ag[u][0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
-        mma16816(ag[u][1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
+        const int h = NH == 2 ? (j >> 1) : 0;
+        mma16816(ag[u][h][0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
+        mma16816(ag[u][h][1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
       }
 #pragma unroll
     for (int u = 0; u < NT; ++u) {
-      float sf[2], sb[2];
-      load_fold<FMT>(tile[u], gid, sf, sb);
+      float sf[NH][2], sb[NH][2];
+      if constexpr (NH == 2) load_fold_halves(tile[u], gid, sf, sb);
+      else load_fold<FMT>(tile[u], gid, sf[0], sb[0]);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int h = 0; h < NH; ++h)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = i >> 1;
-          acc[nt][i] = fmaf(sf[r], ag[u][nt][i], fmaf(sb[r], tx[u][nt][i & 1], acc[nt][i]));
-        }
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = i >> 1;
+            acc[nt][i] = fmaf(sf[h][r], ag[u][h][nt][i], fmaf(sb[h][r], tx[u][h][nt][i & 1], acc[nt][i]));
+          }
     }
   }
 }
@@ -615,18 +632,24 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   }
   if (!down && FMT != VP_FMT_F16 && warp < H / GS) {
     const uint32_t ONE2 = 0x3C003C00u;
-    float xs[2][4] = {};
+    constexpr int NH = fmt_halves(FMT) ? 2 : 1;  // q8g32: one sum per 32-column half
+    float xs[NH][2][4] = {};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint4 b = act_frag_smem(sAct, warp, j, lane);
-      mma16816(xs[0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
-      mma16816(xs[1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
+      const int h = NH == 2 ? (j >> 1) : 0;
+      mma16816(xs[h][0], ONE2, ONE2, ONE2, ONE2, b.x, b.y);
+      mma16816(xs[h][1], ONE2, ONE2, ONE2, ONE2, b.z, b.w);
     }
     if (gid == 0) {
-      sX[warp * 16 + 2 * tid4] = xs[0][0];
-      sX[warp * 16 + 2 * tid4 + 1] = xs[0][1];
-      sX[warp * 16 + 8 + 2 * tid4] = xs[1][0];
-      sX[warp * 16 + 8 + 2 * tid4 + 1] = xs[1][1];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        float* xo = sX + (warp * NH + h) * 16;
+        xo[2 * tid4] = xs[h][0][0];
+        xo[2 * tid4 + 1] = xs[h][0][1];
+        xo[8 + 2 * tid4] = xs[h][1][0];
+        xo[8 + 2 * tid4 + 1] = xs[h][1][1];
+      }
     }
   }
   mk_sync();

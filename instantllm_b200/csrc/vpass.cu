@@ -148,6 +148,7 @@ int launch_pass(vp_ctx* c, const MegaParams& p, cudaStream_t st) {
   switch (c->cfg.format) {
     case VP_FMT_Q4: VP_CUDA(launch(k_pass<VP_FMT_Q4>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
     case VP_FMT_Q8: VP_CUDA(launch(k_pass<VP_FMT_Q8>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
+    case VP_FMT_Q8G32: VP_CUDA(launch(k_pass<VP_FMT_Q8G32>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
     default: VP_CUDA(launch(k_pass<VP_FMT_F16>, c->grid, MK_THREADS, MK_SMEM, st, true, p)); break;
   }
   return VP_OK;
@@ -179,7 +180,7 @@ const char* vp_last_error(void) { return g_err.c_str(); }
 
 size_t vp_packed_bytes(int32_t format, int32_t rows, int32_t cols) {
   if (rows <= 0 || cols <= 0 || rows % 16 || cols % GS) return 0;
-  if (format != VP_FMT_Q4 && format != VP_FMT_Q8 && format != VP_FMT_F16) return 0;
+  if (!fmt_valid(format)) return 0;
   return (size_t)(rows / 16) * (cols / GS) * tile_bytes(format);
 }
 
@@ -199,6 +200,7 @@ int vp_pack_matrix(int32_t format, int32_t kind, int32_t rows, int32_t cols, con
   uint8_t* out = static_cast<uint8_t*>(d_out);
   if (format == VP_FMT_Q4) k_pack<VP_FMT_Q4><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
   else if (format == VP_FMT_Q8) k_pack<VP_FMT_Q8><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
+  else if (format == VP_FMT_Q8G32) k_pack<VP_FMT_Q8G32><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
   else k_pack<VP_FMT_F16><<<grid, block, 0, st>>>(kind, rows, cols, cd, sc, out);
   VP_CUDA(cudaGetLastError());
   return VP_OK;
@@ -207,8 +209,7 @@ int vp_pack_matrix(int32_t format, int32_t kind, int32_t rows, int32_t cols, con
 int vp_create(const vp_config* cfg, vp_ctx** out) {
   if (!cfg || !out) return fail(VP_ERR_ARG, "null argument");
   *out = nullptr;
-  if (cfg->format != VP_FMT_Q4 && cfg->format != VP_FMT_Q8 && cfg->format != VP_FMT_F16)
-    return fail(VP_ERR_ARG, "format must be q4, q8 or f16");
+  if (!fmt_valid(cfg->format)) return fail(VP_ERR_ARG, "format must be q4, q8, q8g32 or f16");
   if (cfg->n_layers < 1 || cfg->n_layers > VP_MAX_LAYERS) return fail(VP_ERR_ARG, "n_layers out of range");
   if (cfg->vocab < 16 || cfg->vocab % 16) return fail(VP_ERR_ARG, "vocab must be a positive multiple of 16");
   if (cfg->vocab > (1 << 24)) return fail(VP_ERR_ARG, "vocab above 2^24");
@@ -280,6 +281,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   }
   if (fmt == VP_FMT_Q4) r = set_attrs<VP_FMT_Q4>(c);
   else if (fmt == VP_FMT_Q8) r = set_attrs<VP_FMT_Q8>(c);
+  else if (fmt == VP_FMT_Q8G32) r = set_attrs<VP_FMT_Q8G32>(c);
   else r = set_attrs<VP_FMT_F16>(c);
   if (r) { vp_destroy(c); return r; }
   *out = c;
@@ -428,6 +430,7 @@ int vp_debug_logits(vp_ctx* c, float* d_out, void* stream) {
   switch (c->cfg.format) {
     case VP_FMT_Q4: VP_CUDA((gemm_launch<VP_FMT_Q4, MODE_ARGMAX>(c->lm, p, st))); break;
     case VP_FMT_Q8: VP_CUDA((gemm_launch<VP_FMT_Q8, MODE_ARGMAX>(c->lm, p, st))); break;
+    case VP_FMT_Q8G32: VP_CUDA((gemm_launch<VP_FMT_Q8G32, MODE_ARGMAX>(c->lm, p, st))); break;
     default: VP_CUDA((gemm_launch<VP_FMT_F16, MODE_ARGMAX>(c->lm, p, st))); break;
   }
   return VP_OK;
@@ -568,6 +571,7 @@ int na_setup(int dev, unsigned char** base) {
     cudaError_t e = cudaGetSymbolAddress(&d.base, g_noalloc_scratch);
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q4>();
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q8>();
+    if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q8G32>();
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_F16>();
     if (e != cudaSuccess) {
       d.base = nullptr;
@@ -585,8 +589,7 @@ int na_setup(int dev, unsigned char** base) {
 extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void* d_embed,
                                       const float* d_final_norm, const float* d_x, int32_t rows,
                                       int32_t* d_tokens, void* stream) {
-  if (format != VP_FMT_Q4 && format != VP_FMT_Q8 && format != VP_FMT_F16)
-    return fail(VP_ERR_ARG, "format must be q4, q8 or f16");
+  if (!fmt_valid(format)) return fail(VP_ERR_ARG, "format must be q4, q8, q8g32 or f16");
   if (vocab < 16 || vocab % 16 || vocab > VP_NOALLOC_MAX_VOCAB)
     return fail(VP_ERR_ARG, "vocab must be a multiple of 16 and at most VP_NOALLOC_MAX_VOCAB (163840)");
   if (rows < 1 || rows > ROWS) return fail(VP_ERR_ARG, "rows must be 1..16");
@@ -625,6 +628,7 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
   switch (format) {
     case VP_FMT_Q4: VP_CUDA((gemm_launch<VP_FMT_Q4, MODE_ARGMAX>(lm, p, s))); break;
     case VP_FMT_Q8: VP_CUDA((gemm_launch<VP_FMT_Q8, MODE_ARGMAX>(lm, p, s))); break;
+    case VP_FMT_Q8G32: VP_CUDA((gemm_launch<VP_FMT_Q8G32, MODE_ARGMAX>(lm, p, s))); break;
     default: VP_CUDA((gemm_launch<VP_FMT_F16, MODE_ARGMAX>(lm, p, s))); break;
   }
   k_na_argmax<<<rows, 256, 0, s>>>(pval, pidx, lm.nrb, st, d_tokens);

@@ -38,6 +38,10 @@ def make_matrix(fmt: str, rows: int, cols: int, rng: np.random.Generator) -> dic
         codes = rng.integers(-127, 128, size=(rows, cols), dtype=np.int8)
         s = np.abs(rng.normal(0.0, 0.0003, size=(rows, cols // 64))).astype(np.float16)
         return {"fmt": "q8", "codes": codes, "scales": s}
+    if fmt == "q8g32":  # the reference's own q8: one scale per 32 columns (Convert.swift:254-282)
+        codes = rng.integers(-127, 128, size=(rows, cols), dtype=np.int8)
+        s = np.abs(rng.normal(0.0, 0.0003, size=(rows, cols // 32))).astype(np.float16)
+        return {"fmt": "q8g32", "codes": codes, "scales": s}
     if fmt == "f16":
         return {"fmt": "f16", "w": rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float16)}
     if fmt == "f32":
@@ -73,6 +77,7 @@ def weight_bytes(fmt: str, n_layers: int = N_LAYERS, vocab: int = VOCAB) -> int:
     and biases (fp32), and the tied lm_head once. q4 full model: 278,139,392."""
     per = {"q4": lambda r, c: r * c // 2 + r * (c // 64) * 4,
            "q8": lambda r, c: r * c + r * (c // 64) * 2,
+           "q8g32": lambda r, c: r * c + r * (c // 32) * 2,
            "f16": lambda r, c: r * c * 2}[fmt]
     layer = per(QKV_ROWS, HIDDEN) + per(HIDDEN, HIDDEN) + per(2 * FFN, HIDDEN) + per(HIDDEN, FFN)
     small = (2 * HIDDEN + QKV_ROWS) * 4

@@ -70,6 +70,8 @@ def dequant(m: dict) -> np.ndarray:
     q4: codes uint8 [R, C/2] (weight 2j in the low nibble of byte j, Convert.swift:317),
         scales float16 [R, C/64, 2] = (scale, min); w = scale * q + min (Convert.swift:290-317).
     q8: codes int8 [R, C], scales float16 [R, C/64]; w = scale * q (group 64 as BASELINE config 3).
+    q8g32: codes int8 [R, C], scales float16 [R, C/32]; w = scale * q (group 32, the reference's
+        quantizeQ8 layout, Convert.swift:254-282).
     f16 / f32: dense.
     """
     fmt = m["fmt"]
@@ -86,11 +88,11 @@ def dequant(m: dict) -> np.ndarray:
         G = s.shape[1]
         q = q.reshape(R, G, 64)
         return (q * s[:, :, None] + b[:, :, None]).reshape(R, G * 64)
-    if fmt == "q8":
+    if fmt in ("q8", "q8g32"):
         R, C = codes.shape
         s = m["scales"].astype(np.float32)
         G = s.shape[1]
-        return (codes.astype(np.float32).reshape(R, G, 64) * s[:, :, None]).reshape(R, C)
+        return (codes.astype(np.float32).reshape(R, G, C // G) * s[:, :, None]).reshape(R, C)
     raise ValueError(fmt)
 
 

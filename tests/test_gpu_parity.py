@@ -28,7 +28,7 @@ def _engine(w, **kw):
     return VerifyEngine(w, **kw)
 
 
-@pytest.fixture(scope="module", params=["q4", "q8", "f16"])
+@pytest.fixture(scope="module", params=["q4", "q8", "q8g32", "f16"])
 def small(request):
     fmt = request.param
     w = synth.make_weights(fmt, n_layers=2, vocab=VOCAB_SMALL, seed=21)
@@ -235,10 +235,12 @@ def test_config2_logits_match_oracle_full_size(full_q4):
     assert eng.tokens(st["step"])[1:] == exp["tokens"]
 
 
-def test_config3_q8_chains_equal_sequential():
-    """Config 3: q8, 1024-token prefix, 8-row chains with p=0.5 matching drafts, 64 tokens, against
-    1-row sequential decode through the same kernels."""
-    w = synth.make_weights("q8", seed=3)
+@pytest.mark.parametrize("fmt", ["q8", "q8g32"])
+def test_config3_q8_chains_equal_sequential(fmt):
+    """Config 3: q8 (group 64 as BASELINE, and the reference's own group 32), 1024-token prefix,
+    8-row chains with p=0.5 matching drafts, 64 tokens, against 1-row sequential decode through
+    the same kernels."""
+    w = synth.make_weights(fmt, seed=3)
     eng = _engine(w, max_ctx=2048, max_steps=128)
     prompt = synth.make_prompt(1024, seed=33).tolist()
     seq = eng.generate(prompt, 64)

@@ -53,6 +53,12 @@ def test_dequant_matches_scalar_restatement():
     m8 = synth.make_matrix("q8", 16, 128, rng)
     d8 = Q.dequant(m8)
     assert d8[3, 70] == np.float32(m8["scales"][3, 1]) * np.float32(m8["codes"][3, 70])
+    # the reference's q8 (quantizeQ8, Convert.swift:254-282): one scale per 32 columns
+    m32 = synth.make_matrix("q8g32", 16, 128, rng)
+    d32 = Q.dequant(m32)
+    assert m32["scales"].shape == (16, 4)
+    for r, i in ((3, 70), (15, 31), (0, 32), (9, 127)):
+        assert d32[r, i] == np.float32(m32["scales"][r, i // 32]) * np.float32(m32["codes"][r, i])
 
 
 def test_accept_tree_matches_reference(golden_dir):
