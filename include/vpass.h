@@ -145,6 +145,16 @@ const char* vp_last_error(void);
  * cached: KV slots already valid (shared prefix); max_new: tokens to generate (incl. a stop). */
 int vp_begin(vp_ctx* ctx, int32_t cached, int32_t max_new, int32_t eos0, int32_t eos1, void* stream);
 
+/* ---- prefix KV cache on disk (Engine.savePrefix / loadPrefix, Engine.swift:788-838) ----
+ * Host copies of the K and V rows of the first n cached positions, laid out as the body of the
+ * reference's prefix file: all K rows, then all V rows, each [layer][kv head][n][64] fp16.
+ * vp_prefix_bytes gives the size (2 * layers * 2 * n * 128 bytes). vp_save_prefix copies device ->
+ * host and synchronises `stream`; vp_load_prefix copies host -> device (stream-ordered), after
+ * which vp_begin(ctx, n, ...) starts a request whose first n positions are that prefix. */
+size_t vp_prefix_bytes(vp_ctx* ctx, int32_t n);
+int vp_save_prefix(vp_ctx* ctx, int32_t n, void* host, void* stream);
+int vp_load_prefix(vp_ctx* ctx, int32_t n, const void* host, void* stream);
+
 /* ---- prefill (Engine.encodePrefill :588-601 = k_embed_prompt + 24 layers + lm_head + commit) ----
  * Runs n prompt tokens at slots pos..pos+n-1 in chunks of 16 rows, then the lm_head on the last
  * row and a 1-row greedy commit (k_commit, Shaders.swift:194-244): out_tokens[step] = argmax. */

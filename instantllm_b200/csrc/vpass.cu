@@ -306,6 +306,44 @@ int vp_set_weights(vp_ctx* c, const vp_weights* w) {
   return VP_OK;
 }
 
+size_t vp_prefix_bytes(vp_ctx* c, int32_t n) {
+  if (!c || n < 1 || n > c->cfg.max_ctx) return 0;
+  return (size_t)2 * c->cfg.n_layers * NKV * n * HD * sizeof(__half);
+}
+
+// Copies the first n rows of every (layer, kv head) slab of the K and V caches to or from the host:
+// one strided 2-D copy per cache (slab pitch max_ctx rows, n rows each).
+static int prefix_copy(vp_ctx* c, int32_t n, void* host, bool save, cudaStream_t st) {
+  const size_t row = (size_t)HD * sizeof(__half), slabs = (size_t)c->cfg.n_layers * NKV;
+  const size_t dev_pitch = (size_t)c->cfg.max_ctx * row, host_pitch = (size_t)n * row;
+  for (int which = 0; which < 2; ++which) {
+    __half* dev = which ? c->s.vc : c->s.kc;
+    uint8_t* h = static_cast<uint8_t*>(host) + (size_t)which * slabs * host_pitch;
+    if (save)
+      VP_CUDA(cudaMemcpy2DAsync(h, host_pitch, dev, dev_pitch, host_pitch, slabs, cudaMemcpyDeviceToHost, st));
+    else
+      VP_CUDA(cudaMemcpy2DAsync(dev, dev_pitch, h, host_pitch, host_pitch, slabs, cudaMemcpyHostToDevice, st));
+  }
+  return VP_OK;
+}
+
+int vp_save_prefix(vp_ctx* c, int32_t n, void* host, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!host || !vp_prefix_bytes(c, n)) return fail(VP_ERR_ARG, "bad prefix length or buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((r = prefix_copy(c, n, host, true, st))) return r;
+  VP_CUDA(cudaStreamSynchronize(st));
+  return VP_OK;
+}
+
+int vp_load_prefix(vp_ctx* c, int32_t n, const void* host, void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!host || !vp_prefix_bytes(c, n) || n + ROWS > c->cfg.max_ctx) return fail(VP_ERR_ARG, "bad prefix length or buffer");
+  return prefix_copy(c, n, const_cast<void*>(host), false, static_cast<cudaStream_t>(stream));
+}
+
 int vp_begin(vp_ctx* c, int32_t cached, int32_t max_new, int32_t eos0, int32_t eos1, void* stream) {
   if (!c) return fail(VP_ERR_ARG, "null context");
   if (cached < 0 || max_new < 1 || max_new > c->cfg.max_steps) return fail(VP_ERR_ARG, "bad request size");

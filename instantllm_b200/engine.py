@@ -182,6 +182,57 @@ class VerifyEngine:
         else:
             check(self.lib.vp_write_state(self.ctx, ctypes.addressof(st), 0, self._s), "vp_write_state")
 
+    # ---- prefix KV cache on disk (Engine.savePrefix / loadPrefix, Engine.swift:788-838) ----
+    PREFIX_MAGIC = 0x3156_4B4C_4C49  # "ILLKV1"
+
+    def _prefix_key(self, model_path: Optional[str]) -> list:
+        """The reference's file key: magic, model file size and mtime (s, ns), max context."""
+        import os
+
+        if model_path is None:  # synthetic weights: no model file
+            return [self.PREFIX_MAGIC, 0, 0, 0, self.max_ctx]
+        stt = os.stat(model_path)
+        return [self.PREFIX_MAGIC, stt.st_size, int(stt.st_mtime), stt.st_mtime_ns % 1_000_000_000, self.max_ctx]
+
+    def save_prefix(self, path: str, tokens, model_path: Optional[str] = None) -> None:
+        """Save the K/V rows of the first len(tokens) cached positions (their tokens are `tokens`)
+        in the reference's prefix-file layout."""
+        toks = np.asarray(tokens, dtype=np.int32)
+        n = int(toks.size)
+        body = np.empty(int(self.lib.vp_prefix_bytes(self.ctx, n)), dtype=np.uint8)
+        if body.size == 0:
+            raise ValueError("bad prefix length")
+        check(self.lib.vp_save_prefix(self.ctx, n, body.ctypes.data, self._s), "vp_save_prefix")
+        head = np.array(self._prefix_key(model_path) + [n], dtype=np.uint64)
+        with open(path, "wb") as f:
+            f.write(head.tobytes())
+            f.write(toks.tobytes())
+            f.write(body.tobytes())
+
+    def load_prefix(self, path: str, model_path: Optional[str] = None) -> Optional[list]:
+        """Load a saved prefix made for this model and context size into the KV cache; returns its
+        tokens (then begin(len(tokens), ...) skips prefilling them), or None if the file does not
+        match."""
+        import os
+
+        if not os.path.exists(path):
+            return None
+        d = np.fromfile(path, dtype=np.uint8)
+        if d.size <= 48:
+            return None
+        head = d[:48].view(np.uint64)
+        if list(map(int, head[:5])) != self._prefix_key(model_path):
+            return None
+        n = int(head[5])
+        nb = int(self.lib.vp_prefix_bytes(self.ctx, n)) if 0 < n < self.max_ctx else 0
+        if nb == 0 or d.size != 48 + 4 * n + nb:
+            return None
+        toks = d[48:48 + 4 * n].view(np.int32).tolist()
+        body = np.ascontiguousarray(d[48 + 4 * n:])
+        check(self.lib.vp_load_prefix(self.ctx, n, body.ctypes.data, self._s), "vp_load_prefix")
+        torch.cuda.synchronize(self.device)
+        return toks
+
     def tokens(self, count: Optional[int] = None) -> list:
         st = self.state()
         count = st["step"] if count is None else count
@@ -215,15 +266,16 @@ class VerifyEngine:
 
     # ---- generate (Engine.generate, Engine.swift:922-1038) ----
     def generate(self, prompt, max_new: int, tree_fn: Optional[Callable] = None, eos=STOP_IDS,
-                 fused: bool = True) -> dict:
+                 fused: bool = True, cached: int = 0) -> dict:
         """Prefill `prompt`, then verify passes until max_new tokens or a stop token. tree_fn(out)
         returns the next pass's tree given the tokens committed so far (None: 1-row passes, i.e.
         plain greedy decoding through the same kernels, the reference's noDraft run). fused=False
-        runs each pass as verify + a separate commit launch instead of one pass launch."""
+        runs each pass as verify + a separate commit launch instead of one pass launch. cached: the
+        first `cached` prompt tokens are already in the KV cache (load_prefix) and not prefilled."""
         from .synth import root_tree
 
-        self.begin(0, max_new, eos)
-        self.prefill(prompt)
+        self.begin(cached, max_new, eos)
+        self.prefill(list(prompt)[cached:])
         st = self.state()
         passes = 0
         while not st["done"]:

@@ -155,6 +155,27 @@ def test_write_state_replays_a_pass(small):
         assert torch.equal(k1, k2) and torch.equal(v1, v2)
 
 
+def test_prefix_file_skips_prefill(small, tmp_path):
+    """Engine.savePrefix / loadPrefix: a fresh engine that loads a saved 32-token prefix and
+    prefills only the rest of the prompt decodes exactly the tokens of a full prefill."""
+    fmt, w, m, eng = small
+    if fmt != "q4":
+        pytest.skip("format independent")
+    prompt = (synth.make_prompt(40, seed=12) % VOCAB_SMALL).tolist()
+    full = eng.generate(prompt, 20)
+    path = str(tmp_path / "prefix.bin")
+    eng.save_prefix(path, prompt[:32])
+    other = _engine(w, max_ctx=512, max_steps=128)
+    assert other.load_prefix(path) == prompt[:32]
+    got = other.generate(prompt, 20, cached=32)
+    assert got["tokens"] == full["tokens"]
+    other.close()
+    # a file made for another context size (or model) is refused
+    third = _engine(w, max_ctx=256, max_steps=128)
+    assert third.load_prefix(path) is None
+    third.close()
+
+
 # ---------------------------------------------------------------------------------------------
 # full-size model
 
