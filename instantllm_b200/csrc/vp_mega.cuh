@@ -379,13 +379,16 @@ __device__ __forceinline__ bool mk_release(MkRing& rg, int k, int lane) {
 // memory.
 struct MkJobs {
   int piece0, rb0, nrb, P, ng;
-  int down;              // activations from global memory (down projection)
   const __half* actg;    // down projection: act blocks of the SiLU output
 };
+// What a stage's jobs are, fixed at compile time so that each stage's code holds only its own
+// loop (instruction-cache footprint): activations in shared memory and partial tiles out (QKV,
+// O, gate/up), activations streamed from global memory (down), or a running argmax (lm_head).
+enum MkJobKind { JOB_SMEM = 0, JOB_DOWN = 1, JOB_ARGMAX = 2 };
 
 // The ring state travels by value (registers) and comes back updated: x = pieces released (or -1
 // after a timeout), y = pieces seen full.
-template <int FMT>
+template <int FMT, int KIND>
 __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid4 = lane & 3;
@@ -396,7 +399,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
   float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
   int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
   const int piece0 = J.piece0, rb0 = J.rb0, nrb = J.nrb, P = J.P, ng = J.ng;
-  const bool down = J.down != 0;
+  constexpr bool down = KIND == JOB_DOWN;
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
   // jobs (row-block i, part q) -> warp (i * P + q) % 16, in increasing tile order per warp
@@ -406,7 +409,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
     const int i = j / P, q = j % P;
     const int ga = q * ng / P, gb = (q + 1) * ng / P;
     float acc[2][4] = {};
-    if (down) {
+    if constexpr (down) {
       // one tile per step, software-pipelined: the act block of tile g + 1 streams from L2 into
       // this warp's 2 KiB staging buffer (cp.async, each lane its own fragments) while tile g
       // computes; the first copy overlaps the wait for the weights
@@ -457,7 +460,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
       }
     }
     if (!ok) break;
-    if (P == 1) {
+    if constexpr (KIND == JOB_ARGMAX) {
       // lm_head: running best (value, lowest id) per token over this warp's row-blocks
       const int rb = rb0 + i;
       const int v0 = rb * 16 + gid, v1 = v0 + 8;
@@ -573,7 +576,7 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
 
 // One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
 // Returns false if a wait timed out.
-template <int FMT, int MODE>
+template <int FMT, int MODE, bool DOWN = false>
 __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
                         uint8_t* smem, volatile int* sAbort) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -589,7 +592,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   const int P = mk_parts(st, nrb), ng = mk_groups(st);
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
-  const bool down = st == MK_DOWN;
+  constexpr bool down = DOWN;
 #ifdef VP_TRACE_DETAIL
   const bool dtr = gp.layer == 5 || MODE == MODE_ARGMAX;
 #endif
@@ -657,8 +660,9 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
 
   const int npieces = (nrb * ng + tp - 1) / tp;
   MkJobs J;
-  J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.down = down ? 1 : 0; J.actg = gp.act;
-  const int2 rs2 = mk_jobs<FMT>(J, rg, smem);
+  J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.actg = gp.act;
+  constexpr int KIND = DOWN ? JOB_DOWN : MODE == MODE_ARGMAX ? JOB_ARGMAX : JOB_SMEM;
+  const int2 rs2 = mk_jobs<FMT, KIND>(J, rg, smem);
   bool ok = rs2.x >= 0;
   if (ok) rg.released = rs2.x;
   rg.waited = rs2.y;
@@ -672,7 +676,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   mk_sync();
   MK_DSTAMP(p, dtr, 256 + 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
-  if (P > 1) mk_epilogue<MODE>(gp, rb0, nrb, P, sPart, sRs, sEpc);
+  if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE>(gp, rb0, nrb, P, sPart, sRs, sEpc);
   MK_DSTAMP(p, dtr, 256 + 8 * st + 5);
   return true;
 }
@@ -811,7 +815,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.wnext = l + 1 < p.n_layers ? p.ln1[l + 1] : p.final_norm;
         gp.ss_out = s.ss; gp.act_out = s.act_h;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort) && barrier();
+        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_DOWN);
       }
       if (ok && p.do_lm) {
