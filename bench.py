@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
+                    help="config5: BASELINE config 5, independent requests sharded over the ranks")
+    ap.add_argument("--requests", type=int, default=256, help="config5: number of requests")
     return ap.parse_args()
 
 
@@ -262,6 +265,101 @@ def run_ours(args, rank, world, local):
                 counts=counts)
 
 
+GEN = 64  # config 5: tokens generated per request
+
+
+def run_config5(args, rank, world, local):
+    """BASELINE config 5 on this rank: its share of the requests (prefixes uniform in 128-2048,
+    shard.assign), each prefilled, decoded sequentially with 1-row passes (untimed: the true
+    continuation the seeded trees draft from), then decoded again with 16-row tree passes to 64
+    tokens. Only the tree passes are timed (CUDA events around each request's passes, all enqueued
+    at once from device-resident trees); the committed tokens are checked against the sequential
+    run (tree == sequential)."""
+    import torch
+
+    from instantllm_b200 import shard, synth
+    from instantllm_b200.engine import VerifyEngine
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    prefixes = shard.config5_requests(n=args.requests)
+    mine = shard.assign(prefixes, world)[rank]
+    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    eng = VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local)
+    no_eos = (-1, -1)
+    tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
+    s = eng.stream
+    dev_ms, tokens, passes, kv_slots, ok = 0.0, 0, 0, 0, True
+    for i in mine:
+        prompt = synth.make_prompt(prefixes[i], seed=5000 + i)
+        eng.begin(0, GEN + 9, no_eos)
+        eng.prefill(prompt)
+        snap = eng.snapshot()
+        for _ in range(GEN + 8):
+            eng.pass_device(tree1)
+        y = eng.tokens(GEN + 9)
+        # trees planned from the true continuation; the device follows the planned acceptances
+        trees, counts, pos = plan_trees(y, 1, 1, args.seed * 7 + i)
+        bufs, cnts = [trees[0]], [counts[0]]
+        while 1 + sum(cnts) < GEN:
+            t, c, _ = plan_trees(y, 1 + sum(cnts), 1, args.seed * 7 + i * 1009 + len(bufs))
+            bufs.append(t[0])
+            cnts.append(c[0])
+        tb = torch.tensor(np.stack(bufs), device=dev)
+        eng.restore(snap)  # back to the post-prefill state over the same cached prefix
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for k in range(len(bufs)):
+            eng.pass_device(tb[k])
+        e1.record(s)
+        torch.cuda.synchronize()
+        dev_ms += e0.elapsed_time(e1)
+        st = eng.state()
+        got = eng.tokens(st["step"])
+        ok = ok and got == y[:st["step"]] and st["step"] >= GEN
+        tokens += st["step"] - 1  # the first token comes from the prefill
+        passes += len(bufs)
+        kv_slots += sum(prefixes[i] + 1 + sum(cnts[:k]) + ROWS for k in range(len(bufs)))
+    eng.close()
+    return dict(ms=dev_ms, tok=tokens, passes=passes, kv_slots=kv_slots, ok=ok, n=len(mine))
+
+
+def main_config5(args, rank, world):
+    import torch
+
+    from instantllm_b200 import synth
+
+    r = run_config5(args, rank, world, int(os.environ.get("LOCAL_RANK", str(rank))))
+    wbytes = synth.weight_bytes("q4", args.layers)
+    gbs = (r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24) / (r["ms"] * 1e-3) / 1e9
+    vals = [r["ms"], float(r["tok"]), float(r["passes"]), 1.0 if r["ok"] else 0.0, gbs]
+    if world > 1:
+        rows = [torch.zeros(len(vals), dtype=torch.float64) for _ in range(world)]
+        torch.distributed.all_gather(rows, torch.tensor(vals, dtype=torch.float64))
+        table = [x.tolist() for x in rows]
+    else:
+        table = [vals]
+    if rank == 0:
+        ms = max(t[0] for t in table)
+        tok = sum(t[1] for t in table)
+        line = {
+            "metric": "config 5: aggregate accepted tok/s of independent q4 requests (16-row tree passes)",
+            "value": tok / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
+            "scaling": "strong", "requests": args.requests, "tokens": int(tok),
+            "passes": int(sum(t[2] for t in table)),
+            "ms_per_rank": [round(t[0], 3) for t in table],
+            "per_gpu_hbm_gbs": [round(t[4], 1) for t in table],
+            "tree_equals_sequential": all(t[3] > 0 for t in table),
+            "config": {"workload": "BASELINE config 5: requests with prefixes uniform in [128, 2048], "
+                                   "64 tokens each, seeded 16-row trees as in config 2, "
+                                   "longest-processing-time-first sharding (no collective)",
+                       "layers": args.layers, "timed": "tree passes only (device time, max over ranks)"},
+            "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
+        }
+        print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(w, prompt, y_full, trees, seconds: float) -> dict:
     """The oracle (numpy fp32 port of the reference CPU path) on a bounded sample of the same
     workload: tree passes over the same trees after the same 256-token prefix."""
@@ -363,6 +461,12 @@ def main():
         # requests are independent: no collective on the data path. gloo (host) carries only the
         # barrier around the timed region and the max / sum over ranks of the device timings.
         torch.distributed.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=300))
+    if args.workload == "config5":
+        main_config5(args, rank, world)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
     r = run_ours(args, rank, world, local)
     ms, tok = r["ms"], r["tok"]
     e2e_s, e2e_tok = r["e2e_s"], r["e2e_tok"]
