@@ -75,6 +75,8 @@ struct Scratch {
   __half* act_a;        // act blocks, K = 896: attention output for O
   __half* act_f;        // act blocks, K = 4864: SiLU(gate)*up for down
   float* ss;            // [HRB][16] per-row-block sums of squares of x (RMSNorm partials)
+  uint64_t* act_ll;     // O output for gate/up: act blocks as (half2, flag) words [H * 16 / 2]
+  uint64_t* ss_ll;      // its RMSNorm partials as (float, flag) words [HRB][16]
   float* part;          // split-K partial tiles [max units][16*16]
   int* tickets;         // split-K / attention arrival counters (self-resetting)
   float* att_part;      // attention split partials
@@ -117,6 +119,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// Flagged words: 32 bits of data and a 32-bit flag written by one 8-byte store, so that a reader
+// that sees the flag sees the data (no fence, no separate signal). Flags are unique per launch and
+// layer; a reader polls until every word it needs carries the current flag.
+__device__ __forceinline__ void st_flagged(uint64_t* p, uint32_t data, uint32_t flag) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((uint64_t)flag << 32) | data) : "memory");
+}
+__device__ __forceinline__ void ld_flagged2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long globaltimer() {

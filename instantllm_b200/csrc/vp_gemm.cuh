@@ -43,6 +43,11 @@ struct GemmParams {
   float* dbg;            // ARGMAX: optional full logits [16][nrb*16]
   float* xs;             // RESID: x[16 tokens][16 dims] of the row-block kept in shared memory by
                          // the CTA that owns it (persistent kernel), or null to use global x
+  uint64_t* act_ll_out;  // RESID (persistent kernel, O): flagged act blocks / partials instead of
+  uint64_t* ss_ll_out;   // act_out / ss_out
+  const uint64_t* act_ll_in;  // SILU (persistent kernel): flagged inputs instead of act / ss_in
+  const uint64_t* ss_ll_in;
+  uint32_t flag;         // flag of this launch and layer
   Scratch s;
 };
 

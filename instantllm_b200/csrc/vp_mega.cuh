@@ -100,6 +100,7 @@ struct MegaParams {
   int max_chunks;             // attention records (32-position sub-chunks) per (row, kv head)
   unsigned long long* bar;    // grid barrier arrival counter (0 at launch, reset by the last CTA)
   unsigned* exit_ctr;         // CTAs that finished this launch
+  unsigned* seq;              // launches so far: the flag of layer l is seq * 64 + l + 1
   unsigned long long* trace;  // CTA 0: %globaltimer after each stage (MK_TRACE entries)
   float* lm_pval;             // [16][gridDim] per-CTA argmax partials
   int* lm_pidx;
@@ -554,13 +555,25 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
         s.x[t * H + d1] = v1;
       }
       const float w0 = nrb == 1 ? sEpc[rp] : gp.wnext[d0], w1 = nrb == 1 ? sEpc[rp + 8] : gp.wnext[d1];
-      gp.act_out[act_index(t, d0)] = __float2half_rn(v0 * w0);
-      gp.act_out[act_index(t, d1)] = __float2half_rn(v1 * w1);
+      const __half h0 = __float2half_rn(v0 * w0), h1 = __float2half_rn(v1 * w1);
       float sq = v0 * v0 + v1 * v1;
       sq += __shfl_xor_sync(0xffffffffu, sq, 1);
       sq += __shfl_xor_sync(0xffffffffu, sq, 2);
       sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-      if (rp == 0) gp.ss_out[rb * 16 + t] = sq;
+      if (gp.act_ll_out) {
+        // columns (d, d + 1) of token t are one flagged word: the even lane takes its neighbour's
+        const uint32_t b0 = __half_as_ushort(h0), b1 = __half_as_ushort(h1);
+        const uint32_t n0 = __shfl_down_sync(0xffffffffu, b0, 1), n1 = __shfl_down_sync(0xffffffffu, b1, 1);
+        if ((rp & 1) == 0) {
+          st_flagged(gp.act_ll_out + act_index(t, d0) / 2, b0 | (n0 << 16), gp.flag);
+          st_flagged(gp.act_ll_out + act_index(t, d1) / 2, b1 | (n1 << 16), gp.flag);
+        }
+        if (rp == 0) st_flagged(gp.ss_ll_out + rb * 16 + t, __float_as_uint(sq), gp.flag);
+      } else {
+        gp.act_out[act_index(t, d0)] = h0;
+        gp.act_out[act_index(t, d1)] = h1;
+        if (rp == 0) gp.ss_out[rb * 16 + t] = sq;
+      }
     } else {  // MODE_SILU
       const int f = rb * 8 + rp;
       float h = 0.f;
@@ -571,6 +584,47 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
       }
       gp.act_out[act_index(t, f)] = __float2half_rn(h);
     }
+  }
+}
+
+// Flagged inputs of a stage (gate/up: the O projection's output): the act blocks (3,584 16-byte
+// units of two flagged words, 7 per thread) and the RMSNorm partials (448 units) go to shared
+// memory as soon as every word carries this layer's flag. The first round issues every load at
+// once; later rounds reload only what was not ready. Bounded: a timeout sets the error bit.
+constexpr int MK_LL_UNITS = (int)(MK_ACT_BYTES / 8 / MK_CONS);  // act units (8 data bytes) per thread
+static_assert(MK_LL_UNITS * MK_CONS * 8 == MK_ACT_BYTES, "flagged act units split evenly");
+__device__ __noinline__ void mk_poll_flagged(const uint64_t* act_ll, const uint64_t* ss_ll, uint32_t F,
+                                             uint8_t* sAct, float* sSs, vp_state* st, volatile int* sAbort) {
+  const int tid = threadIdx.x;
+  const bool has_ss = tid < HRB * 16 / 2;
+  uint32_t pending = (1u << MK_LL_UNITS) - 1u | (has_ss ? 1u << MK_LL_UNITS : 0u);
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 0; pending && it < (1u << 24); ++it) {
+#pragma unroll
+    for (int k = 0; k < MK_LL_UNITS; ++k) {
+      if (!(pending >> k & 1u)) continue;
+      const int u = tid + k * MK_CONS;
+      uint64_t a, b;
+      ld_flagged2(act_ll + 2 * u, a, b);
+      if ((uint32_t)(a >> 32) == F && (uint32_t)(b >> 32) == F) {
+        reinterpret_cast<uint2*>(sAct)[u] = make_uint2((uint32_t)a, (uint32_t)b);
+        pending &= ~(1u << k);
+      }
+    }
+    if (pending >> MK_LL_UNITS & 1u) {
+      uint64_t a, b;
+      ld_flagged2(ss_ll + 2 * tid, a, b);
+      if ((uint32_t)(a >> 32) == F && (uint32_t)(b >> 32) == F) {
+        sSs[2 * tid] = __uint_as_float((uint32_t)a);
+        sSs[2 * tid + 1] = __uint_as_float((uint32_t)b);
+        pending &= ~(1u << MK_LL_UNITS);
+      }
+    }
+    if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+  }
+  if (pending) {
+    set_error(st, VP_DEV_ERR_TIMEOUT);
+    *sAbort = 1;
   }
 }
 
@@ -604,10 +658,10 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   float* sEpc = reinterpret_cast<float*>(smem + MK_OFF_EPC);
   {
     const uint64_t pol = policy_evict_last();
-    if (!down)
+    if (!down && !gp.act_ll_in)
       for (int i = threadIdx.x; i < (int)(MK_ACT_BYTES / 16); i += MK_CONS)
         cp_async16(sAct + (size_t)i * 16, reinterpret_cast<const uint4*>(gp.act) + i, 16u, pol);
-    if (MODE != MODE_RESID && threadIdx.x < HRB * 16 / 4)
+    if (MODE != MODE_RESID && !gp.act_ll_in && threadIdx.x < HRB * 16 / 4)
       cp_async16(sSs + threadIdx.x * 4, gp.ss_in + threadIdx.x * 4, 16u, pol);
     cp_async_commit();
     // constants of the epilogue (QKV bias and RoPE rotations, the next RMSNorm's weights) load
@@ -625,6 +679,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
       if (nrb == 1 && threadIdx.x < 16) sEpc[threadIdx.x] = gp.wnext[rb0 * 16 + threadIdx.x];
     }
     cp_async_wait<0>();
+    if (gp.act_ll_in) mk_poll_flagged(gp.act_ll_in, gp.ss_ll_in, gp.flag, sAct, sSs, gp.s.st, sAbort);
   }
   mk_sync();
   MK_DSTAMP(p, dtr, 256 + 8 * st + 1);
@@ -753,6 +808,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
     mk_sync();
     Scratch s = p.s;
     s.ri = sRi;
+    const uint32_t flag0 = __ldcg(p.seq) * 64u + 1u;  // flag of layer 0 in this launch
     const bool live = ok && sRi->live != 0;
     MkRing rg;
     rg.base = smem;
@@ -795,16 +851,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp = GemmParams{};
         gp.s = s; gp.layer = l;
         gp.w = p.wo[l]; gp.act = s.act_a; gp.nrb = H / 16; gp.ng = H / GS;
-        gp.wnext = p.ln2[l]; gp.ss_out = s.ss; gp.act_out = s.act_h;
+        gp.wnext = p.ln2[l];
+        gp.act_ll_out = s.act_ll; gp.ss_ll_out = s.ss_ll; gp.flag = flag0 + l;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort) && barrier();
+        // no grid barrier: gate/up polls the flagged words it needs (every CTA passed the
+        // attention barrier, so no reader of the previous layer's words is left)
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort);
         piece0 += pieces(MK_O);
         if (!ok) break;
         // gate/up + SiLU
         gp = GemmParams{};
         gp.s = s; gp.layer = l;
         gp.w = p.wgu[l]; gp.act = s.act_h; gp.nrb = 2 * F / 16; gp.ng = H / GS;
-        gp.ss_in = s.ss; gp.act_out = s.act_f;
+        gp.act_ll_in = s.act_ll; gp.ss_ll_in = s.ss_ll; gp.flag = flag0 + l; gp.act_out = s.act_f;
         ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort) && barrier();
         piece0 += pieces(MK_GU);
         if (!ok) break;
@@ -856,6 +915,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
     if (atomicAdd(p.exit_ctr, 1u) == (unsigned)G - 1) {
       *p.bar = 0ull;  // every CTA is past its last barrier: the next launch starts from zero
       *p.exit_ctr = 0u;
+      *p.seq = *p.seq + 1u;  // the next launch's flags differ from every word written here
       __threadfence();
     }
   }

@@ -69,6 +69,7 @@ struct vp_ctx {
   int max_chunks = 0;
   unsigned long long* bar = nullptr;
   unsigned* exit_ctr = nullptr;
+  unsigned* seq = nullptr;  // pass-kernel launches so far (flag epochs)
   float* lm_pval = nullptr;  // [16][grid] per-CTA argmax partials of the last pass
   int* lm_pidx = nullptr;
   unsigned long long* trace = nullptr;  // stage timestamps of the last pass (ns)
@@ -138,6 +139,7 @@ MegaParams mega_params(vp_ctx* c) {
   p.max_chunks = c->max_chunks;
   p.bar = c->bar;
   p.exit_ctr = c->exit_ctr;
+  p.seq = c->seq;
   p.lm_pval = c->lm_pval;
   p.lm_pidx = c->lm_pidx;
   p.trace = c->trace;
@@ -260,6 +262,9 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &s.pidx, (size_t)ROWS * (cfg->vocab / 16) * sizeof(int))) ||
       (r = dalloc(c, &c->bar, sizeof(unsigned long long))) ||
       (r = dalloc(c, &c->exit_ctr, sizeof(unsigned))) ||
+      (r = dalloc(c, &c->seq, sizeof(unsigned))) ||
+      (r = dalloc(c, &s.act_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.ss_ll, (size_t)HRB * ROWS * sizeof(uint64_t))) ||
       (r = dalloc(c, &c->lm_pval, (size_t)ROWS * sms * sizeof(float))) ||
       (r = dalloc(c, &c->lm_pidx, (size_t)ROWS * sms * sizeof(int))) ||
       (r = dalloc(c, &c->trace, MK_TRACE * sizeof(unsigned long long)))) {
