@@ -492,7 +492,9 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int r = 0; r < 4; ++r)
-          part[(gid + 8 * (r >> 1)) * 16 + nt * 8 + 2 * tid4 + (r & 1)] = acc[nt][r];
+          // [row half][token][row & 7]: the epilogue's lanes (8 rows of a token, 4 tokens per
+          // warp) then read 32 consecutive words, free of bank conflicts
+          part[(r >> 1) * 128 + (nt * 8 + 2 * tid4 + (r & 1)) * 8 + gid] = acc[nt][r];
     }
   }
   return make_int2(ok ? rg.released : -1, rg.waited);
@@ -513,8 +515,8 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
     float s0 = 0.f, s1 = 0.f;
     const float* part = sPart + i * P * 256;
     for (int q = 0; q < P; ++q) {
-      s0 += part[q * 256 + rp * 16 + t];
-      s1 += part[q * 256 + (rp + 8) * 16 + t];
+      s0 += part[q * 256 + t * 8 + rp];
+      s1 += part[q * 256 + 128 + t * 8 + rp];
     }
     if constexpr (MODE == MODE_QKV) {
       const int head = rb >> 2, d = (rb & 3) * 8 + rp;
