@@ -240,12 +240,17 @@ __device__ __forceinline__ uint32_t kv_off(int r, int k) { return (uint32_t)(r *
 // One warp: sub-chunk c (virtual positions 32c..32c+31) of row t, kv head g, staged in buf
 // (K rows then V rows). Writes the record to rec (the K rows of buf).
 // kc, vc: the (layer, kv head) K and V caches; q: query row t (all heads).
-__device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, const __half* vc,
+// The pass's own rows (this row's ancestors, slots >= pos) and the query come from the flagged
+// copies the QKV epilogue wrote (qw: row t's queries, kw / vw: kv head g's K / V rows of the pass),
+// polled until they carry `flag`; the cached prefix comes from the KV cache.
+__device__ __noinline__ void attn_warp(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, uint32_t flag,
+                                       vp_state* st, const __half* kc, const __half* vc,
                                        const RowInfo* ri, int t, int g, int c, __half* buf, float* rec,
                                        unsigned long long* tr) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
   if (tr && lane == 0) tr[0] = globaltimer();
   const int pos = ri->pos, L = pos + ri->depth[t] + 1;
+  bool late = false;  // a poll gave up (bounded wait): error bit set, zeros used
   // stage the K rows, then the V rows (two cp.async groups: S starts once K has landed, V keeps
   // arriving behind it): lane copies 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8;
   // positions past the row are zeros
@@ -255,32 +260,95 @@ __device__ __noinline__ void attn_warp(const float* qrow, const __half* kc, cons
     uint8_t* dk = reinterpret_cast<uint8_t*>(buf);
     size_t src[8];
     uint32_t nb[8];
+    int prow[8];     // pass row of position r (an ancestor) or -1 (cached slot or past the row)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int r = (lane >> 3) + 4 * k, jv = c * ATT_SUB + r;
       const bool valid = jv < L;
-      const int slot = !valid ? 0 : jv < pos ? jv : pos + ri->path[t][min(jv - pos, ROWS - 1)];
-      src[k] = (size_t)slot * HD + ch * 8;
+      prow[k] = valid && jv >= pos ? ri->path[t][min(jv - pos, ROWS - 1)] : -1;
+      src[k] = (size_t)(valid && jv < pos ? jv : 0) * HD + ch * 8;
       nb[k] = valid ? 16u : 0u;
-      cp_async16(dk + kv_off(r, ch), kc + src[k], nb[k], pol);
+      if (prow[k] < 0) cp_async16(dk + kv_off(r, ch), kc + src[k], nb[k], pol);
     }
     cp_async_commit();
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      cp_async16(dk + ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch), vc + src[k], nb[k], pol);
+      if (prow[k] < 0) cp_async16(dk + ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch), vc + src[k], nb[k], pol);
     cp_async_commit();
+    // the pass's rows: 16-byte chunk ch of the row = flagged words 4ch .. 4ch + 3
+    uint32_t pend = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (prow[k] >= 0) pend |= 3u << (2 * k);  // bit 2k: K, 2k + 1: V
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          if (!(pend >> (2 * k + kv) & 1u)) continue;
+          const uint64_t* w = (kv ? vw : kw) + (size_t)prow[k] * (HD / 2) + 4 * ch;
+          uint64_t a0, a1, a2, a3;
+          ld_flagged2(w, a0, a1);
+          ld_flagged2(w + 2, a2, a3);
+          if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag && (uint32_t)(a2 >> 32) == flag &&
+              (uint32_t)(a3 >> 32) == flag) {
+            *reinterpret_cast<uint4*>(dk + kv * ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch)) =
+                make_uint4((uint32_t)a0, (uint32_t)a1, (uint32_t)a2, (uint32_t)a3);
+            pend &= ~(1u << (2 * k + kv));
+          }
+        }
+      if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+    }
+    if (pend) {
+      late = true;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv)
+          if (pend >> (2 * k + kv) & 1u)
+            *reinterpret_cast<uint4*>(dk + kv * ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch)) =
+                make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero)
   uint32_t qa[4][2][2];  // [k-step][hi, lo][a0, a2]
   {
-    const float* q = qrow + (g * GQ + min(gid, GQ - 1)) * HD;
+    // dims ks * 16 + 2 t4 + {0, 1} and + 8: two flagged words per 16-byte load
+    const uint64_t* q = qw + (g * GQ + min(gid, GQ - 1)) * HD;
+    float x[4][4];
+    uint32_t pend = 0xffu;  // bit 2 ks + half
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!(pend >> (2 * ks + hh) & 1u)) continue;
+          uint64_t a0, a1;
+          ld_flagged2(q + ks * 16 + 2 * t4 + 8 * hh, a0, a1);
+          if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag) {
+            x[ks][2 * hh] = __uint_as_float((uint32_t)a0);
+            x[ks][2 * hh + 1] = __uint_as_float((uint32_t)a1);
+            pend &= ~(1u << (2 * ks + hh));
+          }
+        }
+      if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+    }
+    if (pend) {
+      late = true;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (pend >> (2 * ks + (i >> 1)) & 1u) x[ks][i] = 0.f;
+    }
+    if (__any_sync(0xffffffffu, late) && lane == 0) set_error(st, VP_DEV_ERR_TIMEOUT);
     const float z = gid < GQ ? ATTN_SCALE : 0.f;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      const float2 x0 = __ldcg(reinterpret_cast<const float2*>(q + ks * 16 + 2 * t4));
-      const float2 x2 = __ldcg(reinterpret_cast<const float2*>(q + ks * 16 + 2 * t4 + 8));
-      split_half2(x0.x * z, x0.y * z, qa[ks][0][0], qa[ks][1][0]);
-      split_half2(x2.x * z, x2.y * z, qa[ks][0][1], qa[ks][1][1]);
+      split_half2(x[ks][0] * z, x[ks][1] * z, qa[ks][0][0], qa[ks][1][0]);
+      split_half2(x[ks][2] * z, x[ks][3] * z, qa[ks][0][1], qa[ks][1][1]);
     }
   }
   if (tr && lane == 0) tr[1] = globaltimer_after(__uint_as_float(qa[3][1][1]));
@@ -389,8 +457,10 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, Attn
   float* rec0 = reinterpret_cast<float*>(&sm.kv[0][0][0][0]);
   if (c0 + warp < c1) {
     const size_t cache = (size_t)(layer * NKV + g) * s.max_ctx * HD;
-    attn_warp(s.q + t * H, s.kc + cache, s.vc + cache, ri, t, g, c0 + warp, &sm.kv[warp][0][0][0],
-              rec0 + warp * ATT_REC_STRIDE, trace ? trace + 8 + 8 * warp : nullptr);
+    const size_t kvw = (size_t)ROWS * (HD / 2);
+    attn_warp(s.q_ll + t * H, s.kv_ll + g * kvw, s.kv_ll + (NKV + g) * kvw, s.flag_q, s.st, s.kc + cache,
+              s.vc + cache, ri, t, g, c0 + warp, &sm.kv[warp][0][0][0], rec0 + warp * ATT_REC_STRIDE,
+              trace ? trace + 8 + 8 * warp : nullptr);
   }
   cons_sync();
   tstamp();

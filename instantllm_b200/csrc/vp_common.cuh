@@ -77,6 +77,9 @@ struct Scratch {
   float* ss;            // [HRB][16] per-row-block sums of squares of x (RMSNorm partials)
   uint64_t* act_ll;     // O output for gate/up: act blocks as (half2, flag) words [H * 16 / 2]
   uint64_t* ss_ll;      // its RMSNorm partials as (float, flag) words [HRB][16]
+  uint64_t* q_ll;       // QKV output for the attention: roped queries as (float, flag) [16][896]
+  uint64_t* kv_ll;      // and the pass rows' K / V as (half2, flag) words [K, V][kv head][16][32]
+  uint32_t flag_q;      // flag of q_ll / kv_ll in this launch and layer
   float* part;          // split-K partial tiles [max units][16*16]
   int* tickets;         // split-K / attention arrival counters (self-resetting)
   float* att_part;      // attention split partials

@@ -520,25 +520,42 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
     }
     if constexpr (MODE == MODE_QKV) {
       const int head = rb >> 2, d = (rb & 3) * 8 + rp;
+      float a = 0.f, b = 0.f;
       if (t < n) {
         // nrb == 1 for QKV (one CTA per row-block): bias and rotations are in shared memory
-        float a = s0 * rs[t] + sEpc[rp];
-        float b = s1 * rs[t] + sEpc[8 + rp];
+        a = s0 * rs[t] + sEpc[rp];
+        b = s1 * rs[t] + sEpc[8 + rp];
         if (head < NQ + NKV) {
           const float2 cs = reinterpret_cast<const float2*>(sEpc + 16)[lt];
           const float a2 = a * cs.x - b * cs.y;
           const float b2 = b * cs.x + a * cs.y;
           a = a2; b = b2;
         }
-        if (head < NQ) {
+      }
+      // the attention polls flagged copies (no grid barrier between QKV and attention); the
+      // plain q and the KV cache stay the record that later passes and the debug buffers read
+      if (head < NQ) {  // uniform over the CTA (one row-block)
+        if (t < n) {
           s.q[t * H + head * HD + d] = a;
           s.q[t * H + head * HD + d + 32] = b;
-        } else {
-          const int kvh = head < NQ + NKV ? head - NQ : head - NQ - NKV;
-          __half* c = head < NQ + NKV ? s.kc : s.vc;
-          __half* row = c + ((size_t)(gp.layer * NKV + kvh) * s.max_ctx + ri->pos + t) * HD;
-          row[d] = __float2half_rn(a);
-          row[d + 32] = __float2half_rn(b);
+          st_flagged(s.q_ll + t * H + head * HD + d, __float_as_uint(a), s.flag_q);
+          st_flagged(s.q_ll + t * H + head * HD + d + 32, __float_as_uint(b), s.flag_q);
+        }
+      } else {
+        const int kind = head < NQ + NKV ? 0 : 1, kvh = kind == 0 ? head - NQ : head - NQ - NKV;
+        const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+        if (t < n) {
+          __half* row = (kind == 0 ? s.kc : s.vc) + ((size_t)(gp.layer * NKV + kvh) * s.max_ctx + ri->pos + t) * HD;
+          row[d] = ha;
+          row[d + 32] = hb;
+        }
+        // dims (d, d + 1) are one flagged word: the even lane takes its neighbour's half
+        const uint32_t ua = __half_as_ushort(ha), ub = __half_as_ushort(hb);
+        const uint32_t na = __shfl_down_sync(0xffffffffu, ua, 1), nb = __shfl_down_sync(0xffffffffu, ub, 1);
+        if (t < n && (rp & 1) == 0) {
+          uint64_t* w = s.kv_ll + ((size_t)(kind * NKV + kvh) * ROWS + t) * (HD / 2);
+          st_flagged(w + d / 2, ua | (na << 16), s.flag_q);
+          st_flagged(w + (d + 32) / 2, ub | (nb << 16), s.flag_q);
         }
       }
     } else if constexpr (MODE == MODE_RESID) {
@@ -833,9 +850,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         // QKV (+ RMSNorm scale, bias, RoPE, KV write)
         gp.w = p.wqkv[l]; gp.act = s.act_h; gp.nrb = QKV / 16; gp.ng = H / GS;
         gp.bias = p.bqkv[l]; gp.ss_in = s.ss;
-        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort) && barrier();
+        gp.s.flag_q = flag0 + l;
+        // no grid barrier: the attention units poll the flagged q and K / V rows they need (every
+        // CTA passed the barrier after the previous down projection, so the previous layer's
+        // words have no reader left)
+        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort);
         piece0 += pieces(MK_QKV);
         if (!ok) break;
+        s.flag_q = flag0 + l;
         // attention
         {
           const int units = attn_units(sRi);

@@ -265,6 +265,8 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &c->seq, sizeof(unsigned))) ||
       (r = dalloc(c, &s.act_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
       (r = dalloc(c, &s.ss_ll, (size_t)HRB * ROWS * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.q_ll, (size_t)ROWS * H * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.kv_ll, (size_t)2 * NKV * ROWS * (HD / 2) * sizeof(uint64_t))) ||
       (r = dalloc(c, &c->lm_pval, (size_t)ROWS * sms * sizeof(float))) ||
       (r = dalloc(c, &c->lm_pidx, (size_t)ROWS * sms * sizeof(int))) ||
       (r = dalloc(c, &c->trace, MK_TRACE * sizeof(unsigned long long)))) {
