@@ -102,6 +102,14 @@ class VerifyEngine:
         self._keep.append(t)
         return t.data_ptr()
 
+    @classmethod
+    def from_ill(cls, path: str, **kw) -> "VerifyEngine":
+        """An engine on the weights of an .ill model file (Engine.init(modelPath:), Engine.swift:71):
+        the file is read into the standard layouts (ill.read_ill) and packed for the tensor cores."""
+        from .ill import read_ill
+
+        return cls(read_ill(path), **kw)
+
     def close(self) -> None:
         if getattr(self, "ctx", None):
             self.lib.vp_destroy(self.ctx)
