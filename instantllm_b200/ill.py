@@ -118,9 +118,10 @@ def _f32(a) -> bytes:
 # container (ModelFile.swift:62-144: ModelFile and ModelWriter)
 
 
-def write_ill(path: str, weights: dict) -> None:
+def write_ill(path: str, weights: dict, embed_hi: Optional[np.ndarray] = None) -> None:
     """Write standard-layout weights (synth.make_weights / read_ill) as an .ill file, rows reordered
-    the way the reference's converter stores them."""
+    the way the reference's converter stores them; embed_hi: the optional 2-bit sketch of a q4
+    embedding (convert.sketch_q4), stored as tensor 291."""
     fmt = weights["fmt"]
     if fmt not in FORMATS:
         raise ValueError(f"the .ill container holds q4, q8g32 or f16 weights, not {fmt}")
@@ -138,6 +139,8 @@ def write_ill(path: str, weights: dict) -> None:
         blobs[layer_id(l, WO)], blobs[layer_id(l, WO_SB)] = _matrix_tensors(L["wo"], None)
         blobs[layer_id(l, WGU)], blobs[layer_id(l, WGU_SB)] = _matrix_tensors(L["wgu"], go)
         blobs[layer_id(l, WD)], blobs[layer_id(l, WD_SB)] = _matrix_tensors(L["wd"], None)
+    if embed_hi is not None:
+        blobs[EMBED_HI] = np.ascontiguousarray(embed_hi, dtype=np.uint8).tobytes()
     table = np.zeros(2 * COUNT, dtype=np.uint64)
     cursor = HEADER_BYTES
     layout = []
