@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
-                    help="config5: BASELINE config 5, independent requests sharded over the ranks")
+    ap.add_argument("--workload", choices=["config2", "config5", "sketch_head"], default="config2",
+                    help="config5: BASELINE config 5, independent requests sharded over the ranks; "
+                         "sketch_head: the optional two-stage lm_head against the full one (1 GPU)")
     ap.add_argument("--requests", type=int, default=256, help="config5: number of requests")
     return ap.parse_args()
 
@@ -446,6 +447,75 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def main_sketch(args):
+    """The optional two-stage sketch lm_head (instantllm_b200.sketch) against the full q4 lm_head
+    (vp_head_argmax_noalloc) at the full vocabulary, 1, 4, 8 and 16 rows: device time per call with
+    L2 flushed before each call (the q4 embedding, 76.6 MB, fits in the 126 MB L2)."""
+    import torch
+
+    from instantllm_b200 import _lib, synth
+    from instantllm_b200.engine import VerifyEngine
+    from instantllm_b200.sketch import SketchHead
+
+    w = synth.make_weights("q4", n_layers=1, seed=args.seed)
+    rng = np.random.default_rng(args.seed + 1)
+    w["final_norm"] = rng.normal(1.0, 0.1, synth.HIDDEN).astype(np.float32)
+    eng = VerifyEngine(w, max_ctx=64, max_steps=8)
+    sk = SketchHead(eng, codes=w["embed"]["codes"])
+    V, s = eng.vocab, eng.stream
+    x = torch.from_numpy(synth.head_rows(w["embed"], w["final_norm"], rng, 16)).to(eng.device)
+    tok = torch.empty(16, dtype=torch.int32, device=eng.device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=eng.device)
+    ws = eng._weights_struct
+
+    def full(rows):
+        _lib.check(eng.lib.vp_head_argmax_noalloc(_lib.FMT["q4"], V, ws.embed, ws.final_norm, x.data_ptr(),
+                                                  rows, tok.data_ptr(), s.cuda_stream), "noalloc")
+
+    def sketch(rows):
+        sk.argmax_device(x, rows)
+
+    def timed(fn, rows):
+        for _ in range(args.warmup):
+            fn(rows)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for a, b in ev:
+            flush.fill_(1)
+            a.record(s)
+            fn(rows)
+            b.record(s)
+        torch.cuda.synchronize()
+        return float(np.median([a.elapsed_time(b) for a, b in ev])) * 1000.0
+
+    hbm_peak, peak_kind = peaks()
+    sk_bytes = V // 16 * 14 * (256 + 64)  # sketch tiles + the q4 tiles' scale blocks
+    full_bytes = V // 16 * 14 * 576
+    res = []
+    for rows in (1, 4, 8, 16):
+        sketch(rows)
+        got = sk.argmax(x, rows)
+        full(rows)
+        torch.cuda.synchronize()
+        same = bool(np.array_equal(got, tok[:rows].cpu().numpy()))
+        tf, ts = timed(full, rows), timed(sketch, rows)
+        c0, call = sk.last_candidates()
+        res.append({"rows": rows, "full_us": round(tf, 2), "sketch_us": round(ts, 2),
+                    "speedup": round(tf / ts, 3), "same_tokens": same, "cand_groups_row0": c0,
+                    "cand_groups_any": call,
+                    "full_hbm_gbs": round(full_bytes / (tf * 1e-6) / 1e9, 1),
+                    "sketch_stream_gbs": round(sk_bytes / (ts * 1e-6) / 1e9, 1)})
+    line = {"metric": "lm_head latency: two-stage sketch head vs full q4 head (median device us per call)",
+            "value": res[0]["sketch_us"], "unit": "us", "higher_is_better": False, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "rows": res,
+            "config": {"workload": "tied q4 lm_head, vocab 151936, rows mixing embedding rows + noise "
+                                   "(clear winners, close runners-up), K = 6", "l2": "flushed before each call"},
+            "peak_gbs": hbm_peak, "peak_kind": peak_kind,
+            "data": "synthetic (seeded random-init q4 embedding)"}
+    print(json.dumps(line), flush=True)
+    eng.close()
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -461,6 +531,9 @@ def main():
         # requests are independent: no collective on the data path. gloo (host) carries only the
         # barrier around the timed region and the max / sum over ranks of the device timings.
         torch.distributed.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=300))
+    if args.workload == "sketch_head":
+        main_sketch(args)
+        return
     if args.workload == "config5":
         main_config5(args, rank, world)
         if world > 1:

@@ -217,6 +217,36 @@ int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void* d_embed,
                            const float* d_final_norm, const float* d_x, int32_t rows,
                            int32_t* d_tokens, void* stream);
 
+/* ---- two-stage lm-head over a 2-bit sketch (q4 only; probabilistic, off by default) ----
+ * Replaces Engine.encodeSketchHead (Sources/Engine/Engine.swift:436-454) and the kernels
+ * k_lmh_sketch_T / k_lmh_tau / k_lmh_exact_T (Shaders.swift:1377-1523). Stage 1 scores every
+ * vocabulary row from the high two bits of its q4 codes with an uncertainty sigma for the dropped
+ * low bits, and keeps per 32-row group the max of A - K sigma and A + K sigma; stage 2 recomputes
+ * exact logits only in the groups whose upper bound reaches tau = max lower bound. The recomputed
+ * logits are bit-identical to vp_head_argmax_noalloc's, so tokens[r] equals its token unless a
+ * residual exceeds k_sigma sigma (the reference's default K is 6).
+ *   hi       the reference's sketch plane (.ill tensor 291): uint8 [vocab][224], byte c holding
+ *            codes 4c .. 4c+3 >> 2 (code 4c in bits 0-1); vp_pack_sketch packs it for the GPU
+ *            into vp_sketch_bytes(vocab) bytes (device buffers, 16-byte aligned).
+ *   embed    the packed q4 embedding (vp_pack_matrix, VP_FMT_Q4, VP_MAT_PLAIN)
+ *   x        fp32 [rows][896] residual rows; tokens int32 [rows] (device)
+ *   work     caller-owned device scratch of vp_sketch_work_bytes(vocab) bytes, 256-byte aligned:
+ *            fp16 normed rows, RMSNorm partials, state, tau, the group bounds fp32 [2][16][ngrp]
+ *            (ngrp = ceil(vocab / 32); lower bounds first) at offset vp_sketch_bounds_offset().
+ *            Calls that share a work buffer must not overlap on the GPU.
+ * Three launches: normed rows, stage 1 over every group, stage 2 over the candidates (its last CTA
+ * writes tokens and ncand).
+ *   ncand    optional int32[2] (device): groups that were candidates for row 0, for any row.
+ *   limits   vocab a positive multiple of 16; 1 <= rows <= VP_MAX_ROWS; k_sigma > 0. */
+size_t vp_sketch_bytes(int32_t vocab);
+int vp_pack_sketch(int32_t vocab, const void* d_hi, void* d_out, void* stream);
+size_t vp_sketch_work_bytes(int32_t vocab);
+size_t vp_sketch_bounds_offset(void);
+int vp_head_argmax_sketch(int32_t vocab, const void* d_embed, const void* d_sketch,
+                          const float* d_final_norm, const float* d_x, int32_t rows, float k_sigma,
+                          void* d_work, size_t work_bytes, int32_t* d_tokens, int32_t* d_ncand,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,8 @@ EXPORTS = (
     "vp_pass", "vp_read_state", "vp_write_state", "vp_prefix_bytes", "vp_save_prefix", "vp_load_prefix",
     "vp_read_tokens", "vp_device_tokens", "vp_device_state",
     "vp_debug_logits", "vp_buffer", "vp_head_argmax_noalloc",
+    "vp_sketch_bytes", "vp_pack_sketch", "vp_sketch_work_bytes", "vp_sketch_bounds_offset",
+    "vp_head_argmax_sketch",
 )
 
 
@@ -90,6 +92,11 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_debug_logits": (ctypes.c_int, [vp, vp, vp]),
         "vp_buffer": (ctypes.c_int, [vp, i32, ctypes.POINTER(vp), ctypes.POINTER(sz)]),
         "vp_head_argmax_noalloc": (ctypes.c_int, [i32, i32, vp, vp, vp, i32, vp, vp]),
+        "vp_sketch_bytes": (sz, [i32]),
+        "vp_pack_sketch": (ctypes.c_int, [i32, vp, vp, vp]),
+        "vp_sketch_work_bytes": (sz, [i32]),
+        "vp_sketch_bounds_offset": (sz, []),
+        "vp_head_argmax_sketch": (ctypes.c_int, [i32, vp, vp, vp, vp, i32, ctypes.c_float, vp, sz, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -61,15 +61,28 @@ __host__ inline size_t gemm_smem_bytes(int fmt, int ng, int nsplit, int cg) {
   return b;
 }
 
+// A fragments of one 16-column k-step from a lane's 32-bit word of a q4 tile.
+__device__ __forceinline__ void q4_frags(uint32_t v, uint32_t (&a)[4]) {
+  const uint32_t v8 = v >> 8;
+  a[0] = v & 0x000F000Fu;   // row gid,   codes * 2^-24
+  a[1] = v & 0x00F000F0u;   // row gid+8, codes * 2^-20
+  a[2] = v8 & 0x000F000Fu;
+  a[3] = v8 & 0x00F000F0u;
+}
+
+// Per-row (gid, gid+8) affine constants of a q4 tile from the lane's 8 bytes of its scale block:
+// y += sf * acc + sb * X.
+__device__ __forceinline__ void q4_fold(uint2 v, float (&sf)[2], float (&sb)[2]) {
+  const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  sf[0] = p0.x * 16777216.f; sb[0] = p0.y;   // codes of row gid are code * 2^-24
+  sf[1] = p1.x * 1048576.f;  sb[1] = p1.y;   // codes of row gid+8 are code * 2^-20
+}
+
 template <int FMT>
 __device__ __forceinline__ void load_a_frags(const uint8_t* tile, int lane, int j, uint32_t (&a)[4]) {
   if constexpr (FMT == VP_FMT_Q4) {
-    const uint32_t v = reinterpret_cast<const uint32_t*>(tile + lane * 16)[j];
-    const uint32_t v8 = v >> 8;
-    a[0] = v & 0x000F000Fu;   // row gid,   codes * 2^-24
-    a[1] = v & 0x00F000F0u;   // row gid+8, codes * 2^-20
-    a[2] = v8 & 0x000F000Fu;
-    a[3] = v8 & 0x00F000F0u;
+    q4_frags(reinterpret_cast<const uint32_t*>(tile + lane * 16)[j], a);
   } else if constexpr (fmt_is_q8(FMT)) {
     const uint2 v = reinterpret_cast<const uint2*>(tile + lane * 32)[j];
     const uint32_t u0 = v.x ^ 0x80808080u, u1 = v.y ^ 0x80808080u;  // q + 128 in 1..255
@@ -100,11 +113,7 @@ template <int FMT>
 __device__ __forceinline__ void load_fold(const uint8_t* tile, int gid, float (&sf)[2], float (&sb)[2]) {
   static_assert(!fmt_halves(FMT), "q8g32 tiles fold per half (load_fold_halves)");
   if constexpr (FMT == VP_FMT_Q4) {
-    const uint2 v = *reinterpret_cast<const uint2*>(tile + 512 + gid * 8);
-    const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-    const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-    sf[0] = p0.x * 16777216.f; sb[0] = p0.y;   // codes of row gid are code * 2^-24
-    sf[1] = p1.x * 1048576.f;  sb[1] = p1.y;   // codes of row gid+8 are code * 2^-20
+    q4_fold(*reinterpret_cast<const uint2*>(tile + 512 + gid * 8), sf, sb);
   } else if constexpr (FMT == VP_FMT_Q8) {
     const uint32_t v = *reinterpret_cast<const uint32_t*>(tile + 1024 + gid * 4);
     const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&v));

@@ -6,6 +6,7 @@
 // (vp_mega.cuh), one CTA per SM, stages separated by grid barriers.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -16,6 +17,7 @@
 #include "vp_commit.cuh"
 #include "vp_gemm.cuh"
 #include "vp_mega.cuh"
+#include "vp_sketch.cuh"
 
 using namespace vp;
 
@@ -527,8 +529,8 @@ namespace {
 
 // x rows -> half(x * final_norm) act blocks and per-row-block sums of squares, with the same
 // expressions and reduction order as the residual epilogue that feeds the pass's own lm_head.
-__global__ void k_na_prep(const float* x, const float* wnorm, int rows, __half* act, float* ss,
-                          vp_state* st, RowInfo* ri) {
+__device__ void na_prep_body(const float* x, const float* wnorm, int rows, __half* act, float* ss,
+                             vp_state* st, RowInfo* ri) {
   const int rb = blockIdx.x, lane = threadIdx.x, gid = lane >> 2, tid4 = lane & 3;
   const int d0 = rb * 16 + gid, d1 = d0 + 8;
   const float w0 = wnorm[d0], w1 = wnorm[d1];
@@ -557,6 +559,21 @@ __global__ void k_na_prep(const float* x, const float* wnorm, int rows, __half* 
     ri->pos = 0;
     ri->mode = 0;
     ri->live = 1;
+  }
+}
+
+__global__ void k_na_prep(const float* x, const float* wnorm, int rows, __half* act, float* ss,
+                          vp_state* st, RowInfo* ri) {
+  na_prep_body(x, wnorm, rows, act, ss, st, ri);
+}
+
+// The sketch head's first launch: the same normed rows, plus a cleared per-call block.
+__global__ void k_sk_prep(const float* x, const float* wnorm, int rows, __half* act, float* ss,
+                          vp_state* st, RowInfo* ri, SketchSmall* small) {
+  na_prep_body(x, wnorm, rows, act, ss, st, ri);
+  if (blockIdx.x == 1) {
+    unsigned* z = reinterpret_cast<unsigned*>(small);
+    for (int i = threadIdx.x; i < (int)(sizeof(SketchSmall) / 4); i += blockDim.x) z[i] = 0u;
   }
 }
 
@@ -680,3 +697,108 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
   VP_CUDA(cudaGetLastError());
   return VP_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// Two-stage lm_head over the 2-bit sketch (vp_head_argmax_sketch; kernels in vp_sketch.cuh).
+
+namespace {
+
+struct SkWork {
+  __half* act;
+  float* ss;
+  vp_state* st;
+  RowInfo* ri;
+  SketchSmall* small;
+  float* bounds;
+  size_t bounds_off;
+  size_t bytes;
+};
+
+SkWork sk_work(int vocab, unsigned char* base) {
+  const size_t ngrp = sk_groups(vocab);
+  size_t o = 0;
+  SkWork w;
+  auto take = [&](size_t n) { unsigned char* q = base ? base + o : nullptr; o += na_align(n); return q; };
+  w.act = reinterpret_cast<__half*>(take(ROWS * H * sizeof(__half)));
+  w.ss = reinterpret_cast<float*>(take(HRB * ROWS * sizeof(float)));
+  w.st = reinterpret_cast<vp_state*>(take(sizeof(vp_state)));
+  w.ri = reinterpret_cast<RowInfo*>(take(sizeof(RowInfo)));
+  w.small = reinterpret_cast<SketchSmall*>(take(sizeof(SketchSmall)));
+  w.bounds_off = o;
+  w.bounds = reinterpret_cast<float*>(take(2 * ROWS * ngrp * sizeof(float)));
+  w.bytes = o;
+  return w;
+}
+
+bool sk_vocab_ok(int vocab) { return vocab >= 16 && vocab % 16 == 0 && vocab <= (1 << 26); }
+
+}  // namespace
+
+extern "C" {
+
+size_t vp_sketch_bytes(int32_t vocab) {
+  return sk_vocab_ok(vocab) ? (size_t)(vocab / 16) * SK_NG * SK_TILE : 0;
+}
+
+int vp_pack_sketch(int32_t vocab, const void* d_hi, void* d_out, void* stream) {
+  if (!sk_vocab_ok(vocab)) return fail(VP_ERR_ARG, "vocab must be a positive multiple of 16");
+  if (!d_hi || !d_out) return fail(VP_ERR_ARG, "null buffer");
+  const long long n = (long long)(vocab / 16) * SK_NG * 32;
+  k_pack_sketch<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      vocab, static_cast<const uint8_t*>(d_hi), static_cast<uint8_t*>(d_out));
+  VP_CUDA(cudaGetLastError());
+  return VP_OK;
+}
+
+size_t vp_sketch_bounds_offset(void) { return sk_work(32, nullptr).bounds_off; }
+
+size_t vp_sketch_work_bytes(int32_t vocab) {
+  return sk_vocab_ok(vocab) ? sk_work(vocab, nullptr).bytes : 0;
+}
+
+int vp_head_argmax_sketch(int32_t vocab, const void* d_embed, const void* d_sketch,
+                          const float* d_final_norm, const float* d_x, int32_t rows, float k_sigma,
+                          void* d_work, size_t work_bytes, int32_t* d_tokens, int32_t* d_ncand,
+                          void* stream) {
+  if (!sk_vocab_ok(vocab)) return fail(VP_ERR_ARG, "vocab must be a positive multiple of 16");
+  if (rows < 1 || rows > ROWS) return fail(VP_ERR_ARG, "rows must be 1..16");
+  if (!(k_sigma > 0.f) || !std::isfinite(k_sigma)) return fail(VP_ERR_ARG, "k_sigma must be positive");
+  if (!d_embed || !d_sketch || !d_final_norm || !d_x || !d_work || !d_tokens)
+    return fail(VP_ERR_ARG, "null buffer");
+  if (reinterpret_cast<uintptr_t>(d_work) % 256 || reinterpret_cast<uintptr_t>(d_sketch) % 16 ||
+      reinterpret_cast<uintptr_t>(d_embed) % 16)
+    return fail(VP_ERR_ARG, "work must be 256-byte aligned, sketch and embed 16-byte aligned");
+  const SkWork w = sk_work(vocab, static_cast<unsigned char*>(d_work));
+  if (work_bytes < w.bytes) return fail(VP_ERR_ARG, "work buffer smaller than vp_sketch_work_bytes");
+  int dev = 0, sms = 0;
+  VP_CUDA(cudaGetDevice(&dev));
+  VP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  SketchParams p = {};
+  p.sk = static_cast<const uint8_t*>(d_sketch);
+  p.emb = static_cast<const uint8_t*>(d_embed);
+  p.act = w.act;
+  p.ss = w.ss;
+  p.bounds = w.bounds;
+  p.small = w.small;
+  p.tokens = d_tokens;
+  p.ncand = d_ncand;
+  p.nrb = vocab / 16;
+  p.ngrp = sk_groups(vocab);
+  p.rows = rows;
+  p.k = k_sigma;
+
+  k_sk_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, w.act, w.ss, w.st, w.ri, w.small);
+  VP_CUDA(cudaGetLastError());
+  const int g1 = std::min((p.ngrp + SK_WARPS - 1) / SK_WARPS, 2 * sms);
+  if (rows <= 8) k_sketch<1><<<g1, SK_THREADS, 0, s>>>(p);
+  else k_sketch<2><<<g1, SK_THREADS, 0, s>>>(p);
+  VP_CUDA(cudaGetLastError());
+  const int g2 = std::min(std::max(2 * sms, (p.ngrp + SK_MAX_GPC - 1) / SK_MAX_GPC), p.ngrp);
+  k_sk_exact<<<g2, SK_THREADS, 0, s>>>(p);
+  VP_CUDA(cudaGetLastError());
+  return VP_OK;
+}
+
+}  // extern "C"

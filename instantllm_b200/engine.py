@@ -49,6 +49,7 @@ class VerifyEngine:
             raise ValueError(f"the GPU path runs q4, q8 or f16 weights, not {self.fmt}")
         self.n_layers = weights["n_layers"]
         self.vocab = weights["vocab"]
+        self.embed_hi = weights.get("embed_hi")  # optional 2-bit sketch plane (sketch.SketchHead)
         self.max_ctx, self.max_steps = max_ctx, max_steps
         self._keep = []
         self._staging = []

@@ -10,7 +10,8 @@ Sources/Engine/Convert.swift (:90-215) writes into it:
 * tensor ids (ModelFile.swift:47-60): 0 embedding codes, 1 its scale data, 2 final norm, then per
   layer l at 3 + 12 l: +0 input norm, +1 QKV codes, +2 QKV scales, +3 QKV bias, +4 O codes,
   +5 O scales, +6 post-attention norm, +7 gate/up codes, +8 gate/up scales, +9 down codes,
-  +10 down scales; 291 the optional 2-bit sketch of the q4 embedding (not used here);
+  +10 down scales; 291 the optional 2-bit sketch of the q4 embedding (read as "embed_hi", the
+  input of sketch.SketchHead);
 * q4: codes uint8 [rows][cols/2] (column 2j in the low nibble) and f16 (scale, bias) pairs
   [rows][cols/64][2]; q8: int8 codes [rows][cols] and one f16 scale per 32 columns (this
   package's "q8g32"); f16: f16 [rows][cols] and an empty scale tensor; norms and biases f32;
@@ -210,6 +211,11 @@ def read_ill(path: str) -> dict:
             "wgu": mat(layer_id(l, WGU), layer_id(l, WGU_SB), 2 * FFN, HIDDEN, go),
             "wd": mat(layer_id(l, WD), layer_id(l, WD_SB), HIDDEN, FFN, None),
         })
+    embed_hi = None
+    if table[EMBED_HI, 1]:
+        if fmt != "q4" or int(table[EMBED_HI, 1]) != vocab * (HIDDEN // 4):
+            raise ValueError(f"{path}: sketch plane of {int(table[EMBED_HI, 1])} bytes does not fit the embedding")
+        embed_hi = np.array(tensor(EMBED_HI)).reshape(vocab, HIDDEN // 4)
     return {"fmt": fmt, "n_layers": len(layers), "vocab": vocab,
             "embed": mat(EMBED, EMBED_SB, vocab, HIDDEN, None),
-            "final_norm": vec(FINAL_NORM, HIDDEN), "layers": layers}
+            "final_norm": vec(FINAL_NORM, HIDDEN), "layers": layers, "embed_hi": embed_hi}

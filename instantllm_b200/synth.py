@@ -84,6 +84,26 @@ def weight_bytes(fmt: str, n_layers: int = N_LAYERS, vocab: int = VOCAB) -> int:
     return n_layers * (layer + small) + HIDDEN * 4 + per(vocab, HIDDEN)
 
 
+def head_rows(embed: dict, final_norm: np.ndarray, rng: np.random.Generator, n: int,
+              mix=(1.0, 0.93, 0.6)) -> np.ndarray:
+    """Residual rows fp32 [n][896] for the tied lm_head with a clear winner and close runners-up, the
+    shape of a trained model's logits: each row mixes a few rows of the q4 embedding (divided by
+    the final norm) and adds noise. Random-init weights alone give flat logits."""
+    V = embed["codes"].shape[0]
+    s = embed["scales"][..., 0].astype(np.float32)
+    b = embed["scales"][..., 1].astype(np.float32)
+    x = np.zeros((n, HIDDEN), dtype=np.float32)
+    for r in range(n):
+        ids = rng.choice(V, size=len(mix), replace=False)
+        for c, i in zip(mix, ids):
+            q = np.empty(HIDDEN, dtype=np.float32)
+            q[0::2], q[1::2] = embed["codes"][i] & 15, embed["codes"][i] >> 4
+            x[r] += np.float32(c) * (q.reshape(-1, 64) * s[i][:, None] + b[i][:, None]).reshape(-1)
+        x[r] /= final_norm
+        x[r] += rng.normal(0, np.abs(x[r]).mean() * 0.5, HIDDEN).astype(np.float32)
+    return x * np.float32(40.0)
+
+
 def make_prompt(n: int, seed: int) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, 7919])))
     return rng.integers(0, PROMPT_VOCAB, size=n, dtype=np.int64).astype(np.int32)
