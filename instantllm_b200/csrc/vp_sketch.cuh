@@ -411,10 +411,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_sk_exact(SketchParams p) {
         }
     }
   }
-  // the last CTA writes the tokens and the candidate counts
-  __threadfence();
+  // the last CTA writes the tokens and the candidate counts (the barrier orders the CTA's atomics
+  // before thread 0's fence and ticket)
   cta_sync();
-  if (threadIdx.x == 0) sLast = atomicAdd(&sm->done, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    sLast = atomicAdd(&sm->done, 1u) == gridDim.x - 1;
+  }
   cta_sync();
   if (sLast) {
     __threadfence();

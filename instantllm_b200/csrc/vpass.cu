@@ -791,11 +791,12 @@ int vp_head_argmax_sketch(int32_t vocab, const void* d_embed, const void* d_sket
 
   k_sk_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, w.act, w.ss, w.st, w.ri, w.small);
   VP_CUDA(cudaGetLastError());
-  const int g1 = std::min((p.ngrp + SK_WARPS - 1) / SK_WARPS, 2 * sms);
+  const int g1 = std::min((p.ngrp + SK_WARPS - 1) / SK_WARPS, 2 * sms);  // resident CTAs
   if (rows <= 8) k_sketch<1><<<g1, SK_THREADS, 0, s>>>(p);
   else k_sketch<2><<<g1, SK_THREADS, 0, s>>>(p);
   VP_CUDA(cudaGetLastError());
-  const int g2 = std::min(std::max(2 * sms, (p.ngrp + SK_MAX_GPC - 1) / SK_MAX_GPC), p.ngrp);
+  // one wave: stage 2 runs one 253-register CTA per SM
+  const int g2 = std::min(std::max(sms, (p.ngrp + SK_MAX_GPC - 1) / SK_MAX_GPC), p.ngrp);
   k_sk_exact<<<g2, SK_THREADS, 0, s>>>(p);
   VP_CUDA(cudaGetLastError());
   return VP_OK;
