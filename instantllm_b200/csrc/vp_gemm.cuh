@@ -22,8 +22,8 @@ namespace vp {
 
 enum GemmMode { MODE_QKV = 0, MODE_RESID = 1, MODE_SILU = 2, MODE_ARGMAX = 3 };
 
-constexpr int GEMM_WARPS = 4;
-constexpr int GEMM_NST = 3;  // ring slots per warp
+constexpr int GEMM_WARPS = 8;
+constexpr int GEMM_NST = 2;  // ring slots per warp
 
 struct GemmParams {
   const uint8_t* w;      // packed tiles [nrb][ng]

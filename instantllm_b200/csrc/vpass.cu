@@ -236,7 +236,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   c->cfg = *cfg;
   const int fmt = cfg->format;
   c->lm = make_stage(fmt, cfg->vocab, H, 1);
-  c->lm.cps = 296 < (c->lm.nrb + 3) / 4 ? 296 : (c->lm.nrb + 3) / 4;
+  c->lm.cps = std::min(296, (c->lm.nrb + GEMM_WARPS - 1) / GEMM_WARPS);  // two CTAs per SM
   c->max_chunks = (cfg->max_ctx + ATT_SUB - 1) / ATT_SUB + 1;
   c->grid = sms;
 
@@ -673,7 +673,7 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
   k_na_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, act, ss, st, ri);
   VP_CUDA(cudaGetLastError());
   StageCfg lm = make_stage(format, vocab, H, 1);
-  lm.cps = 296 < (lm.nrb + 3) / 4 ? 296 : (lm.nrb + 3) / 4;
+  lm.cps = std::min(296, (lm.nrb + GEMM_WARPS - 1) / GEMM_WARPS);  // two CTAs per SM
   GemmParams p = {};
   p.w = static_cast<const uint8_t*>(d_embed);
   p.act = act;
