@@ -133,3 +133,21 @@ def test_engine_from_ill_matches_direct(fmt, tmp_path):
     assert out[0][0] == out[1][0]
     assert np.array_equal(out[0][1], out[1][1])
     assert out[0][2] == out[1][2]
+
+
+def test_sketch_tensor_round_trip(tmp_path):
+    """Tensor 291 (the 2-bit sketch of the q4 embedding) is read back as embed_hi; a sketch whose
+    size does not fit the embedding, or one in a non-q4 file, is rejected."""
+    from instantllm_b200 import convert
+
+    w = _weights("q4", n_layers=1, vocab=256)
+    hi = convert.sketch_q4(w["embed"]["codes"])
+    path = str(tmp_path / "m.ill")
+    ill.write_ill(path, w, embed_hi=hi)
+    r = ill.read_ill(path)
+    assert r["embed_hi"] is not None and np.array_equal(r["embed_hi"], hi)
+    ill.write_ill(path, w)
+    assert ill.read_ill(path)["embed_hi"] is None
+    ill.write_ill(path, w, embed_hi=hi[:128])
+    with pytest.raises(ValueError, match="sketch plane"):
+        ill.read_ill(path)

@@ -134,3 +134,19 @@ def test_sketch_head_matches_full_head(gpu_setup, rows):
                                          eng._weights_struct.final_norm, xd.data_ptr(), rows,
                                          ctypes.c_float(6.0), sk._work_ptr, 100,
                                          full.data_ptr(), None, eng.stream.cuda_stream) != 0
+
+
+def test_sketch_head_rejects_bad_inputs_on_host():
+    """Argument checks that run before any device work (a stub engine stands in)."""
+    from instantllm_b200.sketch import SketchHead
+
+    class Stub:
+        fmt, vocab, embed_hi = "q8", 256, None
+
+    with pytest.raises(ValueError, match="q4"):
+        SketchHead(Stub())
+    Stub.fmt = "q4"
+    with pytest.raises(ValueError, match="no sketch plane"):
+        SketchHead(Stub())
+    with pytest.raises(ValueError, match="shape"):
+        SketchHead(Stub(), hi=np.zeros((128, 224), dtype=np.uint8))
