@@ -207,7 +207,7 @@ int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
  *   x       fp32 [rows][896] residual rows (device); tokens int32 [rows] (device)
  *   limits  1 <= rows <= VP_MAX_ROWS; vocab a multiple of 16, <= VP_NOALLOC_MAX_VOCAB;
  *           larger sizes return VP_ERR_ARG.
- * Scratch is one static device array inside the library (about 1.4 MiB, held by every GPU that
+ * Scratch is one static device array inside the library (about 33 KiB, held by every GPU that
  * loads the library until the process exits). The first call on a device looks the array up on
  * that device (make that first call before any stream capture). All calls share the array:
  * calls whose work overlaps on the GPU (other streams, other threads) race, so serialise them.

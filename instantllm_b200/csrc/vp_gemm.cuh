@@ -25,6 +25,27 @@ enum GemmMode { MODE_QKV = 0, MODE_RESID = 1, MODE_SILU = 2, MODE_ARGMAX = 3 };
 constexpr int GEMM_WARPS = 8;
 constexpr int GEMM_NST = 2;  // ring slots per warp
 
+// Greedy argmax through one atomic max per row: the key orders by logit (an order-preserving
+// unsigned encoding of the float), then by the lower id. A zero key means nothing was inserted.
+struct ArgmaxKeys {
+  unsigned long long best[16];
+  unsigned done;  // CTAs finished
+};
+__device__ __forceinline__ unsigned ordered_bits(float f) {
+  const unsigned u = __float_as_uint(f + 0.f);  // -0 -> +0: equal floats get equal keys
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long argmax_key(float v, int id) {
+  return ((unsigned long long)ordered_bits(v) << 32) | (unsigned)(0x7fffffff - id);
+}
+__device__ __forceinline__ int argmax_key_id(unsigned long long k) {
+  return 0x7fffffff - (int)(unsigned)(k & 0xffffffffu);
+}
+
+// k_gemm<ARGMAX> with keys: the CTA's best key per row, merged into the global keys once per CTA
+// (one copy per CTA; cleared before gemm_cta's first barrier).
+__shared__ unsigned long long gemm_cta_keys[16];
+
 struct GemmParams {
   const uint8_t* w;      // packed tiles [nrb][ng]
   const __half* act;     // act blocks [ng]
@@ -41,6 +62,10 @@ struct GemmParams {
   float* pval;           // ARGMAX
   int* pidx;
   float* dbg;            // ARGMAX: optional full logits [16][nrb*16]
+  ArgmaxKeys* keys;      // ARGMAX: optional; instead of pval / pidx, each row's (logit, id) goes into
+                         // an atomic max and the last CTA writes tokens[0 .. out_rows)
+  int32_t* tokens;
+  int out_rows;
   float* xs;             // RESID: x[16 tokens][16 dims] of the row-block kept in shared memory by
                          // the CTA that owns it (persistent kernel), or null to use global x
   uint64_t* act_ll_out;  // RESID (persistent kernel, O): flagged act blocks / partials instead of
@@ -226,8 +251,12 @@ __device__ void gemm_epilogue(const GemmParams& p, int rb, float (&acc)[2][4], c
           if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (gid == 0) {
-          p.pval[(size_t)t * p.nrb + rb] = bv;
-          p.pidx[(size_t)t * p.nrb + rb] = bi;
+          if (p.keys) {
+            if (t < p.out_rows) atomicMax(gemm_cta_keys + t, argmax_key(bv, bi));
+          } else {
+            p.pval[(size_t)t * p.nrb + rb] = bv;
+            p.pidx[(size_t)t * p.nrb + rb] = bi;
+          }
         }
       }
   }
@@ -477,7 +506,30 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(GEMM_WARPS * 32) k_gemm(GemmParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  if constexpr (MODE == MODE_ARGMAX)
+    if (p.keys && threadIdx.x < 16) gemm_cta_keys[threadIdx.x] = 0ull;
   gemm_cta<FMT, MODE>(p, smem, blockIdx.x);
+  if constexpr (MODE == MODE_ARGMAX) {
+    if (p.keys) {  // the last CTA to finish writes the tokens (-1 after a device-side timeout)
+      __shared__ bool sLast;
+      cta_sync();
+      if (threadIdx.x < p.out_rows && gemm_cta_keys[threadIdx.x])
+        atomicMax(p.keys->best + threadIdx.x, gemm_cta_keys[threadIdx.x]);
+      cta_sync();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        sLast = atomicAdd(&p.keys->done, 1u) == gridDim.x - 1;
+      }
+      cta_sync();
+      if (sLast) {
+        __threadfence();
+        if (threadIdx.x < p.out_rows) {
+          const unsigned long long k = atomicOr(p.keys->best + threadIdx.x, 0ull);
+          p.tokens[threadIdx.x] = (p.s.st->err || !k) ? -1 : argmax_key_id(k);
+        }
+      }
+    }
+  }
 }
 
 }  // namespace vp

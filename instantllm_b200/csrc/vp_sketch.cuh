@@ -44,22 +44,16 @@ __host__ __device__ constexpr int sk_groups(int vocab) { return (vocab + SK_GROU
 // The per-call block both stages share, zeroed by k_sk_prep.
 struct SketchSmall {
   unsigned tau[16];                // encoded max over groups of the lower bound (sk_enc)
-  unsigned long long best[16];     // encoded (logit, id) argmax of the candidates (sk_key)
+  unsigned long long best[16];     // encoded (logit, id) argmax of the candidates (argmax_key)
   int cand0, cand_any;             // candidate groups of row 0, of any row
   unsigned done;                   // stage-2 CTAs finished
 };
 
-// Float max through unsigned atomics: an order-preserving encoding (0 is below every float).
-__device__ __forceinline__ unsigned sk_enc(float f) {
-  const unsigned u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
+// Float max through unsigned atomics: the order-preserving encoding of vp_gemm.cuh (0 is below
+// every float); (logit, id) keys are vp_gemm.cuh's argmax_key.
+__device__ __forceinline__ unsigned sk_enc(float f) { return ordered_bits(f); }
 __device__ __forceinline__ float sk_dec(unsigned u) {
   return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
-}
-// (logit, id) -> a key whose unsigned max is the larger logit, then the lower id.
-__device__ __forceinline__ unsigned long long sk_key(float v, int id) {
-  return ((unsigned long long)sk_enc(v) << 32) | (unsigned)(0x7fffffff - id);
 }
 
 // Standard sketch plane hi [vocab][H/4] (byte c of a row: codes 4c .. 4c+3 >> 2, code 4c in bits
@@ -407,7 +401,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_sk_exact(SketchParams p) {
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
           }
-          if (gid == 0 && ((mask >> t) & 1u)) atomicMax(sm->best + t, sk_key(bv, bi));
+          if (gid == 0 && ((mask >> t) & 1u)) atomicMax(sm->best + t, argmax_key(bv, bi));
         }
     }
   }
@@ -423,7 +417,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_sk_exact(SketchParams p) {
     __threadfence();
     if (threadIdx.x < p.rows) {
       const unsigned long long k = atomicOr(sm->best + threadIdx.x, 0ull);
-      p.tokens[threadIdx.x] = k ? 0x7fffffff - (int)(unsigned)(k & 0xffffffffu) : -1;
+      p.tokens[threadIdx.x] = k ? argmax_key_id(k) : -1;
     }
     if (threadIdx.x == 0 && p.ncand) {
       p.ncand[0] = atomicOr(&sm->cand0, 0);

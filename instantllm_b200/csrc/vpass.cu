@@ -506,7 +506,7 @@ int vp_buffer(vp_ctx* c, int32_t which, void** ptr, size_t* bytes) {
 // Greedy lm-head argmax that allocates nothing (vp_head_argmax_noalloc).
 //
 // For callers that cannot call cudaMalloc: its scratch (the fp16 normed rows, the RMSNorm
-// partials, the per-16-row argmax partials and a state / row-info block) is this file-scope
+// partials, a state / row-info block and the per-row argmax keys) is this file-scope
 // device array. Host code must never use `g_noalloc_scratch` itself as a pointer: on the host it
 // is only a stand-in symbol. The device address is looked up once per device with
 // cudaGetSymbolAddress and passed to the kernels.
@@ -518,8 +518,8 @@ constexpr size_t NA_ACT = na_align(ROWS * H * sizeof(__half));
 constexpr size_t NA_SS = na_align(HRB * ROWS * sizeof(float));
 constexpr size_t NA_ST = na_align(sizeof(vp_state));
 constexpr size_t NA_RI = na_align(sizeof(RowInfo));
-constexpr size_t NA_PART = na_align((size_t)ROWS * (VP_NOALLOC_MAX_VOCAB / 16) * 4);
-constexpr size_t NA_BYTES = NA_ACT + NA_SS + NA_ST + NA_RI + 2 * NA_PART;
+constexpr size_t NA_KEYS = na_align(sizeof(ArgmaxKeys));
+constexpr size_t NA_BYTES = NA_ACT + NA_SS + NA_ST + NA_RI + NA_KEYS;
 
 }  // namespace
 
@@ -563,8 +563,12 @@ __device__ void na_prep_body(const float* x, const float* wnorm, int rows, __hal
 }
 
 __global__ void k_na_prep(const float* x, const float* wnorm, int rows, __half* act, float* ss,
-                          vp_state* st, RowInfo* ri) {
+                          vp_state* st, RowInfo* ri, ArgmaxKeys* keys) {
   na_prep_body(x, wnorm, rows, act, ss, st, ri);
+  if (blockIdx.x == 1) {
+    unsigned* z = reinterpret_cast<unsigned*>(keys);
+    for (int i = threadIdx.x; i < (int)(sizeof(ArgmaxKeys) / 4); i += blockDim.x) z[i] = 0u;
+  }
 }
 
 // The sketch head's first launch: the same normed rows, plus a cleared per-call block.
@@ -574,36 +578,6 @@ __global__ void k_sk_prep(const float* x, const float* wnorm, int rows, __half* 
   if (blockIdx.x == 1) {
     unsigned* z = reinterpret_cast<unsigned*>(small);
     for (int i = threadIdx.x; i < (int)(sizeof(SketchSmall) / 4); i += blockDim.x) z[i] = 0u;
-  }
-}
-
-// One CTA per row: max over the per-16-row partials, lowest id on ties.
-__global__ void k_na_argmax(const float* pval, const int* pidx, int nrb, const vp_state* st,
-                            int32_t* tokens) {
-  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float rv[8];
-  __shared__ int ri_[8];
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = tid; i < nrb; i += 256) {
-    const float v = pval[(size_t)t * nrb + i];
-    const int id = pidx[(size_t)t * nrb + i];
-    if (v > best || (v == best && id < bi)) { best = v; bi = id; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-  }
-  if (lane == 0) { rv[warp] = best; ri_[warp] = bi; }
-  cta_sync();
-  if (tid == 0) {
-    best = rv[0];
-    bi = ri_[0];
-    for (int w = 1; w < 8; ++w)
-      if (rv[w] > best || (rv[w] == best && ri_[w] < bi)) { best = rv[w]; bi = ri_[w]; }
-    tokens[t] = st->err ? -1 : bi;
   }
 }
 
@@ -666,11 +640,10 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
   float* ss = reinterpret_cast<float*>(base + NA_ACT);
   vp_state* st = reinterpret_cast<vp_state*>(base + NA_ACT + NA_SS);
   RowInfo* ri = reinterpret_cast<RowInfo*>(base + NA_ACT + NA_SS + NA_ST);
-  float* pval = reinterpret_cast<float*>(base + NA_ACT + NA_SS + NA_ST + NA_RI);
-  int* pidx = reinterpret_cast<int*>(base + NA_ACT + NA_SS + NA_ST + NA_RI + NA_PART);
+  ArgmaxKeys* keys = reinterpret_cast<ArgmaxKeys*>(base + NA_ACT + NA_SS + NA_ST + NA_RI);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  k_na_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, act, ss, st, ri);
+  k_na_prep<<<HRB, 32, 0, s>>>(d_x, d_final_norm, rows, act, ss, st, ri, keys);
   VP_CUDA(cudaGetLastError());
   StageCfg lm = make_stage(format, vocab, H, 1);
   lm.cps = std::min(296, (lm.nrb + GEMM_WARPS - 1) / GEMM_WARPS);  // two CTAs per SM
@@ -683,8 +656,9 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
   p.cg = lm.cg;
   p.cps = lm.cps;
   p.ss_in = ss;
-  p.pval = pval;
-  p.pidx = pidx;
+  p.keys = keys;
+  p.tokens = d_tokens;
+  p.out_rows = rows;
   p.s.st = st;
   p.s.ri = ri;
   switch (format) {
@@ -693,8 +667,6 @@ extern "C" int vp_head_argmax_noalloc(int32_t format, int32_t vocab, const void*
     case VP_FMT_Q8G32: VP_CUDA((gemm_launch<VP_FMT_Q8G32, MODE_ARGMAX>(lm, p, s))); break;
     default: VP_CUDA((gemm_launch<VP_FMT_F16, MODE_ARGMAX>(lm, p, s))); break;
   }
-  k_na_argmax<<<rows, 256, 0, s>>>(pval, pidx, lm.nrb, st, d_tokens);
-  VP_CUDA(cudaGetLastError());
   return VP_OK;
 }
 
