@@ -246,19 +246,18 @@ def run_ours(args, rank, world, local):
         st = eng.state()
         ok = ok and st["step"] == 1 + counts[i] and eng.tokens(st["step"]) == y_full[:st["step"]]
 
-    # 3) end to end through the C ABI: state and tree from host memory in, state out, every step
+    # 3) end to end through the C ABI, one vp_step per step: the post-prefill state and the tree
+    # (host buffers, VP_TREE_INTS int32 as the drafter hands it over) in, the pass, the state out
+    host_trees = [np.ascontiguousarray(t, dtype=np.int32) for t in trees]
+    snap_host = snap[0]
     for i in range(args.warmup):
-        eng.restore(snap, on_device=False)
-        eng.pass_(trees[i])
-        eng.state()
+        eng.step(host_trees[i], snap_host)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e2e_tok = 0
     for i in range(args.warmup, n_steps):
-        eng.restore(snap, on_device=False)  # host state -> device
-        eng.pass_(trees[i])  # host tree -> device inside vp_pass
-        stt = eng.state()    # device state -> host (synchronises)
-        e2e_tok += stt["step"] - 1
+        stt = eng.step(host_trees[i], snap_host)  # state + tree -> device, pass, state -> host
+        e2e_tok += stt.step - 1
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     return dict(ms=ms, tok=n_tok_timed, ok=ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,

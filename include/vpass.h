@@ -174,6 +174,15 @@ int vp_commit(vp_ctx* ctx, void* stream);
 
 /* ---- whole pass: verify + commit as one persistent-kernel launch (the pass encoder) ---- */
 int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
+/* One step of the host's decode loop (the body of Engine.generate's loop, Engine.swift:937-1015:
+ * fill State, encode the pass, wait, read State) in one call from host memory: optionally the
+ * 64-byte state (state_in, NULL to continue from the device state), the tree (VP_TREE_INTS int32,
+ * host), one pass (verify + commit), the state back into state_out; synchronises `stream`. The
+ * inputs go through the context's pinned staging block in one host-to-device copy (state and tree
+ * are adjacent on the device), the result in one device-to-host copy. Returns VP_ERR_DEVICE when
+ * state_out->err is set. */
+int vp_step(vp_ctx* ctx, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
+            void* stream);
 
 /* ---- results ---- */
 int vp_read_state(vp_ctx* ctx, vp_state* host, void* stream);       /* syncs `stream` */

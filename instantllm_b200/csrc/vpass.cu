@@ -75,7 +75,14 @@ struct vp_ctx {
   float* lm_pval = nullptr;  // [16][grid] per-CTA argmax partials of the last pass
   int* lm_pidx = nullptr;
   unsigned long long* trace = nullptr;  // stage timestamps of the last pass (ns)
+  unsigned char* io = nullptr;   // device: state (64 B) then the tree, one block for one copy in
+  unsigned char* pin = nullptr;  // pinned host staging of vp_step: state + tree in, state out
 };
+
+constexpr size_t IO_TREE = 64;                                  // tree offset in ctx->io
+constexpr size_t IO_BYTES = IO_TREE + VP_TREE_INTS * sizeof(int32_t);
+constexpr size_t PIN_OUT = 512;                                 // state-out offset in ctx->pin
+static_assert(sizeof(vp_state) <= IO_TREE && IO_BYTES <= PIN_OUT, "io layout");
 
 namespace {
 
@@ -247,8 +254,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   s.n_layers = cfg->n_layers;
   const size_t kv = (size_t)cfg->n_layers * NKV * cfg->max_ctx * HD * sizeof(__half);
   int r = VP_OK;
-  if ((r = dalloc(c, &s.st, sizeof(vp_state))) || (r = dalloc(c, &s.ri, sizeof(RowInfo))) ||
-      (r = dalloc(c, &s.tree, VP_TREE_INTS * sizeof(int32_t))) ||
+  if ((r = dalloc(c, &c->io, IO_BYTES)) || (r = dalloc(c, &s.ri, sizeof(RowInfo))) ||
       (r = dalloc(c, &s.out_tokens, (size_t)cfg->max_steps * sizeof(int32_t))) ||
       (r = dalloc(c, &s.x, ROWS * H * sizeof(float))) || (r = dalloc(c, &s.q, ROWS * H * sizeof(float))) ||
       (r = dalloc(c, &s.act_h, ROWS * H * sizeof(__half))) ||
@@ -274,6 +280,16 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &c->trace, MK_TRACE * sizeof(unsigned long long)))) {
     vp_destroy(c);
     return r;
+  }
+  s.st = reinterpret_cast<vp_state*>(c->io);
+  s.tree = reinterpret_cast<int32_t*>(c->io + IO_TREE);
+  {
+    cudaError_t e = cudaHostAlloc(&c->pin, PIN_OUT + sizeof(vp_state), cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+      c->pin = nullptr;
+      vp_destroy(c);
+      return fail(VP_ERR_NOMEM, std::string("cudaHostAlloc: ") + cudaGetErrorString(e));
+    }
   }
   // RoPE table: angle = position * theta^(-2i/64) in double, cos/sin rounded once to fp32
   // (tools/reference/qwen_ref.py:107-116).
@@ -301,6 +317,7 @@ void vp_destroy(vp_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->cfg.device);
   for (void* p : c->allocs) cudaFree(p);
+  if (c->pin) cudaFreeHost(c->pin);
   delete c;
 }
 
@@ -424,6 +441,30 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
   p.do_lm = 1;
   p.do_commit = 1;
   return launch_pass(c, p, st);
+}
+
+int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
+            void* stream) {
+  int r = check_ctx(c);
+  if (r) return r;
+  if (!tree || !state_out) return fail(VP_ERR_ARG, "null tree or state_out");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The previous call synchronised this stream, so the staging block is free to reuse.
+  std::memcpy(c->pin + IO_TREE, tree, VP_TREE_INTS * sizeof(int32_t));
+  size_t off = IO_TREE;
+  if (state_in) {
+    std::memcpy(c->pin, state_in, sizeof(vp_state));
+    off = 0;
+  }
+  VP_CUDA(cudaMemcpyAsync(c->io + off, c->pin + off, IO_BYTES - off, cudaMemcpyHostToDevice, st));
+  MegaParams p = mega_params(c);
+  p.do_lm = 1;
+  p.do_commit = 1;
+  if ((r = launch_pass(c, p, st))) return r;
+  VP_CUDA(cudaMemcpyAsync(c->pin + PIN_OUT, c->s.st, sizeof(vp_state), cudaMemcpyDeviceToHost, st));
+  VP_CUDA(cudaStreamSynchronize(st));
+  std::memcpy(state_out, c->pin + PIN_OUT, sizeof(vp_state));
+  return state_out->err ? VP_ERR_DEVICE : VP_OK;
 }
 
 int vp_read_state(vp_ctx* c, vp_state* host, void* stream) {

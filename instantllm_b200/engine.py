@@ -75,6 +75,7 @@ class VerifyEngine:
         self._weights_struct = w
         self._prompt = torch.empty(max_ctx, dtype=torch.int32, device=self.device)
         self._tree_host = torch.empty(TREE_INTS, dtype=torch.int32).pin_memory()
+        self._step_out = VpState()
 
     # ---- weights ----
     def _pack(self, m: dict, kind: int) -> int:
@@ -158,6 +159,19 @@ class VerifyEngine:
 
     def pass_(self, tree) -> None:
         check(self.lib.vp_pass(self.ctx, self._tree_ptr(tree), self._s), "vp_pass")
+
+    def step(self, tree, state_in: Optional[VpState] = None) -> VpState:
+        """One decode step from host memory (vp_step): optionally write `state_in`, copy the tree,
+        run the pass (verify + commit), read the state back; synchronises. Returns the state as a
+        VpState (fields as attributes, `.as_dict()`)."""
+        buf = tree if isinstance(tree, np.ndarray) else tree_to_buffer(tree)
+        buf = np.ascontiguousarray(buf, dtype=np.int32)
+        out = self._step_out
+        rc = self.lib.vp_step(self.ctx, ctypes.addressof(state_in) if state_in is not None else None,
+                              buf.ctypes.data, ctypes.byref(out), self._s)
+        if rc not in (0, -5):
+            check(rc, "vp_step")
+        return out
 
     def pass_device(self, tree_dev: torch.Tensor) -> None:
         """Graph pass with a device-resident tree buffer (no host round trip)."""
