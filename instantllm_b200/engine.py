@@ -305,12 +305,12 @@ class VerifyEngine:
             out = self.tokens(st["step"])
             tree = tree_fn(out) if tree_fn else root_tree()
             if fused:
-                self.pass_(tree)
+                st = self.step(tree).as_dict()  # tree in, pass, state out: one call
             else:
                 self.verify(tree)
                 self.commit()
+                st = self.state()
             passes += 1
-            st = self.state()
             if st["err"]:
                 raise _lib.VpError(f"device error bits {st['err']}")
         return {"tokens": self.tokens(st["step"]), "passes": passes, "state": st}
