@@ -111,3 +111,23 @@ def test_reader_on_the_reference_table():
     f = t.token_flags()
     for i, v in GOLD["tflags"]:
         assert int(f[i]) == v
+
+
+def test_drafter_golden_trees_are_well_formed():
+    """The reference drafter's trees recorded for a later port (make_drafter_golden.py): best-first
+    order (parents[i] < i, the first node the root's most probable child), B nodes, probabilities
+    sorted, outputs grown from one step to the next."""
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
+    for case in g["cases"]:
+        assert 0 < len(case["neighbours"]) <= GOLD["header"]["KNB"]
+        prev = None
+        for st in case["steps"]:
+            par, tok, pr = st["parents"], st["tokens"], st["probs"]
+            assert len(tok) == len(par) == g["B"]
+            assert all(-1 <= p < i for i, p in enumerate(par))
+            assert par[0] == -1 and tok[0] == pr[0][0]
+            assert all(pr[i][1] >= pr[i + 1][1] for i in range(len(pr) - 1))
+            assert all(0 <= x < dt.VOCAB for x in tok)
+            if prev is not None:
+                assert st["out"][:len(prev)] == prev and len(st["out"]) > len(prev)
+            prev = st["out"]
