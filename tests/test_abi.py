@@ -59,3 +59,24 @@ def test_argument_errors_without_device(lib):
     st = _lib.VpState()
     assert lib.vp_read_state(None, ctypes.byref(st), None) == -1
     assert lib.vp_device_tokens(None) is None
+
+
+def test_step_and_sketch_argument_errors_without_device(lib):
+    """vp_step and the sketch head reject bad arguments before any CUDA call."""
+    st = _lib.VpState()
+    tree = (ctypes.c_int32 * _lib.TREE_INTS)()
+    assert lib.vp_step(None, None, tree, ctypes.byref(st), None) == -1
+    assert b"null context" in lib.vp_last_error()
+    assert lib.vp_sketch_bytes(100) == 0 and lib.vp_sketch_work_bytes(0) == 0
+    assert lib.vp_sketch_bytes(151936) == 151936 // 16 * 14 * 256
+    assert lib.vp_sketch_bounds_offset() % 256 == 0
+    assert lib.vp_pack_sketch(100, None, None, None) == -1
+    d = ctypes.c_void_p(256)  # never dereferenced: every call below fails its checks first
+    tok = ctypes.c_void_p(512)
+    assert lib.vp_head_argmax_sketch(100, d, d, d, d, 1, ctypes.c_float(6.0), d, 1 << 20, tok, None, None) == -1
+    assert lib.vp_head_argmax_sketch(4096, d, d, d, d, 0, ctypes.c_float(6.0), d, 1 << 20, tok, None, None) == -1
+    assert lib.vp_head_argmax_sketch(4096, d, d, d, d, 1, ctypes.c_float(0.0), d, 1 << 20, tok, None, None) == -1
+    assert b"k_sigma" in lib.vp_last_error()
+    assert lib.vp_head_argmax_sketch(4096, d, d, d, d, 1, ctypes.c_float(6.0), d, 16, tok, None, None) == -1
+    assert b"work buffer" in lib.vp_last_error()
+    assert lib.vp_head_argmax_noalloc(2, 4100, d, d, d, 1, tok, None) == -1
