@@ -10,8 +10,8 @@ through the same kernels (1-row passes), and the committed tokens of the timed t
 checked against it (tree == sequential) for every step after the timed loop.
 
 value  = accepted (committed) tokens per second over all ranks, inputs resident in HBM.
-e2e    = the same through the C ABI with the tree in pinned host memory and the committed
-         state / tokens read back to the host every step.
+e2e    = the same through the C ABI from host memory: one vp_step per step (the post-prefill state
+         and the tree in, the pass, the committed state back to the host).
 N > 1  = one independent request per rank (request-level sharding, weak scaling, no collective on
          the data path; torch.distributed over gloo is used only for the barrier around the timed
          region and the max-time reduce; no NCCL).
