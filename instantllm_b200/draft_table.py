@@ -5,8 +5,9 @@ n-gram, word and association lookups (:416-429).
 
 Sections stay as the file stores them: sorted 64-bit keys searched by bisection, with parallel value
 arrays and (first, n) ranges into flat arrays. That is the layout a drafter kernel reads from device
-memory as well (one binary search per lookup, no hash maps). This module covers the table and the
-lookups only; candidate features, the MLP scorer and tree shaping (ildraft.py:520-748) are not built.
+memory as well (one binary search per lookup, no hash maps). This module covers the table, the
+lookups and the request's nearest training documents (the TF-IDF part of Drafter.begin); candidate
+features, the MLP scorer and tree shaping (ildraft.py:520-748) are not built.
 """
 from __future__ import annotations
 
@@ -134,6 +135,34 @@ class DraftTable:
         v = self.sec[b"ASWV"][i]
         t = self.sec[b"ASTK"][int(v["first"]):int(v["first"]) + int(v["n"])]
         return [(int(a), float(b)) for a, b in zip(t["token"], t["loglift"])]
+
+    def neighbours(self, text: str, knb: Optional[int] = None) -> list:
+        """The request's nearest training documents (ildraft.py:455-468, Drafter.begin): TF-IDF
+        cosine between the prompt's distinct words and each document, score = sum over shared
+        words of idf^2 / (|q| |d|), with |q|^2 the sum of idf^2 over the prompt's words found in
+        the table; the top `knb` (default KNB) as [(score, doc)] by score descending, then doc
+        ascending. Scores in float64, summed per document in prompt-word order."""
+        knb = self.KNB if knb is None else knb
+        sc = np.zeros(self.n_docs, dtype=np.float64)
+        hit = np.zeros(self.n_docs, dtype=bool)
+        q2 = 0.0
+        for w in prompt_words(text):
+            e = self.vocab_get(w)
+            if e is None:
+                continue
+            idf, docs = e
+            ii = idf * idf
+            q2 += ii
+            if docs:
+                d = np.asarray(docs, dtype=np.int64)
+                np.add.at(sc, d, ii)
+                hit[d] = True
+        qn = float(np.sqrt(q2)) or 1.0
+        docs = np.nonzero(hit)[0]
+        norms = self.sec[b"DNRM"].astype(np.float64)
+        s = [(float(sc[j]) / (qn * float(norms[j])), int(j)) for j in docs]
+        s.sort(key=lambda x: (-x[0], x[1]))
+        return s[:knb]
 
     def seq(self, doc: int) -> list:
         """Training output `doc` (generated ids and the stop token if it stopped)."""

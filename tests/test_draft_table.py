@@ -131,3 +131,14 @@ def test_drafter_golden_trees_are_well_formed():
             if prev is not None:
                 assert st["out"][:len(prev)] == prev and len(st["out"]) > len(prev)
             prev = st["out"]
+
+
+@pytest.mark.skipif(not os.environ.get("INSTANTLLM_DRAFT_TABLE"), reason="INSTANTLLM_DRAFT_TABLE not set")
+def test_neighbours_match_the_reference_drafter():
+    """Drafter.begin's nearest training documents for the golden requests: same scores (float64,
+    the same summation order) and the same documents (their sequence lengths)."""
+    t = dt.DraftTable.load(os.environ["INSTANTLLM_DRAFT_TABLE"])
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
+    for case in g["cases"]:
+        got = t.neighbours(case["text"])
+        assert [[s, 5 + len(t.seq(j))] for s, j in got] == case["neighbours"]
