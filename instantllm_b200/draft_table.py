@@ -6,8 +6,9 @@ n-gram, word and association lookups (:416-429).
 Sections stay as the file stores them: sorted 64-bit keys searched by bisection, with parallel value
 arrays and (first, n) ranges into flat arrays. That is the layout a drafter kernel reads from device
 memory as well (one binary search per lookup, no hash maps). This module covers the table, the
-lookups and the request's nearest training documents (the TF-IDF part of Drafter.begin); candidate
-features, the MLP scorer and tree shaping (ildraft.py:520-748) are not built.
+lookups, the request's nearest training documents (the TF-IDF part of Drafter.begin) and the
+scorer over given feature rows; the candidate features and tree shaping (ildraft.py:520-692,
+710-748) are not built.
 """
 from __future__ import annotations
 
@@ -163,6 +164,23 @@ class DraftTable:
         s = [(float(sc[j]) / (qn * float(norms[j])), int(j)) for j in docs]
         s.sort(key=lambda x: (-x[0], x[1]))
         return s[:knb]
+
+    def probs(self, tokens, rows) -> list:
+        """The scorer over candidate feature rows (ildraft.py:694-708): score = W2 . relu(W1 x + b1)
+        + b2 + WL . x in float64, a softmax that also counts a null option of score 0, and the
+        candidates as [(token, p)] by p descending, then token ascending."""
+        if len(tokens) == 0:
+            return []
+        m = self.mlp()
+        X = np.asarray(rows, dtype=np.float64)
+        W1, b1 = m["W1"].astype(np.float64), m["b1"].astype(np.float64)
+        W2, WL = m["W2"].astype(np.float64), m["WL"].astype(np.float64)
+        s = np.maximum(X @ W1.T + b1, 0.0) @ W2 + float(m["b2"]) + X @ WL
+        top = max(float(s.max()), 0.0)
+        e = np.exp(s - top)
+        ps = e / (float(e.sum()) + float(np.exp(-top)))
+        order = sorted(range(len(tokens)), key=lambda i: (-ps[i], int(tokens[i])))
+        return [(int(tokens[i]), float(ps[i])) for i in order]
 
     def seq(self, doc: int) -> list:
         """Training output `doc` (generated ids and the stop token if it stopped)."""

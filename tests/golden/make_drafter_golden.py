@@ -1,9 +1,9 @@
 """Golden draft trees from the reference drafter (tools/draft/ildraft.py: Drafter.begin, probs,
 tree, chain) on the table the reference ships, for synthetic requests: prompt ids drawn from a seeded
 generator, prompt texts written for this fixture, and outputs grown by the drafter's own greedy
-chain. No tokenizer is given (the reference's space-variant and edited-neighbour features need one
-and are then skipped), as a drafter without the tokenizer runs. Ground truth for a port of the
-drafter.
+chain, with each step's candidate feature rows (ildraft.py FEATS order). No tokenizer is given
+(the reference's space-variant and edited-neighbour features need one and are then skipped), as a
+drafter without the tokenizer runs. Ground truth for a port of the drafter.
 
 Usage: python tests/golden/make_drafter_golden.py --reference <instantllm checkout> \
            [--out tests/golden/drafter_trees.json]
@@ -41,8 +41,11 @@ def main():
         for _ in range(3):
             parents, tokens = dr.tree(out, 15)
             pr = dr.probs(out)[:5]
+            ftoks, rows = dr.features(out)  # candidate rows: sparse (candidate, feature, value)
+            nz = [[i, f, float(v)] for i, r in enumerate(rows) for f, v in enumerate(r) if v != 0.0]
             steps.append({"out": list(out), "parents": parents, "tokens": tokens,
-                          "probs": [[int(k), float(p)] for k, p in pr]})
+                          "probs": [[int(k), float(p)] for k, p in pr],
+                          "features": {"tokens": [int(x) for x in ftoks], "nz": nz}})
             grow = dr.chain(out, 4)
             if not grow:
                 break

@@ -142,3 +142,31 @@ def test_neighbours_match_the_reference_drafter():
     for case in g["cases"]:
         got = t.neighbours(case["text"])
         assert [[s, 5 + len(t.seq(j))] for s, j in got] == case["neighbours"]
+
+
+def _rows(feat):
+    rows = np.zeros((len(feat["tokens"]), dt.N_FEATURES), dtype=np.float64)
+    for i, f, v in feat["nz"]:
+        rows[i, f] = v
+    return rows
+
+
+def test_golden_feature_rows_are_well_formed():
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
+    for case in g["cases"]:
+        for st in case["steps"]:
+            rows = _rows(st["features"])
+            assert np.all(rows[:, 0] == 1.0)  # the bias feature of every candidate
+            assert {k for k, _ in st["probs"]} <= set(st["features"]["tokens"])
+
+
+@pytest.mark.skipif(not os.environ.get("INSTANTLLM_DRAFT_TABLE"), reason="INSTANTLLM_DRAFT_TABLE not set")
+def test_scorer_matches_the_reference_drafter():
+    """The table's MLP over the reference's own feature rows gives the reference's probabilities."""
+    t = dt.DraftTable.load(os.environ["INSTANTLLM_DRAFT_TABLE"])
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
+    for case in g["cases"]:
+        for st in case["steps"]:
+            got = t.probs(st["features"]["tokens"], _rows(st["features"]))[:5]
+            assert [k for k, _ in got] == [k for k, _ in st["probs"]]
+            assert np.allclose([p for _, p in got], [p for _, p in st["probs"]], rtol=1e-12, atol=0)
