@@ -7,8 +7,8 @@ Sections stay as the file stores them: sorted 64-bit keys searched by bisection,
 arrays and (first, n) ranges into flat arrays. That is the layout a drafter kernel reads from device
 memory as well (one binary search per lookup, no hash maps). This module covers the table, the
 lookups, the request's nearest training documents (the TF-IDF part of Drafter.begin) and the
-scorer over given feature rows; the candidate features and tree shaping (ildraft.py:520-692,
-710-748) are not built.
+scorer over given feature rows, and the best-first tree over a given probability function; the
+candidate features (ildraft.py:520-692) are not built.
 """
 from __future__ import annotations
 
@@ -52,6 +52,37 @@ def prompt_words(text: str) -> list:
             seen.add(w)
             out.append(w)
     return out
+
+
+STOPS = (151645, 151643)
+
+
+def best_first_tree(probs, B: int, branch: int = 8, stops=STOPS) -> tuple:
+    """The draft tree of B nodes grown best first (ildraft.py:724-747): every candidate of a node
+    (the top `branch` of probs(path), path = the tokens from the root to that node) waits in a
+    priority queue keyed by its path probability, the product of the probabilities along the path;
+    the most probable waiting candidate becomes the next node (equal keys: the one queued first),
+    and its own candidates are queued unless it is a stop token. Returns (parents, tokens): node i
+    hangs under node parents[i] (-1: the root, the last accepted token), so parents[i] < i."""
+    import heapq
+
+    parents, tokens, path = [], [], {-1: []}
+    queue, seq = [], 0
+    for tok, p in probs([])[:branch]:
+        heapq.heappush(queue, (-p, seq, -1, tok))
+        seq += 1
+    while queue and len(tokens) < B:
+        key, _, par, tok = heapq.heappop(queue)
+        node = len(tokens)
+        parents.append(par)
+        tokens.append(tok)
+        path[node] = path[par] + [tok]
+        if tok in stops or len(tokens) >= B:
+            continue
+        for tok2, p2 in probs(path[node])[:branch]:
+            heapq.heappush(queue, (key * p2, seq, node, tok2))
+            seq += 1
+    return parents, tokens
 
 
 # section tag -> numpy dtype of one record

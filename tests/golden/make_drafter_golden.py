@@ -39,13 +39,23 @@ def main():
         dr.begin(pids, text)
         out, steps = [], []
         for _ in range(3):
+            calls, real = [], dr.probs
+
+            def recording(o, _real=real, _calls=calls, _n=len(out)):
+                r = _real(o)
+                _calls.append([list(o[_n:]), [[int(k), float(p)] for k, p in r[:8]]])
+                return r
+
+            dr.probs = recording  # every context the tree expands: its path below `out`, top 8
             parents, tokens = dr.tree(out, 15)
+            dr.probs = real
             pr = dr.probs(out)[:5]
             ftoks, rows = dr.features(out)  # candidate rows: sparse (candidate, feature, value)
             nz = [[i, f, float(v)] for i, r in enumerate(rows) for f, v in enumerate(r) if v != 0.0]
             steps.append({"out": list(out), "parents": parents, "tokens": tokens,
                           "probs": [[int(k), float(p)] for k, p in pr],
-                          "features": {"tokens": [int(x) for x in ftoks], "nz": nz}})
+                          "features": {"tokens": [int(x) for x in ftoks], "nz": nz},
+                          "expansions": calls})
             grow = dr.chain(out, 4)
             if not grow:
                 break

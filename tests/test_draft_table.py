@@ -170,3 +170,22 @@ def test_scorer_matches_the_reference_drafter():
             got = t.probs(st["features"]["tokens"], _rows(st["features"]))[:5]
             assert [k for k, _ in got] == [k for k, _ in st["probs"]]
             assert np.allclose([p for _, p in got], [p for _, p in st["probs"]], rtol=1e-12, atol=0)
+
+
+def test_best_first_tree_matches_the_reference_trees():
+    """Fed the probabilities the reference drafter computed for every node it expanded, the tree
+    builder makes the reference's trees (same nodes, order and parents) and asks for exactly the
+    recorded nodes."""
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
+    for case in g["cases"]:
+        for st in case["steps"]:
+            rec = {tuple(path): [tuple(x) for x in top] for path, top in st["expansions"]}
+            asked = []
+
+            def probs(path):
+                asked.append(tuple(path))
+                return rec[tuple(path)]
+
+            par, tok = dt.best_first_tree(probs, g["B"], g["branch"])
+            assert (par, tok) == (st["parents"], st["tokens"])
+            assert asked == [tuple(p) for p, _ in st["expansions"]]
