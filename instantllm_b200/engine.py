@@ -163,7 +163,8 @@ class VerifyEngine:
     def step(self, tree, state_in: Optional[VpState] = None) -> VpState:
         """One decode step from host memory (vp_step): optionally write `state_in`, copy the tree,
         run the pass (verify + commit), read the state back; synchronises. Returns the state as a
-        VpState (fields as attributes, `.as_dict()`)."""
+        VpState (fields as attributes, `.as_dict()`); the same object is refilled by the next call,
+        so copy it (`.as_dict()`) to keep it."""
         buf = tree if isinstance(tree, np.ndarray) else tree_to_buffer(tree)
         buf = np.ascontiguousarray(buf, dtype=np.int32)
         out = self._step_out
