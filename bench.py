@@ -254,13 +254,16 @@ def run_ours(args, rank, world, local):
         eng.step(host_trees[i], snap_host)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e2e_tok = 0
+    e2e_tok, e2e_ok = 0, True
     for i in range(args.warmup, n_steps):
-        stt = eng.step(host_trees[i], snap_host)  # state + tree -> device, pass, state -> host
-        e2e_tok += stt.step - 1
+        # state + tree -> device, pass, state + the pass's committed tokens -> host
+        stt = eng.step(host_trees[i], snap_host)
+        got = eng.last_tokens()
+        e2e_tok += len(got)
+        e2e_ok = e2e_ok and got == y_full[1:1 + len(got)] and stt.step == 1 + len(got)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    return dict(ms=ms, tok=n_tok_timed, ok=ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,
+    return dict(ms=ms, tok=n_tok_timed, ok=ok and e2e_ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,
                 setup_s=time.time() - t_setup, eng=eng, w=w, prompt=prompt, y=y_full, trees=trees,
                 counts=counts)
 
@@ -591,8 +594,10 @@ def main():
                          "frac": achieved / hbm_peak, "traffic": ncu_traffic(),
                          "kernel": "k_pass: the persistent verify-pass kernel (one launch per pass), rank 0",
                          "bytes_per_launch": alg, "peak_kind": peak_kind},
+            # vp_step moves state (64 B) + token slots (64 B) + tree (260 B) in and state + the
+            # pass's committed tokens (128 B) out per step
             "e2e": {"value": e2e_tok / e2e_s, "unit": "tok/s",
-                    "h2d_bytes_per_step": 64 + 65 * 4, "d2h_bytes_per_step": 64},
+                    "h2d_bytes_per_step": 64 + 64 + 65 * 4, "d2h_bytes_per_step": 128},
             "gpu_launches": args.steps,  # one persistent k_pass launch per verify pass
             "clocks": r["clocks"],
         }

@@ -175,14 +175,17 @@ int vp_commit(vp_ctx* ctx, void* stream);
 /* ---- whole pass: verify + commit as one persistent-kernel launch (the pass encoder) ---- */
 int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
 /* One step of the host's decode loop (the body of Engine.generate's loop, Engine.swift:937-1015:
- * fill State, encode the pass, wait, read State) in one call from host memory: optionally the
- * 64-byte state (state_in, NULL to continue from the device state), the tree (VP_TREE_INTS int32,
- * host), one pass (verify + commit), the state back into state_out; synchronises `stream`. The
- * inputs go through the context's pinned staging block in one host-to-device copy (state and tree
- * are adjacent on the device), the result in one device-to-host copy. Returns VP_ERR_DEVICE when
- * state_out->err is set. */
+ * fill State, encode the pass, wait, read State and the committed tokens) in one call from host
+ * memory: optionally the 64-byte state (state_in, NULL to continue from the device state), the
+ * tree (VP_TREE_INTS int32, host), one pass (verify + commit), then the state into state_out and,
+ * if tokens_out is not NULL, the tokens this pass committed into tokens_out (VP_MAX_ROWS int32,
+ * host: the committed tokens in order, then -1; all -1 when the request had already stopped).
+ * Synchronises `stream`, also when it fails. The inputs go through the context's pinned staging
+ * block in one host-to-device copy (state, token slots and tree are adjacent on the device), the
+ * results in one device-to-host copy of 128 bytes. Returns VP_ERR_DEVICE when state_out->err is
+ * set. */
 int vp_step(vp_ctx* ctx, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
-            void* stream);
+            int32_t* tokens_out, void* stream);
 
 /* ---- results ---- */
 int vp_read_state(vp_ctx* ctx, vp_state* host, void* stream);       /* syncs `stream` */
@@ -218,7 +221,8 @@ int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
  *           larger sizes return VP_ERR_ARG.
  * Scratch is one static device array inside the library (about 33 KiB, held by every GPU that
  * loads the library until the process exits). The first call on a device looks the array up on
- * that device (make that first call before any stream capture). All calls share the array:
+ * that device (make that first call before any stream capture; a failed look-up is retried by the
+ * next call). All calls share the array:
  * calls whose work overlaps on the GPU (other streams, other threads) race, so serialise them.
  * Runs on the current device and `stream`; reports a device-side timeout as token -1. */
 #define VP_NOALLOC_MAX_VOCAB 163840

@@ -81,7 +81,7 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_verify_chain": (ctypes.c_int, [vp, vp, i32, vp]),
         "vp_commit": (ctypes.c_int, [vp, vp]),
         "vp_pass": (ctypes.c_int, [vp, vp, vp]),
-        "vp_step": (ctypes.c_int, [vp, ctypes.c_void_p, vp, ctypes.POINTER(VpState), vp]),
+        "vp_step": (ctypes.c_int, [vp, ctypes.c_void_p, vp, ctypes.POINTER(VpState), vp, vp]),
         "vp_read_state": (ctypes.c_int, [vp, ctypes.POINTER(VpState), vp]),
         "vp_write_state": (ctypes.c_int, [vp, ctypes.c_void_p, ctypes.c_int32, vp]),
         "vp_prefix_bytes": (ctypes.c_size_t, [vp, ctypes.c_int32]),

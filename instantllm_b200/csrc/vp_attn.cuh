@@ -163,9 +163,12 @@ __device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
 // positions, so a row's output is bit-identical in a 16-row tree pass and in a 1-row pass.
 //
 // Work split: one unit (CTA) per (row t, kv head g, segment of <= ATT_SEGSUB sub-chunks). Warp w
-// stages sub-chunk w of the segment (its 32 K and V rows, coalesced cp.async into its own
-// XOR-swizzled buffer), loads the 7 query heads as fp16 hi + lo A fragments meanwhile, and computes
-// S = (q/8) K^T, the masked softmax and O = P V on the tensor cores (K and V B fragments by
+// stages the cached rows of sub-chunk w of the segment (coalesced cp.async into its own
+// XOR-swizzled buffer). Two otherwise idle warps poll the words the QKV stage publishes, once per
+// unit: warp ATT_WQ the 7 query rows of row t (into shared memory), warp ATT_WKV the pass rows
+// (row t's ancestors) of the segment's K and V (into the staging buffers of the warps that hold
+// their positions). After a named barrier each sub-chunk warp computes S = (q/8) K^T, the masked
+// softmax and O = P V on the tensor cores (q as fp16 hi + lo A fragments, K and V B fragments by
 // ldmatrix). Its record replaces its K rows in shared memory and the CTA combines the records. A
 // row longer than one segment writes its records to global memory; the segment that arrives last
 // combines them all.
@@ -173,11 +176,18 @@ __device__ void embed_row(const EmbedArgs& p, const Scratch& s, int t) {
 constexpr int GQ = NQ / NKV;            // 7 query heads per KV head
 constexpr int ATT_TICKETS = 1024;       // offset of the attention arrival counters in tickets
 constexpr int ATT_REC = GQ * (2 + HD);  // records of a (row, kv head, sub-chunk): per head m, l, o[64]
-constexpr int ATT_SEGSUB = 10;          // sub-chunks per unit (one per warp; shared-memory bound)
+constexpr int ATT_SEGSUB = 9;           // sub-chunks per unit (one per warp; shared-memory bound)
+constexpr int ATT_WKV = 14;             // warp that polls the pass rows' K and V
+constexpr int ATT_WQ = 15;              // warp that polls the query rows
+static_assert(ATT_SEGSUB < ATT_WKV, "the polling warps hold no sub-chunk");
 
 struct AttnSmem {
   // [warp][K, V][position][dim] staging; the warp's record overwrites its K rows once S is done
   alignas(128) __half kv[ATT_SEGSUB][2][ATT_SUB][HD];
+  float q[GQ][HD];             // query rows of row t for the kv head's 7 heads
+  float wgt[GQ][ATT_SEGSUB];   // combine: e^(m_c - M) per head and record (local records)
+  float inv[GQ];               // combine: 1 / sum_c l_c e^(m_c - M)
+  int late;                    // a polling warp gave up (bounded wait)
   int last;
 };
 constexpr int ATT_REC_STRIDE = 2 * ATT_SUB * HD / 2;  // floats between the records of two warps
@@ -195,24 +205,51 @@ __device__ __forceinline__ int attn_units(const RowInfo* ri) {
   return total;
 }
 
-// Final output of (row t, kv head g) from its records in sub-chunk order (record cc at
-// base + cc * stride): M = max m_c, O = sum o_c e^(m_c - M) / sum l_c e^(m_c - M).
+// Final output of (row t, kv head g) from its nsub records in sub-chunk order (record cc at
+// base + cc * stride): M = max m_c, w_c = e^(m_c - M), O = sum_c o_c w_c / sum_c l_c w_c. The
+// weights are formed once per (head, record) by 7 threads, then every output sums its records.
+// Global records (rows longer than one segment) hold up to max_subs records; their weights are
+// recomputed per output (nsub can exceed the shared array).
 template <bool GLOBAL>
 __device__ __forceinline__ void attn_combine(const Scratch& s, const float* base, int stride, int nsub,
-                                             int t, int g) {
+                                             int t, int g, AttnSmem& sm) {
   auto ld = [&](const float* q) { return GLOBAL ? __ldcg(q) : *q; };
-  for (int i = threadIdx.x; i < GQ * HD; i += PASS_THREADS) {
-    const int h = i / HD, d = i % HD;
-    float M = -INFINITY;
-    for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, ld(base + cc * stride + h * (2 + HD)));
-    float O = 0.f, Ls = 0.f;
-    for (int cc = 0; cc < nsub; ++cc) {
-      const float* r = base + cc * stride + h * (2 + HD);
-      const float w = expf(ld(r) - M);
-      Ls = fmaf(ld(r + 1), w, Ls);
-      O = fmaf(ld(r + 2 + d), w, O);
+  const int tid = threadIdx.x;
+  if constexpr (!GLOBAL) {
+    if (tid < GQ) {
+      const int h = tid;
+      float M = -INFINITY;
+      for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, base[cc * stride + h * (2 + HD)]);
+      float Ls = 0.f;
+      for (int cc = 0; cc < nsub; ++cc) {
+        const float* r = base + cc * stride + h * (2 + HD);
+        const float w = expf(r[0] - M);
+        sm.wgt[h][cc] = w;
+        Ls = fmaf(r[1], w, Ls);
+      }
+      sm.inv[h] = Ls;
     }
-    s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / Ls);
+    cons_sync();
+    for (int i = tid; i < GQ * HD; i += PASS_THREADS) {
+      const int h = i / HD, d = i % HD;
+      float O = 0.f;
+      for (int cc = 0; cc < nsub; ++cc) O = fmaf(base[cc * stride + h * (2 + HD) + 2 + d], sm.wgt[h][cc], O);
+      s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / sm.inv[h]);
+    }
+  } else {
+    for (int i = tid; i < GQ * HD; i += PASS_THREADS) {
+      const int h = i / HD, d = i % HD;
+      float M = -INFINITY;
+      for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, ld(base + cc * stride + h * (2 + HD)));
+      float O = 0.f, Ls = 0.f;
+      for (int cc = 0; cc < nsub; ++cc) {
+        const float* r = base + cc * stride + h * (2 + HD);
+        const float w = expf(ld(r) - M);
+        Ls = fmaf(ld(r + 1), w, Ls);
+        O = fmaf(ld(r + 2 + d), w, O);
+      }
+      s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / Ls);
+    }
   }
 }
 
@@ -237,125 +274,144 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
 // of an 8x8 ldmatrix block fall in distinct bank groups.
 __device__ __forceinline__ uint32_t kv_off(int r, int k) { return (uint32_t)(r * HD * 2 + ((k ^ (r & 7)) << 4)); }
 
-// One warp: sub-chunk c (virtual positions 32c..32c+31) of row t, kv head g, staged in buf
-// (K rows then V rows). Writes the record to rec (the K rows of buf).
-// kc, vc: the (layer, kv head) K and V caches; q: query row t (all heads).
-// The pass's own rows (this row's ancestors, slots >= pos) and the query come from the flagged
-// copies the QKV epilogue wrote (qw: row t's queries, kw / vw: kv head g's K / V rows of the pass),
-// polled until they carry `flag`; the cached prefix comes from the KV cache.
-__device__ __noinline__ void attn_warp(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, uint32_t flag,
-                                       vp_state* st, const __half* kc, const __half* vc,
-                                       const RowInfo* ri, int t, int g, int c, __half* buf, float* rec,
-                                       unsigned long long* tr) {
-  const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
-  if (tr && lane == 0) tr[0] = globaltimer();
+// Barrier of the warps that take part in a unit: the nw sub-chunk warps and the two polling warps
+// (named barrier 2; non-aligned form after a __syncwarp, as cons_sync).
+__device__ __forceinline__ void attn_sync(int nw) {
+  __syncwarp();
+  asm volatile("barrier.sync 2, %0;" ::"r"((nw + 2) * 32) : "memory");
+}
+
+// Sub-chunk warp, first half: stage the cached rows of sub-chunk c (virtual positions 32c..32c+31)
+// of row t: K rows then V rows (two cp.async groups, so S can start once K has landed). Lane copies
+// 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8. Positions past the row are zeros; the
+// pass's own rows (positions pos..L-1) are left to the polling warp.
+__device__ __forceinline__ void attn_stage(const __half* kc, const __half* vc, const RowInfo* ri, int t, int c,
+                                           __half* buf) {
+  const int lane = threadIdx.x & 31;
   const int pos = ri->pos, L = pos + ri->depth[t] + 1;
-  bool late = false;  // a poll gave up (bounded wait): error bit set, zeros used
-  // stage the K rows, then the V rows (two cp.async groups: S starts once K has landed, V keeps
-  // arriving behind it): lane copies 16-byte chunk (lane & 7) of rows (lane >> 3) + 4k, k < 8;
-  // positions past the row are zeros
-  {
-    const uint64_t pol = policy_evict_last();
-    const int ch = lane & 7;
-    uint8_t* dk = reinterpret_cast<uint8_t*>(buf);
-    size_t src[8];
-    uint32_t nb[8];
-    int prow[8];     // pass row of position r (an ancestor) or -1 (cached slot or past the row)
+  const uint64_t pol = policy_evict_last();
+  const int ch = lane & 7;
+  uint8_t* dk = reinterpret_cast<uint8_t*>(buf);
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    const __half* src = kv ? vc : kc;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int r = (lane >> 3) + 4 * k, jv = c * ATT_SUB + r;
-      const bool valid = jv < L;
-      prow[k] = valid && jv >= pos ? ri->path[t][min(jv - pos, ROWS - 1)] : -1;
-      src[k] = (size_t)(valid && jv < pos ? jv : 0) * HD + ch * 8;
-      nb[k] = valid ? 16u : 0u;
-      if (prow[k] < 0) cp_async16(dk + kv_off(r, ch), kc + src[k], nb[k], pol);
+      if (jv < pos || jv >= L)
+        cp_async16(dk + kv * ATT_SUB * HD * 2 + kv_off(r, ch), src + (size_t)(jv < L ? jv : 0) * HD + ch * 8,
+                   jv < L ? 16u : 0u, pol);
     }
     cp_async_commit();
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (prow[k] < 0) cp_async16(dk + ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch), vc + src[k], nb[k], pol);
-    cp_async_commit();
-    // the pass's rows: 16-byte chunk ch of the row = flagged words 4ch .. 4ch + 3
-    uint32_t pend = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (prow[k] >= 0) pend |= 3u << (2 * k);  // bit 2k: K, 2k + 1: V
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-#pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
-          if (!(pend >> (2 * k + kv) & 1u)) continue;
-          const uint64_t* w = (kv ? vw : kw) + (size_t)prow[k] * (HD / 2) + 4 * ch;
-          uint64_t a0, a1, a2, a3;
-          ld_flagged2(w, a0, a1);
-          ld_flagged2(w + 2, a2, a3);
-          if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag && (uint32_t)(a2 >> 32) == flag &&
-              (uint32_t)(a3 >> 32) == flag) {
-            *reinterpret_cast<uint4*>(dk + kv * ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch)) =
-                make_uint4((uint32_t)a0, (uint32_t)a1, (uint32_t)a2, (uint32_t)a3);
-            pend &= ~(1u << (2 * k + kv));
-          }
-        }
-      if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
-    }
-    if (pend) {
-      late = true;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-#pragma unroll
-        for (int kv = 0; kv < 2; ++kv)
-          if (pend >> (2 * k + kv) & 1u)
-            *reinterpret_cast<uint4*>(dk + kv * ATT_SUB * HD * 2 + kv_off((lane >> 3) + 4 * k, ch)) =
-                make_uint4(0u, 0u, 0u, 0u);
-    }
   }
-  // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero)
+}
+
+// Polling warp ATT_WQ: the 7 query rows (fp32) of row t for kv head g, as flagged words, into sm.q.
+__device__ __noinline__ void attn_poll_q(const uint64_t* qw, uint32_t flag, AttnSmem& sm) {
+  const int lane = threadIdx.x & 31;
+  constexpr int PER = GQ * HD / 2 / 32;  // 16-byte loads (two words) per lane: 7
+  uint32_t pend = (1u << PER) - 1u;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      if (!(pend >> k & 1u)) continue;
+      const int u = lane + 32 * k;  // words 2u, 2u + 1
+      uint64_t a, b;
+      ld_flagged2(qw + 2 * u, a, b);
+      if ((uint32_t)(a >> 32) == flag && (uint32_t)(b >> 32) == flag) {
+        reinterpret_cast<float2*>(&sm.q[0][0])[u] = make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+        pend &= ~(1u << k);
+      }
+    }
+    if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+  }
+  if (pend) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k)
+      if (pend >> k & 1u) reinterpret_cast<float2*>(&sm.q[0][0])[lane + 32 * k] = make_float2(0.f, 0.f);
+  }
+  if (__any_sync(0xffffffffu, pend != 0) && lane == 0) sm.late = 1;
+}
+
+// Polling warp ATT_WKV: the pass rows among the segment's positions (row t's ancestors at virtual
+// positions pos..L-1 in sub-chunks c0..c1-1), K and V from the flagged words of the QKV stage, into
+// the staging buffers (sub-chunk c in buffer c - c0). Lane: 16-byte chunk (lane & 7) of rows.
+__device__ __noinline__ void attn_poll_rows(const uint64_t* kw, const uint64_t* vw, uint32_t flag, const RowInfo* ri,
+                                            int t, int c0, int c1, AttnSmem& sm) {
+  const int lane = threadIdx.x & 31, ch = lane & 7;
+  const int pos = ri->pos, L = pos + ri->depth[t] + 1;
+  const int j0 = max(pos, c0 * ATT_SUB), j1 = min(L, c1 * ATT_SUB);  // positions to fill
+  bool late = false;
+  // at most 16 pass rows: lane handles rows (lane >> 3) + 4k of the range, k < 4, K and V
+  uint32_t pend = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (j0 + (lane >> 3) + 4 * k < j1) pend |= 3u << (2 * k);
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv) {
+        if (!(pend >> (2 * k + kv) & 1u)) continue;
+        const int jv = j0 + (lane >> 3) + 4 * k;
+        const int prow = ri->path[t][min(jv - pos, ROWS - 1)];
+        const uint64_t* w = (kv ? vw : kw) + (size_t)prow * (HD / 2) + 4 * ch;
+        uint64_t a0, a1, a2, a3;
+        ld_flagged2(w, a0, a1);
+        ld_flagged2(w + 2, a2, a3);
+        if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag && (uint32_t)(a2 >> 32) == flag &&
+            (uint32_t)(a3 >> 32) == flag) {
+          const int c = jv / ATT_SUB, r = jv % ATT_SUB;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&sm.kv[c - c0][kv][0][0]) + kv_off(r, ch)) =
+              make_uint4((uint32_t)a0, (uint32_t)a1, (uint32_t)a2, (uint32_t)a3);
+          pend &= ~(1u << (2 * k + kv));
+        }
+      }
+    if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+  }
+  if (pend) {
+    late = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv)
+        if (pend >> (2 * k + kv) & 1u) {
+          const int jv = j0 + (lane >> 3) + 4 * k, c = jv / ATT_SUB, r = jv % ATT_SUB;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&sm.kv[c - c0][kv][0][0]) + kv_off(r, ch)) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+  }
+  if (__any_sync(0xffffffffu, late) && lane == 0) sm.late = 1;
+}
+
+// Sub-chunk warp, second half (after the unit's barrier): sub-chunk c of row t staged in buf (K
+// rows then V rows), queries in sm.q. Writes the record to rec (the K rows of buf).
+__device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const AttnSmem& sm, __half* buf,
+                                          float* rec, unsigned long long* tr) {
+#define ATT_DSTAMP(k, dep) do { if (tr) { const unsigned long long v_ = globaltimer_after(dep); if ((threadIdx.x & 31) == 0) tr[256 * (k)] = v_; } } while (0)
+  const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
+  const int L = ri->pos + ri->depth[t] + 1;
+  // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero):
+  // dims ks * 16 + 2 t4 + {0, 1} and + 8
   uint32_t qa[4][2][2];  // [k-step][hi, lo][a0, a2]
   {
-    // dims ks * 16 + 2 t4 + {0, 1} and + 8: two flagged words per 16-byte load
-    const uint64_t* q = qw + (g * GQ + min(gid, GQ - 1)) * HD;
-    float x[4][4];
-    uint32_t pend = 0xffu;  // bit 2 ks + half
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          if (!(pend >> (2 * ks + hh) & 1u)) continue;
-          uint64_t a0, a1;
-          ld_flagged2(q + ks * 16 + 2 * t4 + 8 * hh, a0, a1);
-          if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag) {
-            x[ks][2 * hh] = __uint_as_float((uint32_t)a0);
-            x[ks][2 * hh + 1] = __uint_as_float((uint32_t)a1);
-            pend &= ~(1u << (2 * ks + hh));
-          }
-        }
-      if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
-    }
-    if (pend) {
-      late = true;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (pend >> (2 * ks + (i >> 1)) & 1u) x[ks][i] = 0.f;
-    }
-    if (__any_sync(0xffffffffu, late) && lane == 0) set_error(st, VP_DEV_ERR_TIMEOUT);
+    const float* q = &sm.q[min(gid, GQ - 1)][0];
     const float z = gid < GQ ? ATTN_SCALE : 0.f;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      split_half2(x[ks][0] * z, x[ks][1] * z, qa[ks][0][0], qa[ks][1][0]);
-      split_half2(x[ks][2] * z, x[ks][3] * z, qa[ks][0][1], qa[ks][1][1]);
+      const float2 x0 = *reinterpret_cast<const float2*>(q + ks * 16 + 2 * t4);
+      const float2 x1 = *reinterpret_cast<const float2*>(q + ks * 16 + 8 + 2 * t4);
+      split_half2(x0.x * z, x0.y * z, qa[ks][0][0], qa[ks][1][0]);
+      split_half2(x1.x * z, x1.y * z, qa[ks][0][1], qa[ks][1][1]);
     }
   }
-  if (tr && lane == 0) tr[1] = globaltimer_after(__uint_as_float(qa[3][1][1]));
+  ATT_DSTAMP(3, __uint_as_float(qa[3][1][1]));
   cp_async_wait<1>();  // the K rows (this lane's copies; __syncwarp makes the warp's visible)
   __syncwarp();
-  if (tr && lane == 0) tr[2] = globaltimer();
   const uint32_t sK = smem_u32(buf), sV = sK + ATT_SUB * HD * 2;
+  ATT_DSTAMP(4, __uint_as_float(*reinterpret_cast<const uint32_t*>(buf)));
   const int mi = lane >> 3, ri8 = lane & 7;  // ldmatrix: this lane addresses row ri8 of block mi
   // S = q K^T: n-tile j = positions 8j..8j+7; one x4 load gives the B fragments of two k-steps
   float sacc[4][4];
@@ -374,7 +430,7 @@ __device__ __noinline__ void attn_warp(const uint64_t* qw, const uint64_t* kw, c
       for (int part = 0; part < 2; ++part)
         mma16816(sacc[j], qa[ks][part][0], 0u, qa[ks][part][1], 0u, kb[ks][0], kb[ks][1]);
   }
-  if (tr && lane == 0) tr[3] = globaltimer_after(sacc[3][0]);
+  ATT_DSTAMP(5, sacc[3][0]);
   // masked softmax of query head gid over the 32 positions (position 8j + 2*t4 + e)
   const int cnt = L - c * ATT_SUB;
   float m = -INFINITY;
@@ -399,6 +455,7 @@ __device__ __noinline__ void attn_warp(const uint64_t* qw, const uint64_t* kw, c
   l += __shfl_xor_sync(0xffffffffu, l, 2);
   cp_async_wait<0>();  // the V rows
   __syncwarp();
+  ATT_DSTAMP(6, __uint_as_float(*reinterpret_cast<const uint32_t*>(buf + ATT_SUB * HD)) + l);
   // P as the A operand: k-step kk = positions 16kk..16kk+15 = n-tiles 2kk (a0) and 2kk+1 (a2)
   uint32_t pa[2][2][2];  // [kk][hi, lo][a0, a2]
 #pragma unroll
@@ -431,18 +488,14 @@ __device__ __noinline__ void attn_warp(const uint64_t* qw, const uint64_t* kw, c
   }
   if (gid < GQ && t4 == 0) { r[0] = m; r[1] = l; }
   __syncwarp();
-  if (tr && lane == 0) tr[4] = globaltimer();
+#undef ATT_DSTAMP
 }
 
 // One unit with PASS_THREADS threads: segment seg of (row t, kv head g).
+// tr (performance tracing only): per-warp stamps at tr[256 * (8 * warp + step)]; the polling warps
+// use steps 0 and 2 only, the unit-level stamps sit in warp 15's unused steps 5 and 7.
 __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, AttnSmem& sm,
-                          unsigned long long* trace = nullptr) {
-  int ntr = 0;
-  auto tstamp = [&]() {
-    if (trace && threadIdx.x == 0 && ntr < 8) trace[ntr] = globaltimer();
-    ++ntr;
-  };
-  tstamp();
+                          unsigned long long* tr = nullptr) {
   const RowInfo* ri = s.ri;
   const int tid = threadIdx.x, warp = tid >> 5;
   int t = 0, rem = u, nsub = 1, nseg = 1;
@@ -453,21 +506,40 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, Attn
     rem -= NKV * nseg;
   }
   const int g = rem / nseg, seg = rem % nseg;
-  const int c0 = seg * ATT_SEGSUB, c1 = min(nsub, c0 + ATT_SEGSUB);
+  const int c0 = seg * ATT_SEGSUB, c1 = min(nsub, c0 + ATT_SEGSUB), nw = c1 - c0;
   float* rec0 = reinterpret_cast<float*>(&sm.kv[0][0][0][0]);
-  if (c0 + warp < c1) {
-    const size_t cache = (size_t)(layer * NKV + g) * s.max_ctx * HD;
-    const size_t kvw = (size_t)ROWS * (HD / 2);
-    attn_warp(s.q_ll + t * H, s.kv_ll + g * kvw, s.kv_ll + (NKV + g) * kvw, s.flag_q, s.st, s.kc + cache,
-              s.vc + cache, ri, t, g, c0 + warp, &sm.kv[warp][0][0][0], rec0 + warp * ATT_REC_STRIDE,
-              trace ? trace + 8 + 8 * warp : nullptr);
+  const size_t cache = (size_t)(layer * NKV + g) * s.max_ctx * HD;
+  const size_t kvw = (size_t)ROWS * (HD / 2);
+#define ATT_TSTAMP(k) do { if (tr && (tid & 31) == 0) tr[256 * (8 * warp + (k))] = globaltimer(); } while (0)
+  if (tid == 0) sm.late = 0;
+  cons_sync();
+  ATT_TSTAMP(0);
+  if (warp < nw) {
+    attn_stage(s.kc + cache, s.vc + cache, ri, t, c0 + warp, &sm.kv[warp][0][0][0]);
+    ATT_TSTAMP(1);
+    attn_sync(nw);
+  } else if (warp == ATT_WQ) {
+    attn_poll_q(s.q_ll + t * H + g * GQ * HD, s.flag_q, sm);
+    ATT_TSTAMP(2);
+    attn_sync(nw);
+  } else if (warp == ATT_WKV) {
+    attn_poll_rows(s.kv_ll + g * kvw, s.kv_ll + (NKV + g) * kvw, s.flag_q, ri, t, c0, c1, sm);
+    ATT_TSTAMP(2);
+    attn_sync(nw);
+  }
+  if (warp < nw) {
+    attn_compute(ri, t, c0 + warp, sm, &sm.kv[warp][0][0][0], rec0 + warp * ATT_REC_STRIDE,
+                 tr ? tr + 256 * 8 * warp : nullptr);
+    ATT_TSTAMP(7);
   }
   cons_sync();
-  tstamp();
+  if (tid == 0 && sm.late) set_error(s.st, VP_DEV_ERR_TIMEOUT);
+  if (tr && tid == 0) tr[256 * 125] = globaltimer();
+#undef ATT_TSTAMP
   if (nseg == 1) {
-    attn_combine<false>(s, rec0, ATT_REC_STRIDE, nsub, t, g);
+    attn_combine<false>(s, rec0, ATT_REC_STRIDE, nsub, t, g, sm);
     cons_sync();
-    tstamp();
+    if (tr && tid == 0) tr[256 * 127] = globaltimer();
     return;
   }
   float* base = s.att_part + (size_t)(t * NKV + g) * max_subs * ATT_REC;
@@ -479,11 +551,10 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, Attn
   cons_sync();
   if (sm.last) {
     __threadfence();
-    attn_combine<true>(s, base, ATT_REC, nsub, t, g);
+    attn_combine<true>(s, base, ATT_REC, nsub, t, g, sm);
     if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
   }
   cons_sync();
-  tstamp();
 }
 
 }  // namespace vp

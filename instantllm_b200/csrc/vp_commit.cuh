@@ -70,15 +70,19 @@ __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx
     st->passes += 1;
     st->accepted += m;
     bool stop = false;
-    int last = st->last_token;
+    int last = st->last_token, nc = 0;
     for (int i = 0; i <= m && !stop; ++i) {
       const int tok = g[i == 0 ? 0 : path[i - 1]];
       if (st->step >= s.max_steps) { atomicOr(&st->err, VP_DEV_ERR_STEPS); stop = true; break; }
       s.out_tokens[st->step] = tok;
+      if (s.pass_tok) s.pass_tok[nc] = tok;
+      ++nc;
       st->step += 1;
       last = tok;
       if (tok == st->eos0 || tok == st->eos1 || st->step >= st->maxsteps) stop = true;
     }
+    if (s.pass_tok)
+      for (int i = nc; i < ROWS; ++i) s.pass_tok[i] = -1;
     sPos0 = st->pos;
     sNpath = tree ? m : 0;
     st->pos += ri->mode == 1 ? st->advance : m + 1;

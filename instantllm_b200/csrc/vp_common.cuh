@@ -69,6 +69,7 @@ struct Scratch {
   RowInfo* ri;
   int32_t* tree;        // VP_TREE_INTS
   int32_t* out_tokens;  // max_steps
+  int32_t* pass_tok;    // [16] tokens the last commit added to out_tokens, then -1
   float* x;             // [16][896] residual stream, fp32
   float* q;             // [16][896] roped queries, fp32
   __half* act_h;        // act blocks, K = 896: normed x for QKV / GU / lm_head

@@ -31,7 +31,10 @@ struct ArgmaxKeys {
   unsigned long long best[16];
   unsigned done;  // CTAs finished
 };
+// NaN gets 0, below every number (-inf included): like the commit kernel's `v > best`, which never
+// selects a NaN logit while a number exists.
 __device__ __forceinline__ unsigned ordered_bits(float f) {
+  if (f != f) return 0u;
   const unsigned u = __float_as_uint(f + 0.f);  // -0 -> +0: equal floats get equal keys
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }

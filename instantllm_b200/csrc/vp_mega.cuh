@@ -27,20 +27,29 @@ constexpr int MK_THREADS = MK_CONS + 32;         // + the producer warp
 constexpr int MK_NSLOT = 5;                      // weight ring slots
 constexpr int MK_SLOT = 28672;                   // bytes per slot
 constexpr int MK_PART_SLOTS = 24;                // partial tiles of a stage (1 KiB each)
-constexpr int MK_TRACE = 2048;  // trace slots: [0, 256) stage ends of CTA 0; the rest detail stamps
+// Stage trace: trace[0, 256) holds CTA 0's %globaltimer after each grid barrier of a launch.
+// Compiled with -DVP_TRACE_DETAIL (performance work only), every CTA also stamps the steps of
+// layer MK_TRACE_LAYER (and of the lm_head stage) at trace[MK_TRACE_BASE + 256 * event + cta]:
+// events 8 * stage + step for the GEMM stages (step 0 entry, 1 inputs in shared memory, 2 group
+// sums, 3 jobs done, 4 pieces released, 5 epilogue done), 40 / 41 / 42 attention unit start /
+// records done / combined, 48 + 2k / 49 + 2k arrival at / exit from the k-th grid barrier of the
+// layer, 56 layer start.
+constexpr int MK_TRACE_BASE = 2048;
+constexpr int MK_TRACE_LAYER = 5;
+#ifdef VP_TRACE_DETAIL
+constexpr int MK_TRACE = MK_TRACE_BASE + (64 + 16 * 8 + 96) * 256;
+#define MK_CSTAMP(p, cond, ev)                                                                   \
+  do {                                                                                           \
+    if ((p).trace && threadIdx.x == 0 && (cond) && blockIdx.x < 256)                             \
+      (p).trace[MK_TRACE_BASE + 256 * (ev) + blockIdx.x] = globaltimer();                        \
+  } while (0)
+#else
+constexpr int MK_TRACE = MK_TRACE_BASE;
+#define MK_CSTAMP(p, cond, ev) do {} while (0)
+#endif
 static_assert(MK_CONS == PASS_THREADS && MK_CONS == CONS_THREADS, "consumer warps run the stage code");
 
 enum MkStage { MK_QKV = 0, MK_O = 1, MK_GU = 2, MK_DOWN = 3, MK_LM = 4 };
-
-// Detail timeline for performance work (compiled in only with -DVP_TRACE_DETAIL): CTA 0 stamps the
-// steps of each GEMM stage of layer 5 and of the lm_head stage at trace[256 + 8 * stage + step],
-// and every CTA stamps its grid-barrier arrivals of layer 5 at trace[512 + 148 * k + cta].
-#ifdef VP_TRACE_DETAIL
-#define MK_DSTAMP(p, cond, idx) \
-  do { if ((p).trace && blockIdx.x == 0 && threadIdx.x == 0 && (cond)) (p).trace[(idx)] = globaltimer(); } while (0)
-#else
-#define MK_DSTAMP(p, cond, idx) do {} while (0)
-#endif
 
 // Parts per row-block (K split across the warps of one CTA) of a GEMM stage whose CTA owns nrb
 // row-blocks, and K groups of each GEMM stage. Gate/up fills the 16 warps once: 4 row-blocks x 4
@@ -164,10 +173,13 @@ constexpr size_t MK_OFF_ACT = MK_RING_BYTES;
 constexpr size_t MK_OFF_X = MK_OFF_ACT + MK_ACT_BYTES;            // group sums
 constexpr size_t MK_X_BYTES = 2 * 16 * 16 * 4;  // group sums [14 groups][halves][16 tokens]
 constexpr size_t MK_OFF_PART = MK_OFF_X + MK_X_BYTES;            // partial tiles
-// attention scratch overlays the act blocks, group sums and partial tiles (and extends past them)
-constexpr size_t MK_OVERLAY = sizeof(AttnSmem) > MK_ACT_BYTES + MK_X_BYTES + MK_PART_SLOTS * 1024
-                                  ? ((sizeof(AttnSmem) + 127) & ~size_t(127))
-                                  : MK_ACT_BYTES + MK_X_BYTES + MK_PART_SLOTS * 1024;
+// The overlay holds, by stage: the act blocks, group sums and partial tiles of a GEMM stage; the
+// attention scratch; the down projection's 16 partial tiles and 32 act staging buffers (15 below
+// the partial tiles, 17 above).
+constexpr size_t mk_max(size_t a, size_t b) { return a > b ? a : b; }
+constexpr size_t MK_OVERLAY =
+    mk_max(mk_max((sizeof(AttnSmem) + 127) & ~size_t(127), MK_ACT_BYTES + MK_X_BYTES + MK_PART_SLOTS * 1024),
+           MK_ACT_BYTES + MK_X_BYTES + 16 * 1024 + 17 * 2048);
 constexpr size_t MK_OFF_RS = MK_OFF_ACT + MK_OVERLAY;              // rscale[16]
 constexpr size_t MK_OFF_LMV = MK_OFF_RS + 64;                     // [16 warps][16] best value
 constexpr size_t MK_OFF_LMI = MK_OFF_LMV + 1024;                  // [16 warps][16] best id
@@ -341,13 +353,18 @@ __device__ __forceinline__ void mk_tiles(const uint8_t* const (&tile)[NT], int g
     for (int j = 0; j < 4; ++j) bf[u][j] = act_frag_smem(sAct, g + u, j, lane);
   mk_tiles_bf<FMT, false, NT>(tile, g, bf, sX, lane, acc);
 }
-static_assert(mk_parts(MK_DOWN, 1) * 1024 + (MK_WARPS - H / GS) * 2048 <= MK_PART_SLOTS * 1024,
-              "down-projection staging buffers of warps 14 and 15 sit past the 16 partial tiles");
-// Down projection: per-warp 2 KiB staging buffer of one act block. The act blocks area is free
-// in that stage (14 buffers); warps 14 and 15 use the partial-tile area past the 16 partials.
-__device__ __forceinline__ uint8_t* mk_down_stage(uint8_t* sAct, float* sPart, int warp) {
-  return warp < H / GS ? sAct + (size_t)warp * 2048
-                       : reinterpret_cast<uint8_t*>(sPart) + (size_t)(16 + 2 * (warp - H / GS)) * 1024;
+// Down projection: two 2 KiB staging buffers of act blocks per warp, so that two blocks are in
+// flight while a third computes. In that stage the overlay holds only the 16 partial tiles (at
+// MK_OFF_PART); the 32 buffers fill the rest of it: 15 below the partial tiles (the act blocks and
+// group sums areas), 17 above them.
+constexpr int MK_DOWN_BUFS = 2 * MK_WARPS;
+constexpr size_t MK_DOWN_LOW = (MK_OFF_PART - MK_OFF_ACT) / 2048;                    // 15
+constexpr size_t MK_DOWN_HIGH = MK_OFF_PART - MK_OFF_ACT + (size_t)mk_parts(MK_DOWN, 1) * 1024;
+static_assert(MK_DOWN_LOW == 15, "act blocks + group sums hold 15 staging buffers");
+static_assert(MK_DOWN_HIGH + (MK_DOWN_BUFS - MK_DOWN_LOW) * 2048 <= MK_OVERLAY,
+              "down-projection staging buffers fit the overlay past the partial tiles");
+__device__ __forceinline__ uint8_t* mk_down_stage(uint8_t* smem, int b) {
+  return smem + MK_OFF_ACT + (b < (int)MK_DOWN_LOW ? (size_t)b * 2048 : MK_DOWN_HIGH + (size_t)(b - MK_DOWN_LOW) * 2048);
 }
 
 // Wait until piece k is in the ring (bounded); returns its slot base or null on timeout.
@@ -381,6 +398,7 @@ __device__ __forceinline__ bool mk_release(MkRing& rg, int k, int lane) {
 struct MkJobs {
   int piece0, rb0, nrb, P, ng;
   const __half* actg;    // down projection: act blocks of the SiLU output
+  unsigned long long* trace;  // performance tracing only (null: off)
 };
 // What a stage's jobs are, fixed at compile time so that each stage's code holds only its own
 // loop (instruction-cache footprint): activations in shared memory and partial tiles out (QKV,
@@ -411,32 +429,53 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
     const int ga = q * ng / P, gb = (q + 1) * ng / P;
     float acc[2][4] = {};
     if constexpr (down) {
-      // one tile per step, software-pipelined: the act block of tile g + 1 streams from L2 into
-      // this warp's 2 KiB staging buffer (cp.async, each lane its own fragments) while tile g
-      // computes; the first copy overlaps the wait for the weights
-      uint8_t* sB = mk_down_stage(sAct, sPart, warp);
+      // one tile per step, software-pipelined: the act blocks of tiles g + 1 and g + 2 stream from
+      // L2 into this warp's two staging buffers (cp.async, each lane its own fragments) while tile
+      // g computes from registers; the first copies overlap the wait for the weights
+      uint8_t* const sB[2] = {mk_down_stage(smem, 2 * warp), mk_down_stage(smem, 2 * warp + 1)};
       const uint64_t pol = policy_evict_last();
       auto fetch = [&](int g) {
+        uint8_t* b = sB[(g - ga) & 1];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          cp_async16(sB + j * 512 + lane * 16, J.actg + (size_t)g * 1024 + j * 256 + lane * 8, 16u, pol);
+          cp_async16(b + j * 512 + lane * 16, J.actg + (size_t)g * 1024 + j * 256 + lane * 8, 16u, pol);
         cp_async_commit();
       };
       if (ga < gb) fetch(ga);
+      if (ga + 1 < gb) fetch(ga + 1);
+#ifdef VP_TRACE_DETAIL
+      // per-tile stamps of warps 0..3 of the traced layer: [warp][tile][piece ready, act landed, done]
+      unsigned long long* dtr = (J.trace && warp < 4) ? J.trace + MK_TRACE_BASE + 192 * 256 + blockIdx.x : nullptr;
+      auto dst = [&](int k, float dep) {
+        if (dtr) { const unsigned long long v = globaltimer_after(dep); if (lane == 0) dtr[256 * k] = v; }
+      };
+#endif
       for (int g = ga; g < gb; ++g) {
         const int idx = i * ng + g;
         const int k = piece0 + idx / tp;
         if (!mk_release(rg, k, lane)) { ok = false; break; }
         const uint8_t* base = mk_piece(rg, k);
         if (!base) { ok = false; break; }
-        cp_async_wait<0>();
+#ifdef VP_TRACE_DETAIL
+        dst(warp * 24 + (g - ga) * 3 + 0, __uint_as_float(*reinterpret_cast<const uint32_t*>(base)));
+#endif
+        if (g + 1 < gb) cp_async_wait<1>();  // block g landed (g + 1 may still be in flight)
+        else cp_async_wait<0>();
         __syncwarp();  // converged before the warp-collective MMAs
         uint4 bf[1][4];
+        const uint8_t* b = sB[(g - ga) & 1];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) bf[0][j] = *reinterpret_cast<const uint4*>(sB + j * 512 + lane * 16);
-        if (g + 1 < gb) fetch(g + 1);
+        for (int j = 0; j < 4; ++j) bf[0][j] = *reinterpret_cast<const uint4*>(b + j * 512 + lane * 16);
+#ifdef VP_TRACE_DETAIL
+        dst(warp * 24 + (g - ga) * 3 + 1, __uint_as_float(bf[0][3].w));
+#endif
+        __syncwarp();  // every lane holds its fragments before the buffer is refilled
+        if (g + 2 < gb) fetch(g + 2);
         const uint8_t* const tt[1] = {base + (size_t)(idx % tp) * TB};
         mk_tiles_bf<FMT, true, 1>(tt, g, bf, sX, lane, acc);
+#ifdef VP_TRACE_DETAIL
+        dst(warp * 24 + (g - ga) * 3 + 2, acc[1][3]);
+#endif
       }
       cp_async_wait<0>();
     } else {
@@ -666,10 +705,9 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
   constexpr bool down = DOWN;
-#ifdef VP_TRACE_DETAIL
-  const bool dtr = gp.layer == 5 || MODE == MODE_ARGMAX;
-#endif
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 0);
+  const bool dtr = gp.layer == MK_TRACE_LAYER || MODE == MODE_ARGMAX;
+  (void)dtr;
+  MK_CSTAMP(p, dtr, 8 * st + 0);
   // the act blocks (K = 896 stages) and the RMSNorm scale of the input rows in one round trip: the
   // act copies are in flight while the partial sums load (all 56 at once, summed in fixed order)
   // (the partials land in the partial-tile area, which is free until the jobs start)
@@ -701,7 +739,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
     if (gp.act_ll_in) mk_poll_flagged(gp.act_ll_in, gp.ss_ll_in, gp.flag, sAct, sSs, gp.s.st, sAbort);
   }
   mk_sync();
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 1);
+  MK_CSTAMP(p, dtr, 8 * st + 1);
   if (MODE != MODE_RESID && warp == MK_WARPS - 1 && lane < 16) {
     float sum = 0.f;
     for (int r = 0; r < HRB; ++r) sum += sSs[r * 16 + lane];
@@ -730,17 +768,18 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
     }
   }
   mk_sync();
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 2);
+  MK_CSTAMP(p, dtr, 8 * st + 2);
 
   const int npieces = (nrb * ng + tp - 1) / tp;
   MkJobs J;
   J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.actg = gp.act;
+  J.trace = (gp.layer == MK_TRACE_LAYER && MODE != MODE_ARGMAX) ? p.trace : nullptr;
   constexpr int KIND = DOWN ? JOB_DOWN : MODE == MODE_ARGMAX ? JOB_ARGMAX : JOB_SMEM;
   const int2 rs2 = mk_jobs<FMT, KIND>(J, rg, smem);
   bool ok = rs2.x >= 0;
   if (ok) rg.released = rs2.x;
   rg.waited = rs2.y;
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 3);
+  MK_CSTAMP(p, dtr, 8 * st + 3);
   // this warp is done with every piece of the stage
   if (ok) ok = mk_release(rg, piece0 + npieces, lane);
   if (!ok) {
@@ -748,10 +787,10 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
     *sAbort = 1;
   }
   mk_sync();
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 4);
+  MK_CSTAMP(p, dtr, 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
   if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE>(gp, rb0, nrb, P, sPart, sRs, sEpc);
-  MK_DSTAMP(p, dtr, 256 + 8 * st + 5);
+  MK_CSTAMP(p, dtr, 8 * st + 5);
   return true;
 }
 
@@ -787,15 +826,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
       ++nstamp;
     };
     stamp();
+    int tl = -1, tb = 0;  // layer being run (trace) and grid barriers taken in it
     auto barrier = [&]() -> bool {
-#ifdef VP_TRACE_DETAIL
-      if (p.trace && threadIdx.x == 0) {
-        const int k = nstamp >= 27 && nstamp < 32 ? nstamp - 27 : nstamp == 2 + 5 * p.n_layers ? 5 : -1;
-        if (k >= 0 && G <= 148) p.trace[512 + 148 * k + cta] = globaltimer();
-      }
-#endif
+      MK_CSTAMP(p, tl == MK_TRACE_LAYER, 48 + 2 * tb);
       target += (unsigned long long)G;
       const bool r = grid_barrier(p, target, &sAbort);
+      MK_CSTAMP(p, tl == MK_TRACE_LAYER, 49 + 2 * tb);
+      ++tb;
       stamp();
       return r;
     };
@@ -844,6 +881,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
 
     if (live) {
       for (int l = 0; l < p.n_layers && ok; ++l) {
+        tl = l;
+        tb = 0;
+        MK_CSTAMP(p, l == MK_TRACE_LAYER, 56);
         GemmParams gp = {};
         gp.s = s;
         gp.layer = l;
@@ -861,13 +901,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         // attention
         {
           const int units = attn_units(sRi);
-          for (int u = cta; u < units; u += G)
-            attn_unit(s, l, p.max_chunks, u, sAtt,
+          for (int u = cta; u < units; u += G) {
+            MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 40);
 #ifdef VP_TRACE_DETAIL
-                      (p.trace && cta == 0 && l == 5 && u == 0) ? p.trace + 300 : nullptr);
+            attn_unit(s, l, p.max_chunks, u, sAtt,
+                      (p.trace && l == MK_TRACE_LAYER && u == cta && cta < 256)
+                          ? p.trace + MK_TRACE_BASE + 64 * 256 + cta : nullptr);
 #else
-                      nullptr);
+            attn_unit(s, l, p.max_chunks, u, sAtt);
 #endif
+            MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 42);
+          }
         }
         ok = barrier();
         if (!ok) break;

@@ -75,14 +75,17 @@ struct vp_ctx {
   float* lm_pval = nullptr;  // [16][grid] per-CTA argmax partials of the last pass
   int* lm_pidx = nullptr;
   unsigned long long* trace = nullptr;  // stage timestamps of the last pass (ns)
-  unsigned char* io = nullptr;   // device: state (64 B) then the tree, one block for one copy in
-  unsigned char* pin = nullptr;  // pinned host staging of vp_step: state + tree in, state out
+  // device: the state (64 B), the tokens of the last commit (16 int32) and the tree, adjacent so
+  // that vp_step moves its inputs in one copy and its results (state + tokens) in one copy
+  unsigned char* io = nullptr;
+  unsigned char* pin = nullptr;  // pinned host staging of vp_step: the io block in, its head out
 };
 
-constexpr size_t IO_TREE = 64;                                  // tree offset in ctx->io
+constexpr size_t IO_TOK = 64;                                   // pass-token offset in ctx->io
+constexpr size_t IO_TREE = IO_TOK + ROWS * sizeof(int32_t);     // tree offset in ctx->io
 constexpr size_t IO_BYTES = IO_TREE + VP_TREE_INTS * sizeof(int32_t);
-constexpr size_t PIN_OUT = 512;                                 // state-out offset in ctx->pin
-static_assert(sizeof(vp_state) <= IO_TREE && IO_BYTES <= PIN_OUT, "io layout");
+constexpr size_t PIN_OUT = 512;                                 // result offset in ctx->pin
+static_assert(sizeof(vp_state) <= IO_TOK && IO_BYTES <= PIN_OUT, "io layout");
 
 namespace {
 
@@ -282,9 +285,10 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
     return r;
   }
   s.st = reinterpret_cast<vp_state*>(c->io);
+  s.pass_tok = reinterpret_cast<int32_t*>(c->io + IO_TOK);
   s.tree = reinterpret_cast<int32_t*>(c->io + IO_TREE);
   {
-    cudaError_t e = cudaHostAlloc(&c->pin, PIN_OUT + sizeof(vp_state), cudaHostAllocDefault);
+    cudaError_t e = cudaHostAlloc(&c->pin, PIN_OUT + IO_TREE, cudaHostAllocDefault);
     if (e != cudaSuccess) {
       c->pin = nullptr;
       vp_destroy(c);
@@ -444,14 +448,17 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
 }
 
 int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
-            void* stream) {
+            int32_t* tokens_out, void* stream) {
   int r = check_ctx(c);
   if (r) return r;
   if (!tree || !state_out) return fail(VP_ERR_ARG, "null tree or state_out");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The previous call synchronised this stream, so the staging block is free to reuse.
+  // The previous call synchronised this stream (also on its error paths), so the staging block is
+  // free to reuse.
   std::memcpy(c->pin + IO_TREE, tree, VP_TREE_INTS * sizeof(int32_t));
-  size_t off = IO_TREE;
+  // no tokens unless the commit runs (a finished or failed request skips it)
+  std::memset(c->pin + IO_TOK, 0xff, IO_TREE - IO_TOK);
+  size_t off = IO_TOK;
   if (state_in) {
     std::memcpy(c->pin, state_in, sizeof(vp_state));
     off = 0;
@@ -460,10 +467,16 @@ int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* 
   MegaParams p = mega_params(c);
   p.do_lm = 1;
   p.do_commit = 1;
-  if ((r = launch_pass(c, p, st))) return r;
-  VP_CUDA(cudaMemcpyAsync(c->pin + PIN_OUT, c->s.st, sizeof(vp_state), cudaMemcpyDeviceToHost, st));
-  VP_CUDA(cudaStreamSynchronize(st));
+  r = launch_pass(c, p, st);
+  if (r == VP_OK) {
+    const cudaError_t e = cudaMemcpyAsync(c->pin + PIN_OUT, c->io, IO_TREE, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) r = fail(VP_ERR_CUDA, std::string("cudaMemcpyAsync: ") + cudaGetErrorString(e));
+  }
+  const cudaError_t se = cudaStreamSynchronize(st);  // also on failure: the staging block is in use
+  if (r) return r;
+  if (se != cudaSuccess) return fail(VP_ERR_CUDA, std::string("cudaStreamSynchronize: ") + cudaGetErrorString(se));
   std::memcpy(state_out, c->pin + PIN_OUT, sizeof(vp_state));
+  if (tokens_out) std::memcpy(tokens_out, c->pin + PIN_OUT + IO_TOK, ROWS * sizeof(int32_t));
   return state_out->err ? VP_ERR_DEVICE : VP_OK;
 }
 
@@ -622,11 +635,12 @@ __global__ void k_sk_prep(const float* x, const float* wnorm, int rows, __half* 
   }
 }
 
+// Per-device set-up state. Only a successful look-up is kept: a failed one (for example a first
+// call made during stream capture) is retried by the next call.
 struct NoAllocDevice {
-  std::once_flag once;
+  std::mutex mu;
+  bool ready = false;
   void* base = nullptr;
-  int rc = VP_OK;
-  std::string msg;
 };
 NoAllocDevice g_na_dev[64];
 
@@ -644,19 +658,18 @@ cudaError_t na_smem_attr() {
 // Once per device, with that device current: the device address of the static scratch array.
 int na_setup(int dev, unsigned char** base) {
   NoAllocDevice& d = g_na_dev[dev];
-  std::call_once(d.once, [&d]() {
-    cudaError_t e = cudaGetSymbolAddress(&d.base, g_noalloc_scratch);
+  std::lock_guard<std::mutex> lock(d.mu);
+  if (!d.ready) {
+    void* b = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&b, g_noalloc_scratch);
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q4>();
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q8>();
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_Q8G32>();
     if (e == cudaSuccess) e = na_smem_attr<VP_FMT_F16>();
-    if (e != cudaSuccess) {
-      d.base = nullptr;
-      d.rc = VP_ERR_CUDA;
-      d.msg = std::string("no-alloc set-up: ") + cudaGetErrorString(e);
-    }
-  });
-  if (d.rc != VP_OK) return fail(d.rc, d.msg);
+    if (e != cudaSuccess) return fail(VP_ERR_CUDA, std::string("no-alloc set-up: ") + cudaGetErrorString(e));
+    d.base = b;
+    d.ready = true;
+  }
   *base = static_cast<unsigned char*>(d.base);
   return VP_OK;
 }

@@ -34,6 +34,8 @@ class _DevArray:
 
 def _np_to_dev(a: np.ndarray, device) -> torch.Tensor:
     a = np.ascontiguousarray(a)
+    if not a.flags.writeable:  # torch.from_numpy wants a writable buffer (read-only views warn)
+        a = a.copy()
     if a.dtype == np.float16:
         a = a.view(np.uint16)
     return torch.from_numpy(a.view(np.uint8).reshape(-1)).to(device)
@@ -76,6 +78,7 @@ class VerifyEngine:
         self._prompt = torch.empty(max_ctx, dtype=torch.int32, device=self.device)
         self._tree_host = torch.empty(TREE_INTS, dtype=torch.int32).pin_memory()
         self._step_out = VpState()
+        self._step_tok = np.full(16, -1, dtype=np.int32)
 
     # ---- weights ----
     def _pack(self, m: dict, kind: int) -> int:
@@ -162,17 +165,23 @@ class VerifyEngine:
 
     def step(self, tree, state_in: Optional[VpState] = None) -> VpState:
         """One decode step from host memory (vp_step): optionally write `state_in`, copy the tree,
-        run the pass (verify + commit), read the state back; synchronises. Returns the state as a
-        VpState (fields as attributes, `.as_dict()`); the same object is refilled by the next call,
-        so copy it (`.as_dict()`) to keep it."""
+        run the pass (verify + commit), read the state and this pass's committed tokens back;
+        synchronises. Returns the state as a VpState (fields as attributes, `.as_dict()`); the
+        committed tokens are in `last_tokens()`. Both are refilled by the next call: copy them to
+        keep them."""
         buf = tree if isinstance(tree, np.ndarray) else tree_to_buffer(tree)
         buf = np.ascontiguousarray(buf, dtype=np.int32)
         out = self._step_out
         rc = self.lib.vp_step(self.ctx, ctypes.addressof(state_in) if state_in is not None else None,
-                              buf.ctypes.data, ctypes.byref(out), self._s)
+                              buf.ctypes.data, ctypes.byref(out), self._step_tok.ctypes.data, self._s)
         if rc not in (0, -5):
             check(rc, "vp_step")
         return out
+
+    def last_tokens(self) -> list:
+        """Tokens the last step() committed, in order."""
+        t = self._step_tok
+        return t[:int(np.argmax(t < 0)) if (t < 0).any() else t.size].tolist()
 
     def pass_device(self, tree_dev: torch.Tensor) -> None:
         """Graph pass with a device-resident tree buffer (no host round trip)."""
@@ -301,17 +310,20 @@ class VerifyEngine:
         self.begin(cached, max_new, eos)
         self.prefill(list(prompt)[cached:])
         st = self.state()
+        out = self.tokens(st["step"])
         passes = 0
         while not st["done"]:
-            out = self.tokens(st["step"])
             tree = tree_fn(out) if tree_fn else root_tree()
             if fused:
-                st = self.step(tree).as_dict()  # tree in, pass, state out: one call
+                st = self.step(tree).as_dict()  # tree in, pass, state and tokens out: one call
+                out = out + self.last_tokens()
             else:
                 self.verify(tree)
                 self.commit()
                 st = self.state()
+                out = self.tokens(st["step"])
             passes += 1
             if st["err"]:
                 raise _lib.VpError(f"device error bits {st['err']}")
-        return {"tokens": self.tokens(st["step"]), "passes": passes, "state": st}
+        assert len(out) == st["step"], (len(out), st["step"])
+        return {"tokens": out, "passes": passes, "state": st}

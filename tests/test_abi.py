@@ -65,7 +65,7 @@ def test_step_and_sketch_argument_errors_without_device(lib):
     """vp_step and the sketch head reject bad arguments before any CUDA call."""
     st = _lib.VpState()
     tree = (ctypes.c_int32 * _lib.TREE_INTS)()
-    assert lib.vp_step(None, None, tree, ctypes.byref(st), None) == -1
+    assert lib.vp_step(None, None, tree, ctypes.byref(st), None, None) == -1
     assert b"null context" in lib.vp_last_error()
     assert lib.vp_sketch_bytes(100) == 0 and lib.vp_sketch_work_bytes(0) == 0
     assert lib.vp_sketch_bytes(151936) == 151936 // 16 * 14 * 256

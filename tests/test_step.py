@@ -1,10 +1,11 @@
-"""vp_step (one decode step from host memory: state and tree in, pass, state out) gives the same
-state and committed tokens as the separate calls it stands for: vp_write_state, vp_pass,
-vp_read_state."""
+"""vp_step (one decode step from host memory: state and tree in, pass, state and this pass's
+committed tokens out) gives the same state and committed tokens as the separate calls it stands
+for: vp_write_state, vp_pass, vp_read_state, vp_read_tokens."""
 import numpy as np
 import pytest
 
 from instantllm_b200 import synth
+from instantllm_b200._lib import STATE_FIELDS, VpState
 
 pytestmark = pytest.mark.gpu
 
@@ -31,8 +32,16 @@ def test_step_matches_separate_calls():
     got = []
     st = eng.step(trees[0], snap[0])  # from the snapshot, then continuing from the device state
     got.append((st.as_dict(), eng.tokens(st.step)))
+    returned = list(eng.tokens(1)) + eng.last_tokens()  # the prefill's token, then each pass's
     for t in trees[1:]:
         st = eng.step(t)
         got.append((st.as_dict(), eng.tokens(st.step)))
+        returned += eng.last_tokens()
     assert got == want
+    assert returned == want[-1][1]  # the tokens vp_step handed back are the committed stream
+
+    # a request that has stopped commits nothing: vp_step hands back no tokens
+    done = dict(want[-1][0], done=1)
+    st = eng.step(trees[0], VpState(*[done[n] for n in STATE_FIELDS]))
+    assert st.step == done["step"] and eng.last_tokens() == []
     eng.close()

@@ -2,7 +2,9 @@
 (their device memory belongs to a host pool or budget, or a cudaMalloc would stall a serving loop).
 Its scratch is a static device array in the library, so this checks, through the C ABI, that two
 calls in a row (the second one reusing the first one's scratch) give the same tokens as the
-context-based entry point, vp_debug_logits followed by argmax, on the same residual rows."""
+context-based entry point, vp_debug_logits followed by argmax, on the same residual rows. Both run
+the same GEMM arithmetic and break ties towards the lowest id, so the ids must be equal; the token
+slots past `rows` must stay untouched."""
 import ctypes
 
 import numpy as np
@@ -12,8 +14,6 @@ import torch
 from instantllm_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
-
-NEAR_TIE = 1e-4  # a different id is accepted only if its logit is this close to the reference's
 
 
 def _reference_ids(eng):
@@ -27,14 +27,13 @@ def _noalloc(lib, eng, x, rows):
     rc = lib.vp_head_argmax_noalloc(_lib.FMT[eng.fmt], eng.vocab, w.embed, w.final_norm, x.data_ptr(),
                                     rows, out.data_ptr(), eng.stream.cuda_stream)
     assert rc == 0, lib.vp_last_error()
-    return out[:rows].cpu().numpy()
+    o = out.cpu().numpy()
+    assert (o[rows:] == -7).all(), o  # slots past `rows` are not written
+    return o[:rows]
 
 
 def _check(lg, ref, got):
-    for r, (a, b) in enumerate(zip(ref, got)):
-        if a != b:
-            assert abs(float(lg[r, a]) - float(lg[r, b])) < NEAR_TIE, (r, a, b)
-    assert (ref == got).sum() >= len(ref) - 1
+    assert np.array_equal(ref, got), (ref, got)
 
 
 def test_noalloc_argmax_matches_context_entry_point():
