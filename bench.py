@@ -38,6 +38,7 @@ METRIC = "q4 16-row tree-verify pass µs & accepted tok/s; HBM GB/s vs B200 peak
 PREFIX = 256
 ROWS = 16
 L2_NOTE = "weights (278 MB/pass) exceed the 126 MB L2: no flush needed"
+WORKLOAD2 = "BASELINE config 2: q4 16-row tree verify + greedy commit, 256-token cached prefix, one request per GPU"
 
 
 def parse():
@@ -50,10 +51,15 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "config5", "sketch_head"], default="config2",
-                    help="config5: BASELINE config 5, independent requests sharded over the ranks; "
-                         "sketch_head: the optional two-stage lm_head against the full one (1 GPU)")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "sketch_head"],
+                    default="config2",
+                    help="config3 / config4: the q8 8-row chain and f16 16-row tree workloads (1 GPU, "
+                         "their own line); config5: BASELINE config 5, independent requests sharded "
+                         "over the ranks; sketch_head: the optional two-stage lm_head against the full "
+                         "one (1 GPU)")
     ap.add_argument("--requests", type=int, default=256, help="config5: number of requests")
+    ap.add_argument("--c5-requests", type=int, default=64,
+                    help="requests of the config-5 sub-object of the default line (0: skip it)")
     return ap.parse_args()
 
 
@@ -227,16 +233,18 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     clocks.start()
     s = eng.stream
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # an event between consecutive steps: per-step device times (p50 / p90) and their sum
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     clocks.mark_start()
-    e0.record(s)
-    for i in range(args.warmup, n_steps):
+    evs[0].record(s)
+    for k, i in enumerate(range(args.warmup, n_steps)):
         eng.restore(snap)  # 64-byte device-to-device state write: part of the step
         eng.pass_device(trees_dev[i])
-    e1.record(s)
+        evs[k + 1].record(s)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
+    ms = evs[0].elapsed_time(evs[-1])
+    step_ms = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
 
     # tree == sequential, every step: the committed tokens of each pass are the sequential run's
     ok = True
@@ -263,7 +271,7 @@ def run_ours(args, rank, world, local):
         e2e_ok = e2e_ok and got == y_full[1:1 + len(got)] and stt.step == 1 + len(got)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    return dict(ms=ms, tok=n_tok_timed, ok=ok and e2e_ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,
+    return dict(ms=ms, step_ms=step_ms, tok=n_tok_timed, ok=ok and e2e_ok, clocks=clk, e2e_s=e2e_s, e2e_tok=e2e_tok,
                 setup_s=time.time() - t_setup, eng=eng, w=w, prompt=prompt, y=y_full, trees=trees,
                 counts=counts)
 
@@ -271,7 +279,7 @@ def run_ours(args, rank, world, local):
 GEN = 64  # config 5: tokens generated per request
 
 
-def run_config5(args, rank, world, local):
+def run_config5(args, rank, world, local, w=None, n_requests=None):
     """BASELINE config 5 on this rank: its share of the requests (prefixes uniform in 128-2048,
     shard.assign), each prefilled, decoded sequentially with 1-row passes (untimed: the true
     continuation the seeded trees draft from), then decoded again with 16-row tree passes to 64
@@ -285,9 +293,10 @@ def run_config5(args, rank, world, local):
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    prefixes = shard.config5_requests(n=args.requests)
+    prefixes = shard.config5_requests(n=n_requests or args.requests)
     mine = shard.assign(prefixes, world)[rank]
-    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    if w is None:
+        w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
     eng = VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local)
     no_eos = (-1, -1)
     tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
@@ -328,21 +337,34 @@ def run_config5(args, rank, world, local):
     return dict(ms=dev_ms, tok=tokens, passes=passes, kv_slots=kv_slots, ok=ok, n=len(mine))
 
 
-def main_config5(args, rank, world):
+def config5_table(args, r, world):
+    """Per-rank config-5 figures gathered on every rank: [device ms, tokens, passes, ok, GB/s]."""
     import torch
 
     from instantllm_b200 import synth
 
-    r = run_config5(args, rank, world, int(os.environ.get("LOCAL_RANK", str(rank))))
     wbytes = synth.weight_bytes("q4", args.layers)
-    gbs = (r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24) / (r["ms"] * 1e-3) / 1e9
+    gbs = (r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24) / (max(r["ms"], 1e-9) * 1e-3) / 1e9
     vals = [r["ms"], float(r["tok"]), float(r["passes"]), 1.0 if r["ok"] else 0.0, gbs]
     if world > 1:
         rows = [torch.zeros(len(vals), dtype=torch.float64) for _ in range(world)]
         torch.distributed.all_gather(rows, torch.tensor(vals, dtype=torch.float64))
-        table = [x.tolist() for x in rows]
-    else:
-        table = [vals]
+        return [x.tolist() for x in rows]
+    return [vals]
+
+
+def config5_summary(table, n_requests) -> dict:
+    ms = max(t[0] for t in table)
+    tok = sum(t[1] for t in table)
+    return {"value": tok / (ms * 1e-3), "unit": "tok/s", "requests": n_requests, "tokens": int(tok),
+            "passes": int(sum(t[2] for t in table)), "ms_per_rank": [round(t[0], 3) for t in table],
+            "per_gpu_hbm_gbs": [round(t[4], 1) for t in table],
+            "tree_equals_sequential": all(t[3] > 0 for t in table)}
+
+
+def main_config5(args, rank, world):
+    r = run_config5(args, rank, world, int(os.environ.get("LOCAL_RANK", str(rank))))
+    table = config5_table(args, r, world)
     if rank == 0:
         ms = max(t[0] for t in table)
         tok = sum(t[1] for t in table)
@@ -369,6 +391,7 @@ def cpu_baseline(w, prompt, y_full, trees, seconds: float) -> dict:
     from oracle import accept as A
     from oracle import qwen_oracle as Q
 
+    threads = host_threads()
     m = Q.model_from_weights(w)
     cache = Q.KVCache(len(m.layers), 4096)
     logits = Q.forward_causal(m, cache, list(prompt), 0)
@@ -390,36 +413,59 @@ def cpu_baseline(w, prompt, y_full, trees, seconds: float) -> dict:
         tok += len(res["tokens"])
         passes += 1
     dt = time.perf_counter() - t0
-    threads = os.cpu_count()
     return {"value": tok / dt, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": f"{passes} q4 16-row tree passes (fp32 numpy, dequantised weights) after a "
                       f"{PREFIX}-token prefix, {dt:.1f} s", "pass_ms": 1000 * dt / max(passes, 1)}
 
 
+def host_threads() -> int:
+    """All host threads for numpy's BLAS, set explicitly: torchrun starts ranks with
+    OMP_NUM_THREADS=1, which would leave the reference arm single-threaded at N > 1."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(limits=n)
+        got = [d.get("num_threads") for d in threadpool_info() if d.get("user_api") == "blas"]
+        return int(got[0]) if got else n
+    except ImportError:
+        return n
+
+
 def run_reference(args):
-    """--impl reference: the reference's CPU path (numpy fp32 port) times the same workload."""
+    """--impl reference: the reference's CPU path (numpy fp32 port of tools/reference/qwen_ref.py;
+    the Swift/Metal engine cannot run here) on the workload of the GPU arm: the same N requests that
+    the N ranks serve (prompt seed 1000 + rank), each prefilled once, then one 16-row tree pass +
+    commit per step from the post-prefill state, steps taking the requests in turn. Value = committed
+    tokens / CPU time, so it does not depend on N."""
     from instantllm_b200 import synth
     from oracle import accept as A
     from oracle import qwen_oracle as Q
 
+    threads = host_threads()
+    world = max(1, args.gpus)
     w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
     m = Q.model_from_weights(w)
-    prompt = synth.make_prompt(PREFIX, seed=1000)
     n_steps = args.warmup + args.steps
-    cache = Q.KVCache(len(m.layers), 4096)
-    logits = Q.forward_causal(m, cache, list(prompt), 0)
-    # true continuation for the tree plans: the CPU model's own sequential greedy run
-    y, pos = [int(np.argmax(logits))], PREFIX
-    seq_cache = cache.copy()
-    while len(y) < 10:
-        lg = Q.forward_causal(m, seq_cache, [y[-1]], pos)
-        y.append(int(np.argmax(lg)))
-        pos += 1
+    reqs = []
+    for rk in range(world):
+        prompt = synth.make_prompt(PREFIX, seed=1000 + rk)
+        cache = Q.KVCache(len(m.layers), 4096)
+        logits = Q.forward_causal(m, cache, list(prompt), 0)
+        # true continuation for the tree plans: the CPU model's own sequential greedy run
+        y, pos = [int(np.argmax(logits))], PREFIX
+        seq_cache = cache.copy()
+        while len(y) < 10:
+            lg = Q.forward_causal(m, seq_cache, [y[-1]], pos)
+            y.append(int(np.argmax(lg)))
+            pos += 1
+        reqs.append((cache, y))
     times, toks = [], []
     for i in range(n_steps):
-        # every step from the same state (prefix cached, first token committed), trees seeded as
-        # in the GPU arm (rank 0)
-        rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([args.seed * 100003 + i, 4242])))
+        rk = i % world
+        cache, y = reqs[rk]
+        # trees seeded as in the GPU arm's rank rk
+        rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([(args.seed + rk) * 100003 + i, 4242])))
         tree = synth.seeded_tree(rng, y[1:10], n=ROWS)
         t0 = time.perf_counter()
         lg = Q.tree_pass(m, cache, PREFIX, y[0], tree)
@@ -434,19 +480,145 @@ def run_reference(args):
             toks.append(len(res["tokens"]))
     total = sum(times)
     v = sum(toks) / total
+    sample = (f"{len(times)} q4 16-row tree passes + commits over the {world} request(s) of the GPU arm, "
+              f"numpy fp32 port of tools/reference/qwen_ref.py with {threads} BLAS threads "
+              "(the Swift/Metal engine needs an Apple GPU)")
     line = {
         "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * total / len(times), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2: q4 16-row tree verify + commit, 256-token cached prefix",
-                   "rows": ROWS, "prefix": PREFIX, "layers": args.layers},
+        "config": {"workload": WORKLOAD2, "rows": ROWS, "prefix": PREFIX, "layers": args.layers,
+                   "requests": world},
         "impl": "reference",
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{len(times)} tree passes on the numpy fp32 port of "
-                                   "tools/reference/qwen_ref.py (the Swift/Metal engine needs an Apple GPU)"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_cfg34(args, which: str):
+    """BASELINE config 3 (q8 group-64 weights, 1024-token cached prefix, 8-row chain passes whose
+    draft i equals the true next token with p = 0.5, 64 tokens) or config 4 (f16 weights, a
+    512-token prompt prefilled in 16-row chunks, then 16-row seeded trees as in config 2 to 64
+    tokens). Truth = the same request decoded with 1-row passes through the same kernels; every
+    committed token is checked against it. Timed: the verify passes (device time), and for config 4
+    also the chunked prefill. One JSON line of its own, 1 GPU."""
+    import torch
+
+    from instantllm_b200 import synth
+    from instantllm_b200.engine import VerifyEngine
+    from oracle import accept as A
+    from oracle import qwen_oracle as Q
+
+    fmt, prefix, rows = ("q8", 1024, 8) if which == "config3" else ("f16", 512, 16)
+    gen = 64
+    w = synth.make_weights(fmt, n_layers=args.layers, seed=args.seed)
+    eng = VerifyEngine(w, max_ctx=prefix + gen + 3 * ROWS + 16, max_steps=gen + ROWS + 2, device=0)
+    dev, s = eng.device, eng.stream
+    prompt = synth.make_prompt(prefix, seed=3000 + (3 if which == "config3" else 4))
+    no_eos = (-1, -1)
+    eng.begin(0, gen + ROWS + 1, no_eos)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    eng.prefill(prompt)
+    e1.record(s)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    snap = eng.snapshot()
+    tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
+    for _ in range(gen + ROWS):
+        eng.pass_device(tree1)
+    y = eng.tokens(gen + ROWS + 1)
+    # pass plan from the truth: the device follows the planned acceptances
+    rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([args.seed, 34, prefix])))
+    bufs, counts, pos = [], [], 1
+    while pos < gen:
+        if which == "config3":
+            drafts = [y[pos + i] if rng.random() < 0.5 else int(rng.integers(0, synth.PROMPT_VOCAB))
+                      for i in range(rows - 1)]
+            tree = synth.chain_tree(drafts)
+        else:
+            tree = synth.seeded_tree(rng, y[pos:pos + 9], n=rows)
+        parents, tokens = A.to_python_numbering(tree)
+        a = A.accept_tree(parents, tokens, list(y), pos)
+        bufs.append(synth.tree_to_buffer(tree))
+        counts.append(a + 1)
+        pos += a + 1
+    tb = torch.tensor(np.stack(bufs), device=dev)
+    for _ in range(args.warmup):  # warm-up passes from the same state, then back to it
+        eng.restore(snap)
+        eng.pass_device(tb[0])
+    eng.restore(snap)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark_start()
+    e0.record(s)
+    for k in range(len(bufs)):
+        eng.pass_device(tb[k])
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    st = eng.state()
+    got = eng.tokens(st["step"])
+    ok = got == y[:st["step"]] and st["step"] == 1 + sum(counts)
+    n_pass = len(bufs)
+    pass_ms = ms / n_pass
+    hbm_peak, peak_kind = peaks()
+    wbytes = synth.weight_bytes(fmt, args.layers)
+    # KV bytes per pass: the unique slots read (cached context + the pass's rows) and the rows written
+    ctx = [prefix + 1 + sum(counts[:k]) for k in range(n_pass)]
+    kv = np.mean([12288 * (c + rows) + 12288 * rows for c in ctx]) * args.layers / 24
+    achieved = (wbytes + kv) / (pass_ms * 1e-3) / 1e9
+    line = {
+        "metric": f"{which}: {fmt} {rows}-row {'chain' if which == 'config3' else 'tree'} verify pass us "
+                  "& accepted tok/s; HBM GB/s vs B200 peak",
+        "value": (st["step"] - 1) / (ms * 1e-3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+        "passes": n_pass, "pass_us": 1000 * pass_ms, "tokens_per_pass": sum(counts) / n_pass,
+        "tree_equals_sequential": bool(ok), "dtype": f"{fmt} weights, fp16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights, uniform prompt ids)",
+        "config": {"workload": ("BASELINE config 3: q8 group-64, 1024-token cached prefix, 8-row chains, "
+                                "draft i = true token with p = 0.5, 64 tokens") if which == "config3" else
+                               ("BASELINE config 4: f16, 512-token prompt prefilled in 16-row chunks, "
+                                "16-row seeded trees to 64 tokens"),
+                   "layers": args.layers, "timed": "verify passes, device time"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "bytes_per_launch": wbytes + kv, "peak_kind": peak_kind},
+        "clocks": clk,
+    }
+    if which == "config4":
+        line["prefill_ms"] = prefill_ms
+        line["prefill_tok_s"] = prefix / (prefill_ms * 1e-3)
+    if not args.no_cpu_baseline:
+        # the oracle (numpy fp32 port of the reference CPU path) on a bounded sample: the prompt,
+        # then the same passes until cpu_seconds run out
+        threads = host_threads()
+        m = Q.model_from_weights(w)
+        cache = Q.KVCache(len(m.layers), prefix + gen + 3 * ROWS + 16)
+        t0 = time.perf_counter()
+        lg = Q.forward_causal(m, cache, list(prompt), 0)
+        t_pre = time.perf_counter() - t0
+        first, cpos, step, tok, n = int(np.argmax(lg)), prefix, 1, 0, 0
+        t1 = time.perf_counter()
+        while n < n_pass and time.perf_counter() - t1 < args.cpu_seconds:
+            b = bufs[n]
+            tr = {"n": int(b[0]), "depth": list(b[1:17]), "parent": list(b[17:33]), "tok": list(b[33:49])}
+            lg = Q.tree_pass(m, cache, cpos, first, tr)
+            res = A.commit(tr, lg.argmax(axis=1), cpos, step, 1 << 30, eos=())
+            for src, dst in res["moves"]:
+                for li in range(len(m.layers)):
+                    cache.k[li][:, dst] = cache.k[li][:, src]
+                    cache.v[li][:, dst] = cache.v[li][:, src]
+            tok += len(res["tokens"])
+            first, cpos, step, n = res["tokens"][-1], res["pos"], step + len(res["tokens"]), n + 1
+        dt = time.perf_counter() - t1
+        line["cpu_baseline"] = {"value": tok / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"the {prefix}-token prompt ({t_pre:.1f} s) then {n} of the same "
+                                          f"passes ({dt:.1f} s), numpy fp32 with dequantised weights",
+                                "pass_ms": 1000 * dt / max(n, 1)}
+    print(json.dumps(line), flush=True)
+    eng.close()
 
 
 def main_sketch(args):
@@ -538,6 +710,9 @@ def main():
     if args.workload == "sketch_head":
         main_sketch(args)
         return
+    if args.workload in ("config3", "config4"):
+        run_cfg34(args, args.workload)
+        return
     if args.workload == "config5":
         main_config5(args, rank, world)
         if world > 1:
@@ -548,8 +723,9 @@ def main():
     ms, tok = r["ms"], r["tok"]
     e2e_s, e2e_tok = r["e2e_s"], r["e2e_tok"]
     ok = 1.0 if r["ok"] else 0.0
+    p50, p90 = (float(np.percentile(r["step_ms"], q)) for q in (50, 90))
     if world > 1:
-        t = torch.tensor([ms, float(tok), e2e_s, float(e2e_tok), ok], dtype=torch.float64)
+        t = torch.tensor([ms, float(tok), e2e_s, float(e2e_tok), ok, p50, p90], dtype=torch.float64)
         mx = t.clone()
         torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
         sm = t.clone()
@@ -558,6 +734,8 @@ def main():
         torch.distributed.all_reduce(mn, op=torch.distributed.ReduceOp.MIN)
         ms, tok, e2e_s, e2e_tok = mx[0].item(), sm[1].item(), mx[2].item(), sm[3].item()
         ok = mn[4].item()
+        p50, p90 = mx[5].item(), mx[6].item()
+    line = None
     if rank == 0:
         hbm_peak, peak_kind = peaks()
         wbytes = synth.weight_bytes("q4", args.layers)
@@ -575,6 +753,8 @@ def main():
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": ms / args.steps,
+            "step_us_p50": 1000 * p50,  # per-step device time (CUDA events between steps), max over ranks
+            "step_us_p90": 1000 * p90,
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,  # BASELINE.md publishes a pass time (3.8 ms, Apple M5), not tok/s
@@ -582,10 +762,8 @@ def main():
                                     "pass_time_ratio": 3800.0 / (1000 * pass_ms)},
             "dtype": "q4 weights, fp16 activations, fp32 accumulate",
             "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
-            "config": {"workload": "BASELINE config 2: q4 16-row tree verify + greedy commit, "
-                                   "256-token cached prefix, one request per GPU",
-                       "rows": ROWS, "prefix": PREFIX, "layers": args.layers, "l2": L2_NOTE,
-                       "parallelism": f"request sharding x{world}"},
+            "config": {"workload": WORKLOAD2, "rows": ROWS, "prefix": PREFIX, "layers": args.layers,
+                       "l2": L2_NOTE, "parallelism": f"request sharding x{world}"},
             "pass_us": 1000 * pass_ms,
             "tokens_per_pass": tok / max(1, args.steps * world),
             "hbm_gbs": achieved,
@@ -605,8 +783,19 @@ def main():
             line["cpu_baseline"] = cpu_baseline(r["w"], r["prompt"], r["y"], r["trees"], args.cpu_seconds)
         else:
             line["cpu_baseline"] = None
-        print(json.dumps(line), flush=True)
     r["eng"].close()
+    if args.c5_requests > 0:
+        # BASELINE config 5 on the same ranks (strong scaling: a fixed set of requests split over
+        # the ranks, longest-processing-time first, no collective on the data path)
+        r5 = run_config5(args, rank, world, local, w=r["w"], n_requests=args.c5_requests)
+        table = config5_table(args, r5, world)
+        if rank == 0:
+            line["config5"] = dict(config5_summary(table, args.c5_requests), scaling="strong",
+                                   workload="BASELINE config 5: prefixes uniform in [128, 2048], 64 tokens "
+                                            "each, seeded 16-row trees; device time of the tree passes, "
+                                            "max over ranks")
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -124,6 +124,37 @@ __device__ __forceinline__ void load_a_frags(const uint8_t* tile, int lane, int 
   }
 }
 
+// A fragments of all four k-steps of a tile in one go: the lane's codes are loaded with 128-bit
+// shared-memory reads (q4: one, q8: two, f16: four), conflict-free across the warp.
+template <int FMT>
+__device__ __forceinline__ void load_a_frags_all(const uint8_t* tile, int lane, uint32_t (&a)[4][4]) {
+  if constexpr (FMT == VP_FMT_Q4) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + lane * 16);
+    q4_frags(v.x, a[0]);
+    q4_frags(v.y, a[1]);
+    q4_frags(v.z, a[2]);
+    q4_frags(v.w, a[3]);
+  } else if constexpr (fmt_is_q8(FMT)) {
+    const uint4 v0 = *reinterpret_cast<const uint4*>(tile + lane * 32);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(tile + lane * 32 + 16);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t u0 = w[2 * j] ^ 0x80808080u, u1 = w[2 * j + 1] ^ 0x80808080u;  // q + 128 in 1..255
+      a[j][0] = __byte_perm(u0, 0u, 0x5150);
+      a[j][1] = __byte_perm(u0, 0u, 0x5352);
+      a[j][2] = __byte_perm(u1, 0u, 0x5150);
+      a[j][3] = __byte_perm(u1, 0u, 0x5352);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = reinterpret_cast<const uint4*>(tile + lane * 64)[j];
+      a[j][0] = v.x; a[j][1] = v.y; a[j][2] = v.z; a[j][3] = v.w;
+    }
+  }
+}
+
 // Per-row (gid, gid+8) and per-half constants of a q8g32 tile (one scale per 32 columns):
 // y += sf[h] * acc[h] + sb[h] * X[h] for the halves h = 0 (columns 0..31) and 1 (32..63).
 __device__ __forceinline__ void load_fold_halves(const uint8_t* tile, int gid, float (&sf)[2][2], float (&sb)[2][2]) {

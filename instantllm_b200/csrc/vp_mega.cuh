@@ -269,14 +269,15 @@ __device__ __forceinline__ void mk_tiles_bf(const uint8_t* const (&tile)[NT], in
   const int gid = lane >> 2, tid4 = lane & 3;
   if constexpr (FMT == VP_FMT_F16) {
 #pragma unroll
-    for (int u = 0; u < NT; ++u)
+    for (int u = 0; u < NT; ++u) {
+      uint32_t w[4][4];
+      load_a_frags_all<FMT>(tile[u], lane, w);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint32_t w[4];
-        load_a_frags<FMT>(tile[u], lane, j, w);
-        mma16816(acc[0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
-        mma16816(acc[1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
+        mma16816(acc[0], w[j][0], w[j][1], w[j][2], w[j][3], bf[u][j].x, bf[u][j].y);
+        mma16816(acc[1], w[j][0], w[j][1], w[j][2], w[j][3], bf[u][j].z, bf[u][j].w);
       }
+    }
   } else {
     // NH = 2 for q8g32: the two 32-column halves of a tile accumulate, sum and fold separately
     constexpr int NH = fmt_halves(FMT) ? 2 : 1;
@@ -315,15 +316,16 @@ __device__ __forceinline__ void mk_tiles_bf(const uint8_t* const (&tile)[NT], in
         }
       }
     }
+    uint32_t w[NT][4][4];
+#pragma unroll
+    for (int u = 0; u < NT; ++u) load_a_frags_all<FMT>(tile[u], lane, w[u]);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int u = 0; u < NT; ++u) {
-        uint32_t w[4];
-        load_a_frags<FMT>(tile[u], lane, j, w);
         const int h = NH == 2 ? (j >> 1) : 0;
-        mma16816(ag[u][h][0], w[0], w[1], w[2], w[3], bf[u][j].x, bf[u][j].y);
-        mma16816(ag[u][h][1], w[0], w[1], w[2], w[3], bf[u][j].z, bf[u][j].w);
+        mma16816(ag[u][h][0], w[u][j][0], w[u][j][1], w[u][j][2], w[u][j][3], bf[u][j].x, bf[u][j].y);
+        mma16816(ag[u][h][1], w[u][j][0], w[u][j][1], w[u][j][2], w[u][j][3], bf[u][j].z, bf[u][j].w);
       }
 #pragma unroll
     for (int u = 0; u < NT; ++u) {
