@@ -51,9 +51,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "sketch_head"],
+    ap.add_argument("--workload", choices=["config2", "batch2", "config3", "config4", "config5", "sketch_head"],
                     default="config2",
-                    help="config3 / config4: the q8 8-row chain and f16 16-row tree workloads (1 GPU, "
+                    help="batch2: two config-2 requests per launch (vp_pass_multi), aggregate tok/s (1 GPU); "
+                         "config3 / config4: the q8 8-row chain and f16 16-row tree workloads (1 GPU, "
                          "their own line); config5: BASELINE config 5, independent requests sharded "
                          "over the ranks; sketch_head: the optional two-stage lm_head against the full "
                          "one (1 GPU)")
@@ -496,6 +497,103 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_batch2(args):
+    """Two config-2 requests per launch (vp_pass_multi, each on half of the SMs): each request
+    prefilled with its own 256-token prompt, decoded with 1-row passes two per launch (the truth),
+    then every step = both requests' seeded 16-row tree passes + commits from their post-prefill
+    states in one launch. Also times one request alone on its half (n = 1) and the plain
+    whole-GPU pass. One JSON line of its own, 1 GPU."""
+    import torch
+
+    from instantllm_b200 import synth
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    engs, snaps, ys = [], [], []
+    for r in range(2):
+        eng = VerifyEngine(w, max_ctx=4096, max_steps=4096, device=0)
+        eng.begin(0, 24, (-1, -1))
+        eng.prefill(synth.make_prompt(PREFIX, seed=1000 + r))
+        engs.append(eng)
+        snaps.append(eng.snapshot())
+    dev, s = engs[0].device, engs[0].stream
+    root = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
+    for _ in range(23):
+        VerifyEngine.pass_multi(engs, [root, root])
+    ys = [e.tokens(24) for e in engs]
+    n_steps = args.warmup + args.steps
+    plans = [[plan_trees(ys[r], 1, 1, (args.seed + r) * 100003 + i) for i in range(n_steps)] for r in range(2)]
+    trees = [torch.tensor(np.stack([p[0][0] for p in plans[r]]), device=dev) for r in range(2)]
+    counts = [[p[1][0] for p in plans[r]] for r in range(2)]
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(args.warmup, n_steps):
+            fn(i)
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    def both(i):
+        for e, sn in zip(engs, snaps):
+            e.restore(sn)
+        VerifyEngine.pass_multi(engs, [trees[0][i], trees[1][i]])
+
+    def one(i):
+        engs[0].restore(snaps[0])
+        VerifyEngine.pass_multi(engs[:1], [trees[0][i]])
+
+    def whole(i):
+        engs[0].restore(snaps[0])
+        engs[0].pass_device(trees[0][i])
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark_start()
+    ms2 = timed(both)
+    clk = clocks.stop()
+    ms1 = timed(one)
+    msw = timed(whole)
+    ok = True
+    for i in range(n_steps):  # every step's committed tokens against the truth, both requests
+        both(i)
+        for r in range(2):
+            st = engs[r].state()
+            ok = ok and st["step"] == 1 + counts[r][i] and engs[r].tokens(st["step"]) == ys[r][:st["step"]]
+    tok2 = sum(counts[0][args.warmup:]) + sum(counts[1][args.warmup:])
+    hbm_peak, peak_kind = peaks()
+    wbytes = synth.weight_bytes("q4", args.layers)
+    kv = 12288 * (PREFIX + ROWS) * args.layers / 24 + 12288 * ROWS * args.layers / 24
+    launch_ms = ms2 / args.steps
+    achieved = 2 * (wbytes + kv) / (launch_ms * 1e-3) / 1e9
+    line = {
+        "metric": "batched verify: two requests per launch, aggregate accepted tok/s (q4 16-row trees)",
+        "value": tok2 / (ms2 * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "requests_per_launch": 2,
+        "launch_us": 1000 * launch_ms, "one_request_half_us": 1000 * ms1 / args.steps,
+        "one_request_whole_us": 1000 * msw / args.steps,
+        "single_request_tok_s": sum(counts[0][args.warmup:]) / (msw * 1e-3),
+        "tree_equals_sequential": bool(ok),
+        "hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "bytes_per_launch": 2 * (wbytes + kv), "peak_kind": peak_kind,
+                     "note": "each request streams its own copy of the weights (no shared weight stream)"},
+        "dtype": "q4 weights, fp16 activations, fp32 accumulate",
+        "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
+        "config": {"workload": "two BASELINE config 2 requests (256-token cached prefixes, seeded 16-row "
+                               "trees) per launch, each on half of the SMs", "layers": args.layers},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    for e in engs:
+        e.close()
+
+
 def run_cfg34(args, which: str):
     """BASELINE config 3 (q8 group-64 weights, 1024-token cached prefix, 8-row chain passes whose
     draft i equals the true next token with p = 0.5, 64 tokens) or config 4 (f16 weights, a
@@ -712,6 +810,9 @@ def main():
         return
     if args.workload in ("config3", "config4"):
         run_cfg34(args, args.workload)
+        return
+    if args.workload == "batch2":
+        run_batch2(args)
         return
     if args.workload == "config5":
         main_config5(args, rank, world)

@@ -174,6 +174,17 @@ int vp_commit(vp_ctx* ctx, void* stream);
 
 /* ---- whole pass: verify + commit as one persistent-kernel launch (the pass encoder) ---- */
 int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
+/* Passes of several requests in one launch (no counterpart in the reference, which serves one
+ * request at a time, Engine.swift:567-579): up to 2 contexts (distinct, same device and format),
+ * each with its tree (host or device pointer), run one verify pass + commit each, every request on
+ * its own half of the SMs (its own barriers, state and scratch). A single pass is bound by the
+ * latency of its dependent stages rather than by SMs or HBM, so two requests per launch nearly
+ * double the committed tokens per second. Every request gets half the SMs also when n = 1: the
+ * stage splits follow the CTA count, so a request stays bit-identical across its passes (tree ==
+ * sequential) only if all of them run with the same share. Stream-ordered; contexts not used by
+ * this call are untouched. */
+int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, void* stream);
+
 /* One step of the host's decode loop (the body of Engine.generate's loop, Engine.swift:937-1015:
  * fill State, encode the pass, wait, read State and the committed tokens) in one call from host
  * memory: optionally the 64-byte state (state_in, NULL to continue from the device state), the

@@ -205,11 +205,10 @@ struct MkRing {
 // producer warp: issues every piece of the pass in order (lane 0)
 
 template <int FMT>
-__device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sStop) {
+__device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sStop, int cta, int G) {
   if ((threadIdx.x & 31) != 0) return;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + MK_OFF_BAR);
   uint64_t* empty = full + MK_NSLOT;
-  const int G = gridDim.x, cta = blockIdx.x;
   constexpr int TB = tile_bytes(FMT);
   const int tp = mk_tiles_per_slot(FMT);
   const uint64_t pol = policy_evict_first();
@@ -692,14 +691,13 @@ __device__ __noinline__ void mk_poll_flagged(const uint64_t* act_ll, const uint6
 // Returns false if a wait timed out.
 template <int FMT, int MODE, bool DOWN = false>
 __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
-                        uint8_t* smem, volatile int* sAbort) {
+                        uint8_t* smem, volatile int* sAbort, int cta, int G) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tid4 = lane & 3;
   uint8_t* sAct = smem + MK_OFF_ACT;
   float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
   float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
   float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
-  const int G = gridDim.x, cta = blockIdx.x;
   int rb0, nrb;
   mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
   if (nrb == 0) return true;
@@ -796,12 +794,12 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   return true;
 }
 
+// One pass of one request on the G CTAs of its group; this CTA is number cta of them.
 template <int FMT>
-__global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
+__device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int sAbort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = gridDim.x, cta = blockIdx.x;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + MK_OFF_BAR);
   uint64_t* empty = full + MK_NSLOT;
   RowInfo* sRi = reinterpret_cast<RowInfo*>(smem + MK_OFF_RI);
@@ -818,7 +816,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
   cta_sync();
 
   if (warp == MK_WARPS) {
-    mk_producer<FMT>(p, smem, &sAbort);
+    mk_producer<FMT>(p, smem, &sAbort, cta, G);
     __syncwarp();
   } else {
     unsigned long long target = 0;
@@ -896,7 +894,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         // no grid barrier: the attention units poll the flagged q and K / V rows they need (every
         // CTA passed the barrier after the previous down projection, so the previous layer's
         // words have no reader left)
-        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort);
+        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_QKV);
         if (!ok) break;
         s.flag_q = flag0 + l;
@@ -926,7 +924,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.xs = own_x ? sXrb : nullptr;
         // no grid barrier: gate/up polls the flagged words it needs (every CTA passed the
         // attention barrier, so no reader of the previous layer's words is left)
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort);
+        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_O);
         if (!ok) break;
         // gate/up + SiLU
@@ -934,7 +932,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.s = s; gp.layer = l;
         gp.w = p.wgu[l]; gp.act = s.act_h; gp.nrb = 2 * F / 16; gp.ng = H / GS;
         gp.act_ll_in = s.act_ll; gp.ss_ll_in = s.ss_ll; gp.flag = flag0 + l; gp.act_out = s.act_f;
-        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort) && barrier();
+        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort, cta, G) && barrier();
         piece0 += pieces(MK_GU);
         if (!ok) break;
         // down + residual
@@ -944,7 +942,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
         gp.wnext = l + 1 < p.n_layers ? p.ln1[l + 1] : p.final_norm;
         gp.ss_out = s.ss; gp.act_out = s.act_h;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort) && barrier();
+        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G) && barrier();
         piece0 += pieces(MK_DOWN);
       }
       if (ok && p.do_lm) {
@@ -955,7 +953,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
           reinterpret_cast<float*>(smem + MK_OFF_LMV)[warp * 16 + lane] = -INFINITY;
           reinterpret_cast<int*>(smem + MK_OFF_LMI)[warp * 16 + lane] = 0x7fffffff;
         }
-        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort);
+        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort, cta, G);
         // per-CTA best per token from the warps' running bests
         float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
         int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
@@ -989,6 +987,27 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(MegaParams p) {
       __threadfence();
     }
   }
+}
+
+// One verify pass (or prefill chunk) of one request on every CTA of the launch.
+template <int FMT>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_pass(const __grid_constant__ MegaParams p) {
+  pass_body<FMT>(p, blockIdx.x, gridDim.x);
+}
+
+// Passes of MK_MAX_GROUPS requests in one launch, each on its own contiguous group of
+// gridDim.x / groups CTAs with its own context (barrier counters, state, scratch, KV cache): a
+// single pass is bound by the latency of its dependent stages, not by the SMs or HBM, so a second
+// request on the other half of the SMs costs little time.
+constexpr int MK_MAX_GROUPS = 2;
+struct BatchParams {
+  MegaParams p[MK_MAX_GROUPS];
+  int groups;
+};
+template <int FMT>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_pass_groups(const __grid_constant__ BatchParams bp) {
+  const int per = gridDim.x / bp.groups, g = blockIdx.x / per;
+  pass_body<FMT>(bp.p[g], blockIdx.x - g * per, per);
 }
 
 }  // namespace vp

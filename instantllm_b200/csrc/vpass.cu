@@ -126,6 +126,7 @@ int set_attrs(vp_ctx* c) {
   VP_CUDA(cudaFuncSetAttribute(k_gemm<FMT, MODE_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)c->lm.smem));
   VP_CUDA(cudaFuncSetAttribute(k_pass<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+  VP_CUDA(cudaFuncSetAttribute(k_pass_groups<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
   int per_sm = 0;
   VP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass<FMT>, MK_THREADS, MK_SMEM));
   if (per_sm < 1) return fail(VP_ERR_CUDA, "pass kernel does not fit on an SM");
@@ -176,6 +177,19 @@ int launch_commit(vp_ctx* c, cudaStream_t st) {
   cp.s = c->s;
   VP_CUDA(launch(k_commit, 1, COMMIT_THREADS, 0, st, false, cp));
   return VP_OK;
+}
+
+// Whether a pass fits G CTAs: QKV / O / down take one CTA per row-block (72 / 56 / 56), and every
+// CTA keeps its row-blocks' partial tiles of a stage in MK_PART_SLOTS shared-memory slots.
+bool split_fits(int G, int vocab) {
+  if (G < QKV / 16) return false;
+  for (int st = MK_QKV; st <= MK_DOWN; ++st)
+    for (int cta = 0; cta < G; ++cta) {
+      int rb0, n;
+      mk_range(st, cta, G, vocab / 16, rb0, n);
+      if (n * mk_parts(st, n) > MK_PART_SLOTS) return false;
+    }
+  return true;
 }
 
 int check_ctx(vp_ctx* c) {
@@ -232,16 +246,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   VP_CUDA(cudaSetDevice(cfg->device));
   int sms = 0;
   VP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device));
-  // every CTA keeps its row-blocks' partial tiles of a stage in MK_PART_SLOTS shared-memory slots,
-  // and QKV / O / down need one CTA per row-block
-  if (sms < QKV / 16) return fail(VP_ERR_DEVICE, "the pass kernel needs at least 72 SMs");
-  for (int st = MK_QKV; st <= MK_DOWN; ++st)
-    for (int cta = 0; cta < sms; ++cta) {
-      int rb0, n;
-      mk_range(st, cta, sms, cfg->vocab / 16, rb0, n);
-      if (n * mk_parts(st, n) > MK_PART_SLOTS)
-        return fail(VP_ERR_DEVICE, "too few SMs for the pass kernel's work split");
-    }
+  if (!split_fits(sms, cfg->vocab)) return fail(VP_ERR_DEVICE, "the pass kernel needs at least 72 SMs");
   vp_ctx* c = new vp_ctx();
   c->cfg = *cfg;
   const int fmt = cfg->format;
@@ -445,6 +450,40 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
   p.do_lm = 1;
   p.do_commit = 1;
   return launch_pass(c, p, st);
+}
+
+int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, void* stream) {
+  if (!ctxs || !trees || n < 1 || n > MK_MAX_GROUPS) return fail(VP_ERR_ARG, "n must be 1 or 2");
+  int r = VP_OK;
+  for (int i = 0; i < n; ++i) {
+    if ((r = check_ctx(ctxs[i]))) return r;
+    if (!trees[i]) return fail(VP_ERR_ARG, "null tree");
+    for (int j = 0; j < i; ++j)
+      if (ctxs[j] == ctxs[i]) return fail(VP_ERR_ARG, "the same context twice");
+    if (ctxs[i]->cfg.device != ctxs[0]->cfg.device || ctxs[i]->cfg.format != ctxs[0]->cfg.format)
+      return fail(VP_ERR_ARG, "contexts on different devices or formats");
+  }
+  vp_ctx* c0 = ctxs[0];
+  const int per = c0->grid / MK_MAX_GROUPS;  // every request gets the same share, whatever n is
+  for (int i = 0; i < n; ++i)
+    if (!split_fits(per, ctxs[i]->cfg.vocab)) return fail(VP_ERR_DEVICE, "too few SMs for two pass groups");
+  VP_CUDA(cudaSetDevice(c0->cfg.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  BatchParams bp = {};
+  bp.groups = n;
+  for (int i = 0; i < n; ++i) {
+    VP_CUDA(cudaMemcpyAsync(ctxs[i]->s.tree, trees[i], VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
+    bp.p[i] = mega_params(ctxs[i]);
+    bp.p[i].do_lm = 1;
+    bp.p[i].do_commit = 1;
+  }
+  switch (c0->cfg.format) {
+    case VP_FMT_Q4: VP_CUDA(launch(k_pass_groups<VP_FMT_Q4>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
+    case VP_FMT_Q8: VP_CUDA(launch(k_pass_groups<VP_FMT_Q8>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
+    case VP_FMT_Q8G32: VP_CUDA(launch(k_pass_groups<VP_FMT_Q8G32>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
+    default: VP_CUDA(launch(k_pass_groups<VP_FMT_F16>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
+  }
+  return VP_OK;
 }
 
 int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* state_out,

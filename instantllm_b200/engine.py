@@ -187,6 +187,18 @@ class VerifyEngine:
         """Graph pass with a device-resident tree buffer (no host round trip)."""
         check(self.lib.vp_pass(self.ctx, tree_dev.data_ptr(), self._s), "vp_pass")
 
+    @staticmethod
+    def pass_multi(engines, trees_dev) -> None:
+        """One verify pass + commit of each engine's request in one launch (vp_pass_multi), each
+        request on half of the SMs; trees_dev: one device int32[65] tree buffer per engine."""
+        if not engines or len(engines) != len(trees_dev):
+            raise ValueError("one tree per engine")
+        n = len(engines)
+        ctxs = (ctypes.c_void_p * n)(*[e.ctx.value for e in engines])
+        trees = (ctypes.c_void_p * n)(*[t.data_ptr() for t in trees_dev])
+        e0 = engines[0]
+        check(e0.lib.vp_pass_multi(ctxs, trees, n, e0._s), "vp_pass_multi")
+
     # ---- results ----
     def state(self) -> dict:
         st = VpState()

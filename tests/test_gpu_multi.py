@@ -1,0 +1,91 @@
+"""vp_pass_multi: two requests' verify passes in one launch, each on half of the SMs.
+
+Every request gets the same share of the SMs whatever the number of requests in the launch, so a
+request decoded with 16-row trees through vp_pass_multi commits exactly the tokens that 1-row passes
+through vp_pass_multi commit (tree == sequential), whether its partner request runs beside it or
+not; its logits match the fp32 oracle."""
+import numpy as np
+import pytest
+import torch
+
+from instantllm_b200 import synth
+from oracle import accept as A
+from oracle import qwen_oracle as Q
+
+pytestmark = pytest.mark.gpu
+
+V = 4096
+
+
+def _engine(w, seed):
+    from instantllm_b200.engine import VerifyEngine
+
+    eng = VerifyEngine(w, max_ctx=512, max_steps=96)
+    prompt = (synth.make_prompt(30 + seed, seed=seed) % V).tolist()
+    eng.begin(0, 64, (-1, -1))
+    eng.prefill(prompt)
+    return eng, prompt, eng.snapshot()
+
+
+def _root(eng):
+    return torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=eng.device)
+
+
+def test_two_requests_per_launch_tree_equals_sequential():
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=2, vocab=V, seed=61)
+    (ea, pa, sa), (eb, pb, sb) = _engine(w, 1), _engine(w, 2)
+    root = _root(ea)
+    # sequential truth of both requests, two per launch
+    for _ in range(24):
+        VerifyEngine.pass_multi([ea, eb], [root, root])
+    ya, yb = ea.tokens(25), eb.tokens(25)
+    assert ea.state()["err"] == 0 and eb.state()["err"] == 0
+    # request a alone through the same entry point: the same tokens (its half of the SMs only)
+    ea.restore(sa)
+    for _ in range(24):
+        VerifyEngine.pass_multi([ea], [root])
+    assert ea.tokens(25) == ya
+    # 16-row trees from the truth, both requests per launch, every committed token checked
+    rng = np.random.default_rng(61)
+    ea.restore(sa)
+    eb.restore(sb)
+    for _ in range(5):
+        sta, stb = ea.state(), eb.state()
+        ta = synth.seeded_tree(rng, ya[sta["step"]:sta["step"] + 9], n=16, vocab=V)
+        tb = synth.seeded_tree(rng, yb[stb["step"]:stb["step"] + 9], n=16, vocab=V)
+        VerifyEngine.pass_multi([ea, eb], [torch.tensor(synth.tree_to_buffer(t), device=ea.device)
+                                           for t in (ta, tb)])
+        for eng, y, st0, tree in ((ea, ya, sta, ta), (eb, yb, stb, tb)):
+            st = eng.state()
+            parents, tokens = A.to_python_numbering(tree)
+            acc = A.accept_tree(parents, tokens, y, st0["step"])
+            assert st["step"] == st0["step"] + acc + 1
+            assert eng.tokens(st["step"]) == y[:st["step"]]
+    # logits of b's last pass against the fp32 oracle over the same committed context
+    m = Q.model_from_weights(w)
+    cache = Q.KVCache(2, 512)
+    Q.forward_causal(m, cache, pb + yb[:stb["step"] - 1], 0)
+    ref = Q.tree_pass(m, cache, len(pb) + stb["step"] - 1, yb[stb["step"] - 1], tb)
+    got = eb.logits().cpu().numpy()[:16]
+    assert float(np.abs(got - ref).max()) < 0.05
+    ea.close()
+    eb.close()
+
+
+def test_pass_multi_rejects_bad_arguments():
+    import ctypes
+
+    from instantllm_b200 import _lib
+
+    lib = _lib.load()
+    w = synth.make_weights("q4", n_layers=1, vocab=V, seed=62)
+    eng, _, _ = _engine(w, 3)
+    tree = _root(eng)
+    one = (ctypes.c_void_p * 2)(eng.ctx.value, eng.ctx.value)
+    trees = (ctypes.c_void_p * 2)(tree.data_ptr(), tree.data_ptr())
+    assert lib.vp_pass_multi(one, trees, 2, None) == -1  # the same context twice
+    assert lib.vp_pass_multi(one, trees, 3, None) == -1
+    assert lib.vp_pass_multi(one, trees, 0, None) == -1
+    eng.close()
