@@ -271,6 +271,51 @@ int vp_head_argmax_sketch(int32_t vocab, const void* d_embed, const void* d_sket
                           void* d_work, size_t work_bytes, int32_t* d_tokens, int32_t* d_ncand,
                           void* stream);
 
+/* ---- the learned drafter on the device (k_ildraft, Shaders.swift:428-872; specification
+ * tools/draft/ildraft.py:441-747; table loading ILDraft.swift:39-60) ----
+ * vp_drafter_create parses an ILDRAFT1 table (the bytes of the file, host memory) and copies the
+ * parts the drafter reads per step to `device`. vp_drafter_begin takes the request context the host
+ * builds at request start (Drafter.begin, ildraft.py:452-516; ILDraft.swift:138): prompt ids, the
+ * sorted distinct prompt ids (copy candidates), the nearest training documents (score, sequence =
+ * the 5-token assistant tail + the document's output, and the sorted keys of the sequence's n-grams
+ * of 1..MAXM tokens with the index after each one's first occurrence that has a next token), and
+ * the association map (token -> max loglift, count; sorted by token) with the association
+ * candidates. vp_draft runs one step on `stream`: from the request's output tokens (d_out_tokens:
+ * d_state->step of them when d_state is given, which also makes a finished request (done) produce a
+ * 1-row tree; else n_out) it grows the best-first tree of at most B (<= 15) drafts with `branch`
+ * (<= 8) children per expansion and writes it to d_tree (VP_TREE_INTS int32, the verify pass's tree
+ * buffer: row 0 the last output token). Passing a context's vp_device_tokens / vp_device_state and
+ * then d_tree to vp_pass keeps the decode loop on the device. The optional debug block receives the
+ * nodes (parents: -1 = root, -2 = unused; tokens), each expansion's top 8 (tokens -1 past the end,
+ * probabilities float64) and a status (bit 0: more than 1024 candidates in a context, the rest
+ * dropped). Errors: VP_ERR_ARG (bad table or sizes), VP_ERR_STATE (no request), VP_ERR_CUDA. */
+#define VP_DRAFT_MAX_PROMPT 8192
+typedef struct vp_drafter vp_drafter;
+typedef struct {
+  int32_t n_prompt; const int32_t* prompt;
+  int32_t n_copy; const int32_t* copy;
+  int32_t n_nb; const double* nb_score;
+  const int32_t* nb_seq_off;   /* [n_nb + 1] */
+  const int32_t* nb_seq;
+  const int32_t* nb_key_off;   /* [n_nb + 1] */
+  const uint64_t* nb_keys;     /* FNV-1a 64 of (order byte, tokens as u32 LE), ascending per document */
+  const int32_t* nb_pos;
+  int32_t n_as; const int32_t* as_tok; const double* as_max; const int32_t* as_cnt;
+  int32_t n_as_cand; const int32_t* as_cand;
+} vp_draft_request;
+typedef struct {
+  int32_t* parents;     /* device int32[15] */
+  int32_t* tokens;      /* device int32[15] */
+  int32_t* exp_tokens;  /* device int32[16][8] */
+  double* exp_probs;    /* device double[16][8] */
+  int32_t* status;      /* device int32[1] */
+} vp_draft_debug;
+int vp_drafter_create(const void* table, size_t bytes, int32_t device, vp_drafter** out);
+void vp_drafter_destroy(vp_drafter* d);
+int vp_drafter_begin(vp_drafter* d, const vp_draft_request* req);
+int vp_draft(vp_drafter* d, const int32_t* d_out_tokens, const vp_state* d_state, int32_t n_out, int32_t B,
+             int32_t branch, int32_t* d_tree, const vp_draft_debug* dbg, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

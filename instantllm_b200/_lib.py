@@ -22,7 +22,7 @@ EXPORTS = (
     "vp_read_tokens", "vp_device_tokens", "vp_device_state",
     "vp_debug_logits", "vp_buffer", "vp_head_argmax_noalloc",
     "vp_sketch_bytes", "vp_pack_sketch", "vp_sketch_work_bytes", "vp_sketch_bounds_offset",
-    "vp_head_argmax_sketch",
+    "vp_head_argmax_sketch", "vp_drafter_create", "vp_drafter_destroy", "vp_drafter_begin", "vp_draft",
 )
 
 
@@ -99,6 +99,10 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_sketch_work_bytes": (sz, [i32]),
         "vp_sketch_bounds_offset": (sz, []),
         "vp_head_argmax_sketch": (ctypes.c_int, [i32, vp, vp, vp, vp, i32, ctypes.c_float, vp, sz, vp, vp, vp]),
+        "vp_drafter_create": (ctypes.c_int, [vp, sz, i32, ctypes.POINTER(vp)]),
+        "vp_drafter_destroy": (None, [vp]),
+        "vp_drafter_begin": (ctypes.c_int, [vp, vp]),
+        "vp_draft": (ctypes.c_int, [vp, vp, vp, i32, i32, i32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

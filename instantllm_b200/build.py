@@ -7,7 +7,7 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
-SOURCES = [PKG / "csrc" / "vpass.cu"]
+SOURCES = [PKG / "csrc" / "vpass.cu", PKG / "csrc" / "vpdraft.cu"]
 HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "vpass.h"]
 OUT = PKG / "libvpass.so"
 

@@ -30,6 +30,12 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+}  // namespace
+
+void vp_set_last_error(const std::string& msg) { g_err = msg; }
+
+namespace {
+
 #define VP_CUDA(call)                                                                  \
   do {                                                                                 \
     cudaError_t e_ = (call);                                                           \

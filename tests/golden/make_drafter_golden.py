@@ -22,15 +22,8 @@ TEXTS = [  # synthetic prompts written for this fixture
 ]
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", required=True)
-    ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "drafter_trees.json"))
-    a = ap.parse_args()
-    sys.path.insert(0, os.path.join(a.reference, "tools", "draft"))
-    import ildraft as d
-
-    t = d.Tables.load(os.path.join(a.reference, "tools", "draft", "ildraft-q4.bin"))
+def golden_cases(d, t) -> dict:
+    """The golden record of the TEXTS requests on table t with the reference module d (ildraft)."""
     rnd = random.Random(11)
     cases = []
     for text in TEXTS:
@@ -62,8 +55,20 @@ def main():
             out = out + grow
         cases.append({"pids": pids, "text": text, "neighbours": [[float(s), len(seq)] for s, seq, _ in dr.nb],
                       "steps": steps})
+    return {"B": 15, "branch": 8, "cases": cases}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    ap.add_argument("--out", default=os.path.join(os.path.dirname(__file__), "drafter_trees.json"))
+    a = ap.parse_args()
+    sys.path.insert(0, os.path.join(a.reference, "tools", "draft"))
+    import ildraft as d
+
+    t = d.Tables.load(os.path.join(a.reference, "tools", "draft", "ildraft-q4.bin"))
     with open(a.out, "w") as f:
-        json.dump({"B": 15, "branch": 8, "cases": cases}, f, separators=(",", ":"))
+        json.dump(golden_cases(d, t), f, separators=(",", ":"))
     print(a.out, os.path.getsize(a.out), "bytes")
 
 

@@ -1,0 +1,59 @@
+"""The device drafter (vp_draft, k_draft) against the reference drafter's golden record
+(tests/golden/drafter_trees.json, made by the reference's tools/draft/ildraft.py) on the table
+subset tests/golden/draft_subset.ildraft: for every golden step the same tree node for node, every
+expansion in the reference's order with the reference's 8 probabilities (to 1e-9), and the tree
+buffer the next verify pass reads.
+
+Candidates with identical feature rows have identical scores on the GPU, so their order is the
+token order the reference's rule asks for (probability descending, then token ascending). The
+reference computes its scores with a BLAS matrix product whose rounding can differ by a few ulps
+between identical rows, which may order such candidates differently; so each expansion's tokens are
+checked through the CPU oracle (pinned to the golden record by tests/test_drafter_oracle.py): every
+token the GPU ranks k-th has, in the reference's arithmetic, the reference's k-th probability."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(__file__)
+GOLD = json.load(open(os.path.join(HERE, "golden", "drafter_trees.json")))
+
+
+def test_device_drafter_reproduces_the_reference_trees():
+    from instantllm_b200 import draft_table as dt
+    from instantllm_b200.drafter import DeviceDrafter
+    from oracle import drafter as D
+
+    ot = D.OracleTable(dt.DraftTable.load(os.path.join(HERE, "golden", "draft_subset.ildraft")))
+    d = DeviceDrafter(os.path.join(HERE, "golden", "draft_subset.ildraft"))
+    dev = d.device
+    tree = torch.zeros(65, dtype=torch.int32, device=dev)
+    n_steps = 0
+    for case in GOLD["cases"]:
+        d.begin(case["pids"], case["text"])
+        req = D.Request(ot, case["pids"], case["text"])
+        for st in case["steps"]:
+            out = torch.tensor(st["out"] + [0], dtype=torch.int32, device=dev)  # non-empty buffer
+            got = d.draft(tree, out, n_out=len(st["out"]), B=GOLD["B"], branch=GOLD["branch"], debug=True)
+            assert got["status"] == 0
+            assert (got["parents"], got["tokens"]) == (st["parents"], st["tokens"]), (case["text"], st["out"])
+            for k, (path, top) in enumerate(st["expansions"]):
+                want_p = [p for _, p in top]
+                gt = [int(x) for x in got["exp_tokens"][k][:len(top)]]
+                assert len(set(gt)) == len(gt) and all(x >= 0 for x in gt), (k, path)
+                assert np.allclose(got["exp_probs"][k][:len(top)], want_p, rtol=1e-9, atol=0), (k, path)
+                ref = dict(req.probs(list(st["out"]) + list(path)))
+                assert np.allclose([ref[x] for x in gt], want_p, rtol=1e-9, atol=0), (k, path, gt)
+            tb = tree.cpu().numpy()
+            n = len(st["tokens"]) + 1
+            assert tb[0] == n
+            for i, (par, tok) in enumerate(zip(st["parents"], st["tokens"])):
+                assert tb[17 + i + 1] == par + 1 and tb[33 + i + 1] == tok
+                assert tb[1 + i + 1] == tb[1 + par + 1] + 1
+            n_steps += 1
+    assert n_steps == sum(len(c["steps"]) for c in GOLD["cases"])
+    d.close()
