@@ -185,8 +185,6 @@ struct AttnSmem {
   // [warp][K, V][position][dim] staging; the warp's record overwrites its K rows once S is done
   alignas(128) __half kv[ATT_SEGSUB][2][ATT_SUB][HD];
   float q[GQ][HD];             // query rows of row t for the kv head's 7 heads
-  float wgt[GQ][ATT_SEGSUB];   // combine: e^(m_c - M) per head and record (local records)
-  float inv[GQ];               // combine: 1 / sum_c l_c e^(m_c - M)
   int late;                    // a polling warp gave up (bounded wait)
   int last;
 };
@@ -206,50 +204,64 @@ __device__ __forceinline__ int attn_units(const RowInfo* ri) {
 }
 
 // Final output of (row t, kv head g) from its nsub records in sub-chunk order (record cc at
-// base + cc * stride): M = max m_c, w_c = e^(m_c - M), O = sum_c o_c w_c / sum_c l_c w_c. The
-// weights are formed once per (head, record) by 7 threads, then every output sums its records.
-// Global records (rows longer than one segment) hold up to max_subs records; their weights are
-// recomputed per output (nsub can exceed the shared array).
-template <bool GLOBAL>
-__device__ __forceinline__ void attn_combine(const Scratch& s, const float* base, int stride, int nsub,
-                                             int t, int g, AttnSmem& sm) {
-  auto ld = [&](const float* q) { return GLOBAL ? __ldcg(q) : *q; };
-  const int tid = threadIdx.x;
-  if constexpr (!GLOBAL) {
-    if (tid < GQ) {
-      const int h = tid;
-      float M = -INFINITY;
-      for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, base[cc * stride + h * (2 + HD)]);
-      float Ls = 0.f;
-      for (int cc = 0; cc < nsub; ++cc) {
-        const float* r = base + cc * stride + h * (2 + HD);
-        const float w = expf(r[0] - M);
-        sm.wgt[h][cc] = w;
-        Ls = fmaf(r[1], w, Ls);
+// base + cc * stride): M = max m_c, w_c = e^(m_c - M), O = sum_c o_c w_c / sum_c l_c w_c.
+//
+// The outputs go to the O projection as flagged words (two adjacent columns per word, written by
+// the even lane), so that the O stage needs no grid barrier: GQ * HD = 448 outputs fill 14 warps
+// exactly, so both lanes of a pair are always active.
+__device__ __forceinline__ void attn_out(uint64_t* att_ll, uint32_t flag, int t, int col, float v) {
+  const uint32_t u = __half_as_ushort(__float2half_rn(v));
+  const uint32_t nb = __shfl_down_sync(0xffffffffu, u, 1);
+  if ((col & 1) == 0) st_flagged(att_ll + act_index(t, col) / 2, u | (nb << 16), flag);
+}
+static_assert((GQ * HD) % 32 == 0, "attention outputs fill whole warps");
+
+// Records in shared memory (one segment, nsub <= ATT_SEGSUB): every output thread forms the
+// weights of its head itself (the same values in all 64 threads of the head), so no thread waits
+// for another and the record loads and exponentials of all sub-chunks are in flight together.
+__device__ __forceinline__ void attn_combine_local(uint64_t* att_ll, uint32_t flag, const float* base, int stride,
+                                                   int nsub, int t, int g) {
+  for (int i = threadIdx.x; i < GQ * HD; i += PASS_THREADS) {
+    const int h = i / HD, d = i % HD;
+    const float* rh = base + h * (2 + HD);
+    float m[ATT_SEGSUB], l[ATT_SEGSUB], o[ATT_SEGSUB];
+    float M = -INFINITY;
+#pragma unroll
+    for (int cc = 0; cc < ATT_SEGSUB; ++cc) {
+      m[cc] = cc < nsub ? rh[cc * stride] : -INFINITY;
+      l[cc] = cc < nsub ? rh[cc * stride + 1] : 0.f;
+      o[cc] = cc < nsub ? rh[cc * stride + 2 + d] : 0.f;
+      M = fmaxf(M, m[cc]);
+    }
+    float O = 0.f, Ls = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < ATT_SEGSUB; ++cc) {
+      if (cc < nsub) {
+        const float w = expf(m[cc] - M);
+        Ls = fmaf(l[cc], w, Ls);
+        O = fmaf(o[cc], w, O);
       }
-      sm.inv[h] = Ls;
     }
-    cons_sync();
-    for (int i = tid; i < GQ * HD; i += PASS_THREADS) {
-      const int h = i / HD, d = i % HD;
-      float O = 0.f;
-      for (int cc = 0; cc < nsub; ++cc) O = fmaf(base[cc * stride + h * (2 + HD) + 2 + d], sm.wgt[h][cc], O);
-      s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / sm.inv[h]);
+    attn_out(att_ll, flag, t, (g * GQ + h) * HD + d, O / Ls);
+  }
+}
+
+// Records in global memory (rows longer than one segment) hold up to max_subs records; their
+// weights are recomputed per output (nsub can exceed the shared array).
+__device__ __forceinline__ void attn_combine_global(const Scratch& s, const float* base, int stride, int nsub,
+                                                    int t, int g) {
+  for (int i = threadIdx.x; i < GQ * HD; i += PASS_THREADS) {
+    const int h = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, __ldcg(base + cc * stride + h * (2 + HD)));
+    float O = 0.f, Ls = 0.f;
+    for (int cc = 0; cc < nsub; ++cc) {
+      const float* r = base + cc * stride + h * (2 + HD);
+      const float w = expf(__ldcg(r) - M);
+      Ls = fmaf(__ldcg(r + 1), w, Ls);
+      O = fmaf(__ldcg(r + 2 + d), w, O);
     }
-  } else {
-    for (int i = tid; i < GQ * HD; i += PASS_THREADS) {
-      const int h = i / HD, d = i % HD;
-      float M = -INFINITY;
-      for (int cc = 0; cc < nsub; ++cc) M = fmaxf(M, ld(base + cc * stride + h * (2 + HD)));
-      float O = 0.f, Ls = 0.f;
-      for (int cc = 0; cc < nsub; ++cc) {
-        const float* r = base + cc * stride + h * (2 + HD);
-        const float w = expf(ld(r) - M);
-        Ls = fmaf(ld(r + 1), w, Ls);
-        O = fmaf(ld(r + 2 + d), w, O);
-      }
-      s.act_a[act_index(t, (g * GQ + h) * HD + d)] = __float2half_rn(O / Ls);
-    }
+    attn_out(s.att_ll, s.flag_q, t, (g * GQ + h) * HD + d, O / Ls);
   }
 }
 
@@ -313,14 +325,19 @@ __device__ __noinline__ void attn_poll_q(const uint64_t* qw, uint32_t flag, Attn
   uint32_t pend = (1u << PER) - 1u;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+    // all loads of the round in flight before the first check (words 2u, 2u + 1, u = lane + 32k)
+    uint64_t a[PER], b[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
-      if (!(pend >> k & 1u)) continue;
-      const int u = lane + 32 * k;  // words 2u, 2u + 1
-      uint64_t a, b;
-      ld_flagged2(qw + 2 * u, a, b);
-      if ((uint32_t)(a >> 32) == flag && (uint32_t)(b >> 32) == flag) {
-        reinterpret_cast<float2*>(&sm.q[0][0])[u] = make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+      a[k] = 0;
+      b[k] = 0;
+      if (pend >> k & 1u) ld_flagged2(qw + 2 * (lane + 32 * k), a[k], b[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      if ((pend >> k & 1u) && (uint32_t)(a[k] >> 32) == flag && (uint32_t)(b[k] >> 32) == flag) {
+        reinterpret_cast<float2*>(&sm.q[0][0])[lane + 32 * k] =
+            make_float2(__uint_as_float((uint32_t)a[k]), __uint_as_float((uint32_t)b[k]));
         pend &= ~(1u << k);
       }
     }
@@ -349,24 +366,39 @@ __device__ __noinline__ void attn_poll_rows(const uint64_t* kw, const uint64_t* 
   for (int k = 0; k < 4; ++k)
     if (j0 + (lane >> 3) + 4 * k < j1) pend |= 3u << (2 * k);
   const unsigned long long t0 = globaltimer();
+  // source words of each (row, K / V) slot of this lane, fixed for the unit
+  const uint64_t* src[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const int jv = j0 + (lane >> 3) + 4 * k;
+      const int prow = ri->path[t][min(max(jv - pos, 0), ROWS - 1)];
+      src[2 * k + kv] = (kv ? vw : kw) + (size_t)prow * (HD / 2) + 4 * ch;
+    }
   for (uint32_t it = 0; pend && it < (1u << 24); ++it) {
+    // all loads of the round in flight before the first check
+    uint64_t a[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0;
+      if (pend >> i & 1u) {
+        ld_flagged2(src[i], a[i][0], a[i][1]);
+        ld_flagged2(src[i] + 2, a[i][2], a[i][3]);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
       for (int kv = 0; kv < 2; ++kv) {
-        if (!(pend >> (2 * k + kv) & 1u)) continue;
-        const int jv = j0 + (lane >> 3) + 4 * k;
-        const int prow = ri->path[t][min(jv - pos, ROWS - 1)];
-        const uint64_t* w = (kv ? vw : kw) + (size_t)prow * (HD / 2) + 4 * ch;
-        uint64_t a0, a1, a2, a3;
-        ld_flagged2(w, a0, a1);
-        ld_flagged2(w + 2, a2, a3);
-        if ((uint32_t)(a0 >> 32) == flag && (uint32_t)(a1 >> 32) == flag && (uint32_t)(a2 >> 32) == flag &&
-            (uint32_t)(a3 >> 32) == flag) {
+        const int i = 2 * k + kv;
+        if ((pend >> i & 1u) && (uint32_t)(a[i][0] >> 32) == flag && (uint32_t)(a[i][1] >> 32) == flag &&
+            (uint32_t)(a[i][2] >> 32) == flag && (uint32_t)(a[i][3] >> 32) == flag) {
+          const int jv = j0 + (lane >> 3) + 4 * k;
           const int c = jv / ATT_SUB, r = jv % ATT_SUB;
           *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&sm.kv[c - c0][kv][0][0]) + kv_off(r, ch)) =
-              make_uint4((uint32_t)a0, (uint32_t)a1, (uint32_t)a2, (uint32_t)a3);
-          pend &= ~(1u << (2 * k + kv));
+              make_uint4((uint32_t)a[i][0], (uint32_t)a[i][1], (uint32_t)a[i][2], (uint32_t)a[i][3]);
+          pend &= ~(1u << i);
         }
       }
     if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
@@ -393,9 +425,11 @@ __device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const
 #define ATT_DSTAMP(k, dep) do { if (tr) { const unsigned long long v_ = globaltimer_after(dep); if ((threadIdx.x & 31) == 0) tr[256 * (k)] = v_; } } while (0)
   const int lane = threadIdx.x & 31, gid = lane >> 2, t4 = lane & 3;
   const int L = ri->pos + ri->depth[t] + 1;
-  // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads (MMA rows 7..15 are zero):
-  // dims ks * 16 + 2 t4 + {0, 1} and + 8
-  uint32_t qa[4][2][2];  // [k-step][hi, lo][a0, a2]
+  // q * 0.125 (exact) as fp16 hi + lo A fragments of the 7 query heads: the hi halves in MMA rows
+  // 0..6, the lo halves in rows 8..14 (rows 7 and 15 are zero), so that one MMA forms both
+  // products and the two accumulator rows of a thread are added once at the end; dims
+  // ks * 16 + 2 t4 + {0, 1} (a0 / a1) and + 8 (a2 / a3)
+  uint32_t qa[4][2][2];  // [k-step][hi, lo][k 0..7, k 8..15]
   {
     const float* q = &sm.q[min(gid, GQ - 1)][0];
     const float z = gid < GQ ? ATTN_SCALE : 0.f;
@@ -413,7 +447,8 @@ __device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const
   const uint32_t sK = smem_u32(buf), sV = sK + ATT_SUB * HD * 2;
   ATT_DSTAMP(4, __uint_as_float(*reinterpret_cast<const uint32_t*>(buf)));
   const int mi = lane >> 3, ri8 = lane & 7;  // ldmatrix: this lane addresses row ri8 of block mi
-  // S = q K^T: n-tile j = positions 8j..8j+7; one x4 load gives the B fragments of two k-steps
+  // S = q K^T: n-tile j = positions 8j..8j+7; one x4 load gives the B fragments of two k-steps.
+  // sacc[j][e] is the hi product of position 8j + 2 t4 + e, sacc[j][2 + e] the lo product.
   float sacc[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -426,9 +461,9 @@ __device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const
               kb[2 * hh + 1][1]);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks)
+      mma16816(sacc[j], qa[ks][0][0], qa[ks][1][0], qa[ks][0][1], qa[ks][1][1], kb[ks][0], kb[ks][1]);
 #pragma unroll
-      for (int part = 0; part < 2; ++part)
-        mma16816(sacc[j], qa[ks][part][0], 0u, qa[ks][part][1], 0u, kb[ks][0], kb[ks][1]);
+    for (int e = 0; e < 2; ++e) sacc[j][e] += sacc[j][2 + e];
   }
   ATT_DSTAMP(5, sacc[3][0]);
   // masked softmax of query head gid over the 32 positions (position 8j + 2*t4 + e)
@@ -456,8 +491,9 @@ __device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const
   cp_async_wait<0>();  // the V rows
   __syncwarp();
   ATT_DSTAMP(6, __uint_as_float(*reinterpret_cast<const uint32_t*>(buf + ATT_SUB * HD)) + l);
-  // P as the A operand: k-step kk = positions 16kk..16kk+15 = n-tiles 2kk (a0) and 2kk+1 (a2)
-  uint32_t pa[2][2][2];  // [kk][hi, lo][a0, a2]
+  // P as the A operand: k-step kk = positions 16kk..16kk+15 = n-tiles 2kk (k 0..7) and 2kk+1
+  // (k 8..15); hi halves in rows 0..6, lo halves in rows 8..14, as for q
+  uint32_t pa[2][2][2];  // [kk][hi, lo][k 0..7, k 8..15]
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
     split_half2(sacc[2 * kk][0], sacc[2 * kk][1], pa[kk][0][0], pa[kk][1][0]);
@@ -473,16 +509,14 @@ __device__ __noinline__ void attn_compute(const RowInfo* ri, int t, int c, const
     for (int kk = 0; kk < 2; ++kk) {
       uint32_t b00, b01, b10, b11;  // [n-tile 2np + x][b0, b1]
       ldsm_x4_trans(sV + kv_off(16 * kk + 8 * (mi & 1) + ri8, 2 * np + (mi >> 1)), b00, b01, b10, b11);
-#pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        mma16816(oacc[0], pa[kk][part][0], 0u, pa[kk][part][1], 0u, b00, b01);
-        mma16816(oacc[1], pa[kk][part][0], 0u, pa[kk][part][1], 0u, b10, b11);
-      }
+      mma16816(oacc[0], pa[kk][0][0], pa[kk][1][0], pa[kk][0][1], pa[kk][1][1], b00, b01);
+      mma16816(oacc[1], pa[kk][0][0], pa[kk][1][0], pa[kk][0][1], pa[kk][1][1], b10, b11);
     }
     if (gid < GQ) {
 #pragma unroll
       for (int x = 0; x < 2; ++x)
-        *reinterpret_cast<float2*>(r + 2 + (2 * np + x) * 8 + 2 * t4) = make_float2(oacc[x][0], oacc[x][1]);
+        *reinterpret_cast<float2*>(r + 2 + (2 * np + x) * 8 + 2 * t4) =
+            make_float2(oacc[x][0] + oacc[x][2], oacc[x][1] + oacc[x][3]);
     }
     __syncwarp();
   }
@@ -537,7 +571,7 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, Attn
   if (tr && tid == 0) tr[256 * 125] = globaltimer();
 #undef ATT_TSTAMP
   if (nseg == 1) {
-    attn_combine<false>(s, rec0, ATT_REC_STRIDE, nsub, t, g, sm);
+    attn_combine_local(s.att_ll, s.flag_q, rec0, ATT_REC_STRIDE, nsub, t, g);
     cons_sync();
     if (tr && tid == 0) tr[256 * 127] = globaltimer();
     return;
@@ -551,7 +585,7 @@ __device__ void attn_unit(const Scratch& s, int layer, int max_subs, int u, Attn
   cons_sync();
   if (sm.last) {
     __threadfence();
-    attn_combine<true>(s, base, ATT_REC, nsub, t, g, sm);
+    attn_combine_global(s, base, ATT_REC, nsub, t, g);
     if (tid == 0) s.tickets[ATT_TICKETS + t * NKV + g] = 0;
   }
   cons_sync();

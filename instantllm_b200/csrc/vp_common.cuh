@@ -73,13 +73,15 @@ struct Scratch {
   float* x;             // [16][896] residual stream, fp32
   float* q;             // [16][896] roped queries, fp32
   __half* act_h;        // act blocks, K = 896: normed x for QKV / GU / lm_head
-  __half* act_a;        // act blocks, K = 896: attention output for O
   __half* act_f;        // act blocks, K = 4864: SiLU(gate)*up for down
   float* ss;            // [HRB][16] per-row-block sums of squares of x (RMSNorm partials)
   uint64_t* act_ll;     // O output for gate/up: act blocks as (half2, flag) words [H * 16 / 2]
   uint64_t* ss_ll;      // its RMSNorm partials as (float, flag) words [HRB][16]
   uint64_t* q_ll;       // QKV output for the attention: roped queries as (float, flag) [16][896]
   uint64_t* kv_ll;      // and the pass rows' K / V as (half2, flag) words [K, V][kv head][16][32]
+  uint64_t* att_ll;     // attention output for O: act blocks as (half2, flag) words [H * 16 / 2]
+  uint64_t* dn_ll;      // down output for the next QKV: normed x as act blocks of (half2, flag) words
+  uint64_t* dn_ss_ll;   // and its RMSNorm partials as (float, flag) words [HRB][16]
   uint32_t flag_q;      // flag of q_ll / kv_ll in this launch and layer
   float* part;          // split-K partial tiles [max units][16*16]
   int* tickets;         // split-K / attention arrival counters (self-resetting)

@@ -76,6 +76,8 @@ struct GemmParams {
   const uint64_t* act_ll_in;  // SILU (persistent kernel): flagged inputs instead of act / ss_in
   const uint64_t* ss_ll_in;
   uint32_t flag;         // flag of this launch and layer
+  const unsigned* gate;  // persistent kernel: flagged inputs are polled once this arrival counter
+  unsigned gate_target;  // reaches gate_target (every producer CTA wrote its words), or null
   Scratch s;
 };
 

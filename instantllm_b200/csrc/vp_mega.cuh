@@ -50,6 +50,17 @@ constexpr int MK_TRACE = MK_TRACE_BASE;
 static_assert(MK_CONS == PASS_THREADS && MK_CONS == CONS_THREADS, "consumer warps run the stage code");
 
 enum MkStage { MK_QKV = 0, MK_O = 1, MK_GU = 2, MK_DOWN = 3, MK_LM = 4 };
+// Stage arrival counters of a launch (reset by the last CTA to exit): attention units and
+// down-projection CTAs that have written their flagged outputs.
+enum MkGate { MK_GATE_ATT = 0, MK_GATE_DOWN = 1, MK_GATES = 2 };
+// Arrival count at which the consumers of a stage with `count` producers per layer start polling
+// the flagged words of layer l: half of the producers. The producers of a stage finish within a
+// fraction of a microsecond of each other, so by then the rest of the words are landing; polling
+// the words directly from there saves the second L2 round trip of a full gate (counter, then
+// data), and waiting for half keeps the polls from loading L2 while the producer stage runs.
+__device__ __forceinline__ unsigned mk_gate_target(int l, int count) {
+  return (unsigned)((l + 1) * count - count / 2);
+}
 
 // Parts per row-block (K split across the warps of one CTA) of a GEMM stage whose CTA owns nrb
 // row-blocks, and K groups of each GEMM stage. Gate/up fills the 16 warps once: 4 row-blocks x 4
@@ -110,6 +121,7 @@ struct MegaParams {
   unsigned long long* bar;    // grid barrier arrival counter (0 at launch, reset by the last CTA)
   unsigned* exit_ctr;         // CTAs that finished this launch
   unsigned* seq;              // launches so far: the flag of layer l is seq * 64 + l + 1
+  unsigned* gate;             // [MK_GATES] stage arrival counters (0 at launch)
   unsigned long long* trace;  // CTA 0: %globaltimer after each stage (MK_TRACE entries)
   float* lm_pval;             // [16][gridDim] per-CTA argmax partials
   int* lm_pidx;
@@ -162,6 +174,36 @@ __device__ bool grid_barrier(const MegaParams& p, unsigned long long target, int
   }
   mk_sync();
   return *(volatile int*)sAbort == 0;
+}
+
+// Gated flagged transport: a producer CTA writes its outputs as flagged words, then (after a CTA
+// barrier) adds one to the stage's arrival counter with a relaxed atomic: no fence, since every
+// word carries its own flag. A consumer CTA polls that one counter (one thread) until enough
+// producers arrived (mk_gate_target) and only then polls the words themselves, so that the
+// consumers do not flood L2 with polls of the data while the producer stage still runs.
+__device__ __forceinline__ void gate_arrive(unsigned* ctr) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded: a timeout sets the error bit and the CTA's abort flag. Ends with a CTA barrier.
+__device__ void gate_wait(const unsigned* ctr, unsigned target, vp_state* st, volatile int* sAbort) {
+  if (threadIdx.x == 0 && *sAbort == 0) {
+    bool ok = false;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 0; i < (1u << 26); ++i) {
+      if (ld_relaxed_u32(ctr) >= target) { ok = true; break; }
+      if ((i & 63) == 63 && globaltimer() - t0 > WAIT_NS) break;
+    }
+    if (!ok) {
+      set_error(st, VP_DEV_ERR_TIMEOUT);
+      *sAbort = 1;
+    }
+  }
+  mk_sync();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -646,38 +688,49 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
   }
 }
 
-// Flagged inputs of a stage (gate/up: the O projection's output): the act blocks (3,584 16-byte
-// units of two flagged words, 7 per thread) and the RMSNorm partials (448 units) go to shared
-// memory as soon as every word carries this layer's flag. The first round issues every load at
-// once; later rounds reload only what was not ready. Bounded: a timeout sets the error bit.
+// Flagged inputs of a stage (O: the attention outputs; gate/up: O's output; QKV: the previous
+// down projection's output): the act blocks (3,584 16-byte units of two flagged words, 7 per
+// thread) and the RMSNorm partials (448 units, if any) go to shared memory as soon as every word
+// carries this layer's flag. The first round issues every load at once; later rounds reload only
+// what was not ready. Only the pass's n rows are waited for (the attention writes no padding
+// rows); the padding rows of the act blocks are zeros. Bounded: a timeout sets the error bit.
 constexpr int MK_LL_UNITS = (int)(MK_ACT_BYTES / 8 / MK_CONS);  // act units (8 data bytes) per thread
 static_assert(MK_LL_UNITS * MK_CONS * 8 == MK_ACT_BYTES, "flagged act units split evenly");
-__device__ __noinline__ void mk_poll_flagged(const uint64_t* act_ll, const uint64_t* ss_ll, uint32_t F,
+__device__ __noinline__ void mk_poll_flagged(const uint64_t* act_ll, const uint64_t* ss_ll, uint32_t F, int n,
                                              uint8_t* sAct, float* sSs, vp_state* st, volatile int* sAbort) {
   const int tid = threadIdx.x;
-  const bool has_ss = tid < HRB * 16 / 2;
-  uint32_t pending = (1u << MK_LL_UNITS) - 1u | (has_ss ? 1u << MK_LL_UNITS : 0u);
+  const bool has_ss = ss_ll != nullptr && tid < HRB * 16 / 2;
+  uint32_t pending = has_ss ? 1u << MK_LL_UNITS : 0u;
+#pragma unroll
+  for (int k = 0; k < MK_LL_UNITS; ++k) {
+    // unit u holds data words 2u, 2u + 1 of an act block: lane (u / 2) % 32, token half u % 2
+    const int u = tid + k * MK_CONS, t = (u & 1) * 8 + ((u >> 1) & 31) / 4;
+    if (t < n) pending |= 1u << k;
+    else reinterpret_cast<uint2*>(sAct)[u] = make_uint2(0u, 0u);
+  }
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 0; pending && it < (1u << 24); ++it) {
+    // every load of the round is in flight before the first check: one L2 round trip per round
+    uint64_t a[MK_LL_UNITS + 1], b[MK_LL_UNITS + 1];
+#pragma unroll
+    for (int k = 0; k <= MK_LL_UNITS; ++k) {
+      a[k] = 0;
+      b[k] = 0;
+      if (pending >> k & 1u)
+        ld_flagged2(k < MK_LL_UNITS ? act_ll + 2 * (tid + k * MK_CONS) : ss_ll + 2 * tid, a[k], b[k]);
+    }
 #pragma unroll
     for (int k = 0; k < MK_LL_UNITS; ++k) {
-      if (!(pending >> k & 1u)) continue;
-      const int u = tid + k * MK_CONS;
-      uint64_t a, b;
-      ld_flagged2(act_ll + 2 * u, a, b);
-      if ((uint32_t)(a >> 32) == F && (uint32_t)(b >> 32) == F) {
-        reinterpret_cast<uint2*>(sAct)[u] = make_uint2((uint32_t)a, (uint32_t)b);
+      if ((pending >> k & 1u) && (uint32_t)(a[k] >> 32) == F && (uint32_t)(b[k] >> 32) == F) {
+        reinterpret_cast<uint2*>(sAct)[tid + k * MK_CONS] = make_uint2((uint32_t)a[k], (uint32_t)b[k]);
         pending &= ~(1u << k);
       }
     }
-    if (pending >> MK_LL_UNITS & 1u) {
-      uint64_t a, b;
-      ld_flagged2(ss_ll + 2 * tid, a, b);
-      if ((uint32_t)(a >> 32) == F && (uint32_t)(b >> 32) == F) {
-        sSs[2 * tid] = __uint_as_float((uint32_t)a);
-        sSs[2 * tid + 1] = __uint_as_float((uint32_t)b);
-        pending &= ~(1u << MK_LL_UNITS);
-      }
+    if ((pending >> MK_LL_UNITS & 1u) && (uint32_t)(a[MK_LL_UNITS] >> 32) == F &&
+        (uint32_t)(b[MK_LL_UNITS] >> 32) == F) {
+      sSs[2 * tid] = __uint_as_float((uint32_t)a[MK_LL_UNITS]);
+      sSs[2 * tid + 1] = __uint_as_float((uint32_t)b[MK_LL_UNITS]);
+      pending &= ~(1u << MK_LL_UNITS);
     }
     if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
   }
@@ -736,7 +789,11 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
       if (nrb == 1 && threadIdx.x < 16) sEpc[threadIdx.x] = gp.wnext[rb0 * 16 + threadIdx.x];
     }
     cp_async_wait<0>();
-    if (gp.act_ll_in) mk_poll_flagged(gp.act_ll_in, gp.ss_ll_in, gp.flag, sAct, sSs, gp.s.st, sAbort);
+    if (gp.act_ll_in) {
+      if (gp.gate) gate_wait(gp.gate, gp.gate_target, gp.s.st, sAbort);
+      if (!*sAbort)
+        mk_poll_flagged(gp.act_ll_in, gp.ss_ll_in, gp.flag, gp.s.ri->n, sAct, sSs, gp.s.st, sAbort);
+    }
   }
   mk_sync();
   MK_CSTAMP(p, dtr, 8 * st + 1);
@@ -880,70 +937,90 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     };
 
     if (live) {
+      // One grid barrier per layer (after gate/up): every other stage boundary is a flagged
+      // transport (QKV -> attention and O -> gate/up polled directly; attention -> O and down ->
+      // the next QKV gated by the producers' arrival counter). No buffer of flagged words is rewritten
+      // while a reader of its previous contents is left: each is written once per layer, and its
+      // next writer depends, through the layer's chain of stages, on every one of its readers.
+      const int units = attn_units(sRi);
       for (int l = 0; l < p.n_layers && ok; ++l) {
         tl = l;
         tb = 0;
         MK_CSTAMP(p, l == MK_TRACE_LAYER, 56);
+        const bool last = l + 1 == p.n_layers;
         GemmParams gp = {};
         gp.s = s;
         gp.layer = l;
-        // QKV (+ RMSNorm scale, bias, RoPE, KV write)
+        // QKV (+ RMSNorm scale, bias, RoPE, KV write): layer 0 reads the embed's act blocks (after
+        // the embed barrier), later layers the previous down projection's flagged words
         gp.w = p.wqkv[l]; gp.act = s.act_h; gp.nrb = QKV / 16; gp.ng = H / GS;
         gp.bias = p.bqkv[l]; gp.ss_in = s.ss;
+        if (l > 0) {
+          gp.act_ll_in = s.dn_ll; gp.ss_ll_in = s.dn_ss_ll; gp.flag = flag0 + l - 1;
+          gp.gate = p.gate + MK_GATE_DOWN; gp.gate_target = mk_gate_target(l - 1, HRB);
+        }
         gp.s.flag_q = flag0 + l;
-        // no grid barrier: the attention units poll the flagged q and K / V rows they need (every
-        // CTA passed the barrier after the previous down projection, so the previous layer's
-        // words have no reader left)
+        // the attention units poll the flagged q and K / V rows they need
         ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_QKV);
         if (!ok) break;
         s.flag_q = flag0 + l;
-        // attention
-        {
-          const int units = attn_units(sRi);
-          for (int u = cta; u < units; u += G) {
-            MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 40);
+        // attention: each unit writes its outputs as flagged words, then arrives at the gate
+        for (int u = cta; u < units; u += G) {
+          MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 40);
 #ifdef VP_TRACE_DETAIL
-            attn_unit(s, l, p.max_chunks, u, sAtt,
-                      (p.trace && l == MK_TRACE_LAYER && u == cta && cta < 256)
-                          ? p.trace + MK_TRACE_BASE + 64 * 256 + cta : nullptr);
+          attn_unit(s, l, p.max_chunks, u, sAtt,
+                    (p.trace && l == MK_TRACE_LAYER && u == cta && cta < 256)
+                        ? p.trace + MK_TRACE_BASE + 64 * 256 + cta : nullptr);
 #else
-            attn_unit(s, l, p.max_chunks, u, sAtt);
+          attn_unit(s, l, p.max_chunks, u, sAtt);
 #endif
-            MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 42);
-          }
+          if (threadIdx.x == 0) gate_arrive(p.gate + MK_GATE_ATT);
+          MK_CSTAMP(p, l == MK_TRACE_LAYER && u == cta, 42);
         }
-        ok = barrier();
-        if (!ok) break;
-        // O + residual
+        // O + residual: polls the attention outputs once every unit arrived
         gp = GemmParams{};
         gp.s = s; gp.layer = l;
-        gp.w = p.wo[l]; gp.act = s.act_a; gp.nrb = H / 16; gp.ng = H / GS;
+        gp.w = p.wo[l]; gp.nrb = H / 16; gp.ng = H / GS;
+        gp.act_ll_in = s.att_ll; gp.flag = flag0 + l;
+        gp.gate = p.gate + MK_GATE_ATT; gp.gate_target = mk_gate_target(l, units);
         gp.wnext = p.ln2[l];
-        gp.act_ll_out = s.act_ll; gp.ss_ll_out = s.ss_ll; gp.flag = flag0 + l;
+        gp.act_ll_out = s.act_ll; gp.ss_ll_out = s.ss_ll;
         gp.xs = own_x ? sXrb : nullptr;
-        // no grid barrier: gate/up polls the flagged words it needs (every CTA passed the
-        // attention barrier, so no reader of the previous layer's words is left)
         ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_O);
         if (!ok) break;
-        // gate/up + SiLU
+        // gate/up + SiLU: polls O's outputs directly (no gate: the O stage is short, and the
+        // polls start as its CTAs finish their part)
         gp = GemmParams{};
         gp.s = s; gp.layer = l;
-        gp.w = p.wgu[l]; gp.act = s.act_h; gp.nrb = 2 * F / 16; gp.ng = H / GS;
+        gp.w = p.wgu[l]; gp.nrb = 2 * F / 16; gp.ng = H / GS;
         gp.act_ll_in = s.act_ll; gp.ss_ll_in = s.ss_ll; gp.flag = flag0 + l; gp.act_out = s.act_f;
         ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort, cta, G) && barrier();
         piece0 += pieces(MK_GU);
         if (!ok) break;
-        // down + residual
+        // down + residual: flagged words for the next QKV; the last layer's output feeds the
+        // lm_head through plain act blocks and a grid barrier
         gp = GemmParams{};
         gp.s = s; gp.layer = l;
         gp.w = p.wd[l]; gp.act = s.act_f; gp.nrb = H / 16; gp.ng = F / GS;
-        gp.wnext = l + 1 < p.n_layers ? p.ln1[l + 1] : p.final_norm;
-        gp.ss_out = s.ss; gp.act_out = s.act_h;
+        gp.wnext = last ? p.final_norm : p.ln1[l + 1];
+        const bool to_lm = last && p.do_lm;
+        if (to_lm) {
+          gp.ss_out = s.ss; gp.act_out = s.act_h;
+        } else {
+          gp.act_ll_out = s.dn_ll; gp.ss_ll_out = s.dn_ss_ll; gp.flag = flag0 + l;
+        }
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G) && barrier();
+        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_DOWN);
+        if (!ok) break;
+        if (to_lm) {
+          ok = barrier();
+        } else if (cta < HRB) {  // the down CTAs
+          mk_sync();
+          if (threadIdx.x == 0) gate_arrive(p.gate + MK_GATE_DOWN);
+        }
       }
       if (ok && p.do_lm) {
         GemmParams gp = {};
@@ -982,6 +1059,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     __threadfence();
     if (atomicAdd(p.exit_ctr, 1u) == (unsigned)G - 1) {
       *p.bar = 0ull;  // every CTA is past its last barrier: the next launch starts from zero
+      for (int i = 0; i < MK_GATES; ++i) p.gate[i] = 0u;
       *p.exit_ctr = 0u;
       *p.seq = *p.seq + 1u;  // the next launch's flags differ from every word written here
       __threadfence();

@@ -78,6 +78,7 @@ struct vp_ctx {
   unsigned long long* bar = nullptr;
   unsigned* exit_ctr = nullptr;
   unsigned* seq = nullptr;  // pass-kernel launches so far (flag epochs)
+  unsigned* gate = nullptr;  // [MK_GATES] stage arrival counters of the pass kernel
   float* lm_pval = nullptr;  // [16][grid] per-CTA argmax partials of the last pass
   int* lm_pidx = nullptr;
   unsigned long long* trace = nullptr;  // stage timestamps of the last pass (ns)
@@ -159,6 +160,7 @@ MegaParams mega_params(vp_ctx* c) {
   p.bar = c->bar;
   p.exit_ctr = c->exit_ctr;
   p.seq = c->seq;
+  p.gate = c->gate;
   p.lm_pval = c->lm_pval;
   p.lm_pidx = c->lm_pidx;
   p.trace = c->trace;
@@ -272,7 +274,6 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &s.out_tokens, (size_t)cfg->max_steps * sizeof(int32_t))) ||
       (r = dalloc(c, &s.x, ROWS * H * sizeof(float))) || (r = dalloc(c, &s.q, ROWS * H * sizeof(float))) ||
       (r = dalloc(c, &s.act_h, ROWS * H * sizeof(__half))) ||
-      (r = dalloc(c, &s.act_a, ROWS * H * sizeof(__half))) ||
       (r = dalloc(c, &s.act_f, ROWS * F * sizeof(__half))) ||
       (r = dalloc(c, &s.ss, HRB * ROWS * sizeof(float))) ||
       (r = dalloc(c, &s.part, 256 * sizeof(float))) ||
@@ -289,6 +290,10 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &s.ss_ll, (size_t)HRB * ROWS * sizeof(uint64_t))) ||
       (r = dalloc(c, &s.q_ll, (size_t)ROWS * H * sizeof(uint64_t))) ||
       (r = dalloc(c, &s.kv_ll, (size_t)2 * NKV * ROWS * (HD / 2) * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.att_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.dn_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.dn_ss_ll, (size_t)HRB * ROWS * sizeof(uint64_t))) ||
+      (r = dalloc(c, &c->gate, MK_GATES * sizeof(unsigned))) ||
       (r = dalloc(c, &c->lm_pval, (size_t)ROWS * sms * sizeof(float))) ||
       (r = dalloc(c, &c->lm_pidx, (size_t)ROWS * sms * sizeof(int))) ||
       (r = dalloc(c, &c->trace, MK_TRACE * sizeof(unsigned long long)))) {
