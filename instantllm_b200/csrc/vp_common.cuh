@@ -116,13 +116,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// A thread whose phase is not complete is suspended (it issues nothing) until the phase completes
+// or MBAR_SUSPEND_NS pass, so that waiting warps (the weight producer, consumers ahead of the ring)
+// do not take issue slots from the warps of their SM sub-partition that compute.
+constexpr uint32_t MBAR_SUSPEND_NS = 2000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(MBAR_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
@@ -252,6 +256,18 @@ __device__ __forceinline__ void cta_sync() {
 __device__ __forceinline__ void set_error(vp_state* st, int bits) {
   atomicOr(&st->err, bits);
   atomicExch(&st->done, 1);
+}
+
+// RMSNorm scale 1 / sqrt(mean(x^2) + eps) of one token from its HRB per-row-block partial sums of
+// squares, ld(r) giving partial r: four independent chains (partials r = c mod 4) added in a fixed
+// order, a short dependent chain that every kernel normalising the same rows shares, so that all
+// of them get the same bits.
+template <typename Ld>
+__device__ __forceinline__ float rms_inv(Ld ld) {
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int r = 0; r < HRB; ++r) a[r & 3] += ld(r);
+  return 1.f / sqrtf(((a[0] + a[1]) + (a[2] + a[3])) / (float)H + EPS);
 }
 
 // Reduction helpers with a fixed combination order (results never depend on timing).

@@ -362,15 +362,8 @@ __device__ void gemm_cta(const GemmParams& p, uint8_t* smem, int cta) {
       mbar_arrive_expect_tx(barAct, bytes);
       bulk_g2s(sAct, p.act + (size_t)g0 * 1024, bytes, barAct, policy_evict_last());
     }
-    if (MODE != MODE_RESID && threadIdx.x < 16) {
-      float v[HRB];  // all loads in flight at once, summed in fixed order
-#pragma unroll
-      for (int r = 0; r < HRB; ++r) v[r] = __ldcg(p.ss_in + r * 16 + threadIdx.x);
-      float sum = 0.f;
-#pragma unroll
-      for (int r = 0; r < HRB; ++r) sum += v[r];
-      sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
-    }
+    if (MODE != MODE_RESID && threadIdx.x < 16)
+      sRs[threadIdx.x] = rms_inv([&](int r) { return __ldcg(p.ss_in + r * 16 + threadIdx.x); });
     // every warp waits (warp-uniform) for the act blocks; a timeout is recorded, not acted on per lane
     const bool act_ok = mbar_wait_warp(barAct, 0);
     if (!act_ok && lane == 0) sOk = 0;

@@ -27,6 +27,12 @@ constexpr int MK_THREADS = MK_CONS + 32;         // + the producer warp
 constexpr int MK_NSLOT = 5;                      // weight ring slots
 constexpr int MK_SLOT = 28672;                   // bytes per slot
 constexpr int MK_PART_SLOTS = 24;                // partial tiles of a stage (1 KiB each)
+// The RMSNorm partials of a normalising stage's input (HRB x 16 floats) are staged in the first
+// MK_SS_SLOTS partial-tile slots and read while the jobs run, so those stages' jobs write their
+// partial tiles past them.
+constexpr int MK_SS_SLOTS = 4;
+static_assert(MK_SS_SLOTS * 256 >= HRB * 16 && MK_SS_SLOTS + 16 <= MK_PART_SLOTS,
+              "the staged RMSNorm partials and up to 16 jobs' partial tiles fit the partial area");
 // Stage trace: trace[0, 256) holds CTA 0's %globaltimer after each grid barrier of a launch.
 // Compiled with -DVP_TRACE_DETAIL (performance work only), every CTA also stamps the steps of
 // layer MK_TRACE_LAYER (and of the lm_head stage) at trace[MK_TRACE_BASE + 256 * event + cta]:
@@ -230,7 +236,8 @@ constexpr size_t MK_OFF_XRB = MK_OFF_RI + ((sizeof(RowInfo) + 15) & ~size_t(15))
 constexpr size_t MK_OFF_EPC = MK_OFF_XRB + 16 * 16 * 4;  // epilogue constants: 16 bias / norm weights,
                                                          // 128 (cos, sin) pairs
 constexpr size_t MK_OFF_BAR = (MK_OFF_EPC + (16 + 256) * 4 + 127) & ~size_t(127);
-constexpr size_t MK_SMEM = MK_OFF_BAR + 8 * (2 * MK_NSLOT);
+constexpr size_t MK_OFF_GS = MK_OFF_BAR + 8 * (2 * MK_NSLOT);  // group sums ready (mbarrier)
+constexpr size_t MK_SMEM = MK_OFF_GS + 8;
 static_assert(sizeof(AttnSmem) <= MK_OFF_RS - MK_OFF_ACT, "attention scratch fits its overlay");
 static_assert(MK_SMEM <= 232448, "dynamic shared memory of the pass kernel fits one sm_100 CTA");
 
@@ -241,6 +248,8 @@ struct MkRing {
   uint64_t* empty;  // [MK_NSLOT], one arrival per consumer warp
   int released;     // pieces this warp has released (identical in all lanes)
   int waited;       // pieces this warp has seen full
+  uint64_t* gsum;   // mbarrier: the H / GS group-sum warps of a stage wrote their sums
+  uint32_t gs_phase;  // phases of gsum completed so far (its parity is the next wait's)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -274,7 +283,7 @@ __device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sS
         const unsigned long long t0 = globaltimer();
         for (uint32_t i = 0; i < (1u << 26); ++i) {
           if (mbar_try_wait(empty + slot, par)) { got = true; break; }
-          if ((i & 63) == 63 && (*sStop || globaltimer() - t0 > WAIT_NS)) break;
+          if (*sStop || ((i & 15) == 15 && globaltimer() - t0 > WAIT_NS)) break;
         }
         if (!got) { ok = false; break; }
       }
@@ -440,6 +449,9 @@ __device__ __forceinline__ bool mk_release(MkRing& rg, int k, int lane) {
 // memory.
 struct MkJobs {
   int piece0, rb0, nrb, P, ng;
+  float* part;           // partial tile of job j at part + j * 256
+  uint64_t* gsum;        // non-null: wait for this phase of the group-sum mbarrier before the
+  uint32_t gs_parity;    // first tile (the fold reads the group sums)
   const __half* actg;    // down projection: act blocks of the SiLU output
   unsigned long long* trace;  // performance tracing only (null: off)
 };
@@ -456,7 +468,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
   const int gid = lane >> 2, tid4 = lane & 3;
   uint8_t* sAct = smem + MK_OFF_ACT;
   float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
-  float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
+  float* sPart = J.part;
   const float* sRs = reinterpret_cast<const float*>(smem + MK_OFF_RS);
   float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
   int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
@@ -467,6 +479,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
   // jobs (row-block i, part q) -> warp (i * P + q) % 16, in increasing tile order per warp
   const int jobs = nrb * P;
   bool ok = true;
+  if (J.gsum && warp < jobs) ok = mbar_wait_warp(J.gsum, J.gs_parity);
   for (int j = warp; j < jobs && ok; j += MK_WARPS) {
     const int i = j / P, q = j % P;
     const int ga = q * ng / P, gb = (q + 1) * ng / P;
@@ -592,6 +605,35 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
   const Scratch& s = gp.s;
   const RowInfo* ri = s.ri;
   const int n = ri->n;
+  if constexpr (MODE == MODE_SILU) {
+    // up to 5 row-blocks (640 elements) on 512 threads: a thread's two elements are summed
+    // together, so that the second one does not wait for the first one's latency chain
+    const int ne = nrb * 128;
+    for (int e0 = threadIdx.x; e0 < ne; e0 += 2 * MK_CONS) {
+      const bool two = e0 + MK_CONS < ne;
+      const int e[2] = {e0, two ? e0 + MK_CONS : e0};
+      float g[2] = {0.f, 0.f}, u[2] = {0.f, 0.f};
+      for (int q = 0; q < P; ++q)
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float* part = sPart + (e[k] >> 7) * P * 256 + q * 256 + ((e[k] & 127) >> 3) * 8 + (e[k] & 7);
+          g[k] += part[0];
+          u[k] += part[128];
+        }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int lt = e[k] & 127, t = lt >> 3, f = (rb0 + (e[k] >> 7)) * 8 + (lt & 7);
+        float h = 0.f;
+        if (t < n) {
+          const float gg = g[k] * rs[t];
+          const float uu = u[k] * rs[t];
+          h = gg / (1.f + expf(-gg)) * uu;
+        }
+        if (k == 0 || two) gp.act_out[act_index(t, f)] = __float2half_rn(h);
+      }
+    }
+    return;
+  }
   for (int e = threadIdx.x; e < nrb * 128; e += MK_CONS) {
     const int i = e >> 7, lt = e & 127, t = lt >> 3, rp = lt & 7, rb = rb0 + i;
     float s0 = 0.f, s1 = 0.f;
@@ -675,15 +717,6 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
         gp.act_out[act_index(t, d1)] = h1;
         if (rp == 0) gp.ss_out[rb * 16 + t] = sq;
       }
-    } else {  // MODE_SILU
-      const int f = rb * 8 + rp;
-      float h = 0.f;
-      if (t < n) {
-        const float g = s0 * rs[t];
-        const float u = s1 * rs[t];
-        h = g / (1.f + expf(-g)) * u;
-      }
-      gp.act_out[act_index(t, f)] = __float2half_rn(h);
     }
   }
 }
@@ -797,12 +830,14 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   }
   mk_sync();
   MK_CSTAMP(p, dtr, 8 * st + 1);
-  if (MODE != MODE_RESID && warp == MK_WARPS - 1 && lane < 16) {
-    float sum = 0.f;
-    for (int r = 0; r < HRB; ++r) sum += sSs[r * 16 + lane];
-    sRs[lane] = 1.f / sqrtf(sum / (float)H + EPS);
-  }
-  if (!down && FMT != VP_FMT_F16 && warp < H / GS) {
+  // The group sums (ones-matrix MMA, one warp per K group) are handed to the tile loops through
+  // an mbarrier rather than a CTA barrier, and the RMSNorm scale (read by the epilogue, after the
+  // CTA barrier that ends the jobs) is formed meanwhile: neither waits for the other. The lm_head
+  // folds the scale into its running argmax inside the jobs, so it keeps a CTA barrier.
+  constexpr bool kGsums = !DOWN && FMT != VP_FMT_F16;
+  if (MODE != MODE_RESID && warp == MK_WARPS - 1 && lane < 16)
+    sRs[lane] = rms_inv([&](int r) { return sSs[r * 16 + lane]; });
+  if (kGsums && warp < H / GS) {
     const uint32_t ONE2 = 0x3C003C00u;
     constexpr int NH = fmt_halves(FMT) ? 2 : 1;  // q8g32: one sum per 32-column half
     float xs[NH][2][4] = {};
@@ -823,19 +858,37 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
         xo[8 + 2 * tid4 + 1] = xs[h][1][1];
       }
     }
+    __syncwarp();
+    if (lane == 0 && MODE != MODE_ARGMAX)
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(rg.gsum)) : "memory");
   }
-  mk_sync();
+  if constexpr (MODE == MODE_ARGMAX) mk_sync();
   MK_CSTAMP(p, dtr, 8 * st + 2);
 
   const int npieces = (nrb * ng + tp - 1) / tp;
   MkJobs J;
   J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.actg = gp.act;
+  float* const sJobPart = sPart + (MODE == MODE_QKV || MODE == MODE_SILU ? MK_SS_SLOTS * 256 : 0);
+  J.part = sJobPart;
+  J.gsum = (kGsums && MODE != MODE_ARGMAX) ? rg.gsum : nullptr;
+  J.gs_parity = rg.gs_phase & 1u;
   J.trace = (gp.layer == MK_TRACE_LAYER && MODE != MODE_ARGMAX) ? p.trace : nullptr;
   constexpr int KIND = DOWN ? JOB_DOWN : MODE == MODE_ARGMAX ? JOB_ARGMAX : JOB_SMEM;
+#ifdef VP_TRACE_TWICE
+  // performance experiment: the QKV jobs once more on the same data (idempotent: one piece per
+  // CTA, nothing released inside), to time a warm second run
+  if (MODE == MODE_QKV) {
+    (void)mk_jobs<FMT, KIND>(J, rg, smem);
+    MK_CSTAMP(p, dtr, 8 * st + 6);
+    mk_sync();
+    MK_CSTAMP(p, dtr, 8 * st + 7);
+  }
+#endif
   const int2 rs2 = mk_jobs<FMT, KIND>(J, rg, smem);
   bool ok = rs2.x >= 0;
   if (ok) rg.released = rs2.x;
   rg.waited = rs2.y;
+  if (kGsums && MODE != MODE_ARGMAX) ++rg.gs_phase;
   MK_CSTAMP(p, dtr, 8 * st + 3);
   // this warp is done with every piece of the stage
   if (ok) ok = mk_release(rg, piece0 + npieces, lane);
@@ -846,7 +899,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   mk_sync();
   MK_CSTAMP(p, dtr, 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
-  if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE>(gp, rb0, nrb, P, sPart, sRs, sEpc);
+  if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE>(gp, rb0, nrb, P, sJobPart, sRs, sEpc);
   MK_CSTAMP(p, dtr, 8 * st + 5);
   return true;
 }
@@ -867,6 +920,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, MK_WARPS);
     }
+    mbar_init(reinterpret_cast<uint64_t*>(smem + MK_OFF_GS), H / GS);
     fence_barrier_init();
     sAbort = 0;
   }
@@ -929,6 +983,8 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     rg.empty = empty;
     rg.released = 0;
     rg.waited = 0;
+    rg.gsum = reinterpret_cast<uint64_t*>(smem + MK_OFF_GS);
+    rg.gs_phase = 0;
     int piece0 = 0;
     auto pieces = [&](int st) {
       int rb0, nrb;

@@ -99,15 +99,7 @@ __device__ void sk_load_act(const SketchParams& p, uint8_t* sAct, float* sRs) {
   const uint4* src = reinterpret_cast<const uint4*>(p.act);
   uint4* dst = reinterpret_cast<uint4*>(sAct);
   for (int i = threadIdx.x; i < SK_NG * 2048 / 16; i += blockDim.x) dst[i] = __ldcg(src + i);
-  if (threadIdx.x < 16) {
-    float v[HRB];
-#pragma unroll
-    for (int r = 0; r < HRB; ++r) v[r] = __ldcg(p.ss + r * 16 + threadIdx.x);
-    float sum = 0.f;
-#pragma unroll
-    for (int r = 0; r < HRB; ++r) sum += v[r];
-    sRs[threadIdx.x] = 1.f / sqrtf(sum / (float)H + EPS);
-  }
+  if (threadIdx.x < 16) sRs[threadIdx.x] = rms_inv([&](int r) { return __ldcg(p.ss + r * 16 + threadIdx.x); });
 }
 
 // Stage 1. NT = 1 when rows <= 8 (one n8 half of the MMA), else 2. Each warp takes whole 32-row
