@@ -633,7 +633,7 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
       }
     }
     return;
-  }
+  } else {  // QKV, O, down: one 16-row block (128 elements) per CTA
   for (int e = threadIdx.x; e < nrb * 128; e += MK_CONS) {
     const int i = e >> 7, lt = e & 127, t = lt >> 3, rp = lt & 7, rb = rb0 + i;
     float s0 = 0.f, s1 = 0.f;
@@ -718,6 +718,7 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
         if (rp == 0) gp.ss_out[rb * 16 + t] = sq;
       }
     }
+  }
   }
 }
 

@@ -188,6 +188,44 @@ def full_q4():
     eng.close()
 
 
+def _check_head_partials(eng, rows):
+    """The pass's lm_head stage (per CTA: the largest logit of its vocabulary rows and the lowest
+    id holding it, per token) against the stand-alone head's full logits on the same rows: equal
+    bit for bit. The two are separate kernels with their own work split; the tokens the commit
+    takes, the no-alloc head and the sketch head all rely on their arithmetic being the same."""
+    pval, pidx = (a.cpu().numpy() for a in eng.argmax_partials())
+    gl = eng.logits().cpu().numpy()
+    G = pval.shape[1]
+    nrb = gl.shape[1] // 16
+    for cta in range(G):
+        rb0, rb1 = cta * nrb // G, (cta + 1) * nrb // G
+        seg = gl[:rows, 16 * rb0:16 * rb1]
+        best = seg.max(axis=1)
+        ids = seg.argmax(axis=1) + 16 * rb0  # first maximum = lowest id
+        assert np.array_equal(best.view(np.uint32), pval[:rows, cta].view(np.uint32)), (cta, best, pval[:rows, cta])
+        assert np.array_equal(ids, pidx[:rows, cta]), (cta, ids, pidx[:rows, cta])
+
+
+def test_pass_lm_head_equals_standalone_head(small):
+    fmt, w, m, eng = small
+    prompt = (synth.make_prompt(29, seed=11) % VOCAB_SMALL).tolist()
+    eng.begin(0, 32)
+    eng.prefill(prompt)
+    first = eng.tokens(1)[0]
+    eng.verify(synth.seeded_tree(np.random.default_rng(5), [first] * 9, n=16, vocab=VOCAB_SMALL))
+    _check_head_partials(eng, 16)
+
+
+def test_pass_lm_head_equals_standalone_head_full_vocab(full_q4):
+    w, eng = full_q4
+    prompt = synth.make_prompt(64, seed=77).tolist()
+    eng.begin(0, 32)
+    eng.prefill(prompt)
+    first = eng.tokens(1)[0]
+    eng.verify(synth.seeded_tree(np.random.default_rng(6), [first] * 9, n=16))
+    _check_head_partials(eng, 16)
+
+
 def _tree_fn(y_seq, rng, n=16, p=0.6):
     def fn(out):
         y = list(y_seq[len(out):len(out) + 9])
