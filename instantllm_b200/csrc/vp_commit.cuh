@@ -21,8 +21,11 @@ struct CommitParams {
 //  3. Commit g along the path to out_tokens, stopping at EOS or max_steps (:326-333).
 //  4. pos += m + 1 (verify) or += prompt length (prefill, :335-338).
 //  5. KV compaction: accepted row path[k-1] moves from slot pos0+path[k-1] to pos0+k in every
-//     layer; it was already rotated for position pos0+k (its depth is k). Copies run in k order,
-//     which is safe because path rows strictly increase (:351-365).
+//     layer; it was already rotated for position pos0+k (its depth is k) (:351-365). The moves
+//     go in batches of four k: a batch reads all its sources before writing its destinations, and
+//     its destinations (pos0+k, k <= the batch's last) lie below every later batch's sources
+//     (pos0+path[k'-1] >= pos0+k', since path rows strictly increase), so no read sees a moved row.
+//     Each thread keeps the same 16-byte words in every batch, so batches need no barrier.
 __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx, int nparts) {
   vp_state* st = s.st;
   const RowInfo* ri = s.ri;
@@ -31,8 +34,11 @@ __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx
   const int nwarps = nthr >> 5;
   __shared__ int g[ROWS];
   __shared__ int path[ROWS];
+  __shared__ int sTree[VP_TREE_INTS];
   __shared__ int sNpath, sPos0;
   const int nv = st->nver, r0 = st->vrow0;
+  // the tree buffer comes in with the partials, so the walk below reads shared memory only
+  if (tid < VP_TREE_INTS) sTree[tid] = __ldcg(s.tree + tid);
   // one warp per row: argmax over the partials, lowest id on ties
   for (int t = warp; t < nv; t += nwarps) {
     const float* pv = pval + (size_t)(r0 + t) * nparts;
@@ -61,7 +67,7 @@ __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx
       for (;;) {
         int c = -1;
         for (int i = 1; i < nv; ++i)
-          if (s.tree[VP_TR_PARENT + i] == cur && s.tree[VP_TR_TOK + i] == g[cur]) { c = i; break; }
+          if (sTree[VP_TR_PARENT + i] == cur && sTree[VP_TR_TOK + i] == g[cur]) { c = i; break; }
         if (c < 0) break;
         path[m++] = c;
         cur = c;
@@ -91,21 +97,24 @@ __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx
   }
   cons_sync();
   const int np = sNpath, pos0 = sPos0;
-  for (int k = 1; k <= np; ++k) {
-    const int src = pos0 + path[k - 1], dst = pos0 + k;
-    if (src != dst) {
-      // 2 caches x layers x 2 KV heads x 64 halves, moved as 16-byte words (8 per row).
-      const int words = 2 * s.n_layers * NKV * (HD / 8);
-      for (int w = tid; w < words; w += nthr) {
-        const int cache = w / (s.n_layers * NKV * 8);
-        const int rem = w % (s.n_layers * NKV * 8);
-        const int lh = rem / 8, part = rem % 8;
-        __half* base = (cache ? s.vc : s.kc) + (size_t)lh * s.max_ctx * HD;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(base + (size_t)src * HD + part * 8));
-        *reinterpret_cast<uint4*>(base + (size_t)dst * HD + part * 8) = v;
-      }
+  // 2 caches x layers x 2 KV heads x 64 halves, moved as 16-byte words (8 per row)
+  const int words = 2 * s.n_layers * NKV * (HD / 8);
+  for (int k0 = 1; k0 <= np; k0 += 4) {
+    const int kn = min(4, np - k0 + 1);
+    for (int w = tid; w < words; w += nthr) {
+      const int cache = w / (s.n_layers * NKV * 8);
+      const int rem = w % (s.n_layers * NKV * 8);
+      const int lh = rem / 8, part = rem % 8;
+      __half* base = (cache ? s.vc : s.kc) + (size_t)lh * s.max_ctx * HD + part * 8;
+      uint4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < kn) v[j] = __ldcg(reinterpret_cast<const uint4*>(base + (size_t)(pos0 + path[k0 + j - 1]) * HD));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < kn && path[k0 + j - 1] != k0 + j)
+          *reinterpret_cast<uint4*>(base + (size_t)(pos0 + k0 + j) * HD) = v[j];
     }
-    cons_sync();
   }
 }
 
