@@ -6,9 +6,9 @@ n-gram, word and association lookups (:416-429).
 Sections stay as the file stores them: sorted 64-bit keys searched by bisection, with parallel value
 arrays and (first, n) ranges into flat arrays. That is the layout a drafter kernel reads from device
 memory as well (one binary search per lookup, no hash maps). This module covers the table, the
-lookups, the request's nearest training documents (the TF-IDF part of Drafter.begin) and the
-scorer over given feature rows, and the best-first tree over a given probability function; the
-candidate features (ildraft.py:520-692) are not built.
+lookups and the request's nearest training documents (the TF-IDF part of Drafter.begin, which the
+host runs at request start); the candidate features, the scorer and the best-first tree run on
+the GPU (csrc/vp_draft.cuh), and their CPU restatement is the checker in oracle/drafter.py.
 """
 from __future__ import annotations
 
@@ -55,34 +55,6 @@ def prompt_words(text: str) -> list:
 
 
 STOPS = (151645, 151643)
-
-
-def best_first_tree(probs, B: int, branch: int = 8, stops=STOPS) -> tuple:
-    """The draft tree of B nodes grown best first (ildraft.py:724-747): every candidate of a node
-    (the top `branch` of probs(path), path = the tokens from the root to that node) waits in a
-    priority queue keyed by its path probability, the product of the probabilities along the path;
-    the most probable waiting candidate becomes the next node (equal keys: the one queued first),
-    and its own candidates are queued unless it is a stop token. Returns (parents, tokens): node i
-    hangs under node parents[i] (-1: the root, the last accepted token), so parents[i] < i."""
-    import heapq
-
-    parents, tokens, path = [], [], {-1: []}
-    queue, seq = [], 0
-    for tok, p in probs([])[:branch]:
-        heapq.heappush(queue, (-p, seq, -1, tok))
-        seq += 1
-    while queue and len(tokens) < B:
-        key, _, par, tok = heapq.heappop(queue)
-        node = len(tokens)
-        parents.append(par)
-        tokens.append(tok)
-        path[node] = path[par] + [tok]
-        if tok in stops or len(tokens) >= B:
-            continue
-        for tok2, p2 in probs(path[node])[:branch]:
-            heapq.heappush(queue, (key * p2, seq, node, tok2))
-            seq += 1
-    return parents, tokens
 
 
 # section tag -> numpy dtype of one record
@@ -195,23 +167,6 @@ class DraftTable:
         s = [(float(sc[j]) / (qn * float(norms[j])), int(j)) for j in docs]
         s.sort(key=lambda x: (-x[0], x[1]))
         return s[:knb]
-
-    def probs(self, tokens, rows) -> list:
-        """The scorer over candidate feature rows (ildraft.py:694-708): score = W2 . relu(W1 x + b1)
-        + b2 + WL . x in float64, a softmax that also counts a null option of score 0, and the
-        candidates as [(token, p)] by p descending, then token ascending."""
-        if len(tokens) == 0:
-            return []
-        m = self.mlp()
-        X = np.asarray(rows, dtype=np.float64)
-        W1, b1 = m["W1"].astype(np.float64), m["b1"].astype(np.float64)
-        W2, WL = m["W2"].astype(np.float64), m["WL"].astype(np.float64)
-        s = np.maximum(X @ W1.T + b1, 0.0) @ W2 + float(m["b2"]) + X @ WL
-        top = max(float(s.max()), 0.0)
-        e = np.exp(s - top)
-        ps = e / (float(e.sum()) + float(np.exp(-top)))
-        order = sorted(range(len(tokens)), key=lambda i: (-ps[i], int(tokens[i])))
-        return [(int(tokens[i]), float(ps[i])) for i in order]
 
     def seq(self, doc: int) -> list:
         """Training output `doc` (generated ids and the stop token if it stopped)."""

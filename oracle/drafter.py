@@ -92,6 +92,16 @@ def softmax_null(s) -> np.ndarray:
     return e / (float(e.sum()) + math.exp(-m))
 
 
+def probs_of_rows(ot: OracleTable, tokens, rows) -> list:
+    """The scorer over given candidate feature rows (ildraft.py:694-708): [(token, p)] by p
+    descending, then token ascending."""
+    if len(tokens) == 0:
+        return []
+    ps = softmax_null(score(ot, rows))
+    order = sorted(range(len(tokens)), key=lambda i: (-ps[i], int(tokens[i])))
+    return [(int(tokens[i]), float(ps[i])) for i in order]
+
+
 class Request:
     """The drafter's state of one request (ildraft.py Drafter, tokenizer absent)."""
 

