@@ -51,13 +51,15 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "batch2", "config3", "config4", "config5", "sketch_head"],
+    ap.add_argument("--workload", choices=["config2", "batch2", "config3", "config4", "config5",
+                                           "sketch_head", "decode_loop"],
                     default="config2",
                     help="batch2: two config-2 requests per launch (vp_pass_multi), aggregate tok/s (1 GPU); "
                          "config3 / config4: the q8 8-row chain and f16 16-row tree workloads (1 GPU, "
                          "their own line); config5: BASELINE config 5, independent requests sharded "
                          "over the ranks; sketch_head: the optional two-stage lm_head against the full "
-                         "one (1 GPU)")
+                         "one (1 GPU); decode_loop: the device-resident loop with the learned drafter "
+                         "(1 GPU)")
     ap.add_argument("--requests", type=int, default=256, help="config5: number of requests")
     ap.add_argument("--c5-requests", type=int, default=64,
                     help="requests of the config-5 sub-object of the default line (0: skip it)")
@@ -594,6 +596,95 @@ def run_batch2(args):
         e.close()
 
 
+def run_decode_loop(args):
+    """The device-resident decode loop (VerifyEngine.generate_drafted): one request with a
+    256-token prompt decoded 64 tokens, every step k_draft (the learned drafter on the device, on
+    the committed table subset tests/golden/draft_subset.ildraft) + one verify pass, enqueued one
+    step ahead, the shape from the adaptive rule. Against it: the same request by plain greedy
+    decoding (1-row passes) and by the loop with fixed trees; and k_draft alone. The weights are
+    random-init, so the drafter's candidates (trained on real text) are rarely accepted: the line
+    measures the loop's overhead, not a speed-up. One JSON line of its own, 1 GPU."""
+    import os
+
+    import torch
+
+    from instantllm_b200 import synth
+    from instantllm_b200.drafter import DeviceDrafter
+    from instantllm_b200.engine import PassShape, VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
+    eng = VerifyEngine(w, max_ctx=4096, max_steps=4096, device=0)
+    d = DeviceDrafter(os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden",
+                                   "draft_subset.ildraft"))
+    s = eng.stream
+    prompt = synth.make_prompt(PREFIX, seed=args.seed + 7).tolist()
+    n_new = 64
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        outs = []
+        e0.record(s)
+        for _ in range(args.steps):
+            outs.append(fn())
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps, outs[-1]
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.mark_start()
+    ms_loop, r = timed(lambda: eng.generate_drafted(prompt, n_new, d, pids=prompt, text="", depth=1))
+    clk = clocks.stop()
+    ms_tree, rt = timed(lambda: eng.generate_drafted(prompt, n_new, d, pids=prompt, text="", depth=1,
+                                                     shape=PassShape(adaptive=False)))
+    ms_greedy, g = timed(lambda: eng.generate(prompt, n_new))
+    # k_draft alone, after the request's last committed token (device state as the loop left it)
+    tree_ptr = eng.buffer(7, (synth.TREE_INTS,), "<i4").data_ptr()
+    st_ptr, tok_ptr = eng.lib.vp_device_state(eng.ctx), eng.lib.vp_device_tokens(eng.ctx)
+    n_tok = len(r["tokens"])
+    draft_us = {}
+    for B, br in ((15, 8), (7, 1)):
+        def draft():
+            d.draft(tree_ptr, tok_ptr, n_out=n_tok, B=B, branch=br, stream=eng._s)
+        for _ in range(3):
+            draft()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(20):
+            draft()
+        e1.record(s)
+        torch.cuda.synchronize()
+        draft_us[f"B{B}_branch{br}"] = 1000 * e0.elapsed_time(e1) / 20
+    ntok = len(r["tokens"])
+    line = {
+        "metric": "device-resident decode loop (k_draft + verify pass per step, one step enqueued ahead): "
+                  "tok/s of one request, prefill included",
+        "value": ntok / (ms_loop * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True,
+        "ms_per_request": ms_loop, "tokens": ntok, "passes": r["passes"],
+        "accepted_per_pass": r["state"]["accepted"] / max(1, r["passes"]),
+        "shapes": {f"B{b}_branch{br}": r["shapes"].count((b, br)) for b, br in sorted(set(r["shapes"]))},
+        "host_waits": r["host_waits"],
+        "fixed_tree_loop_tok_s": len(rt["tokens"]) / (ms_tree * 1e-3),
+        "greedy_tok_s": len(g["tokens"]) / (ms_greedy * 1e-3),
+        "tokens_equal_greedy": r["tokens"] == g["tokens"] == rt["tokens"],
+        "k_draft_us": draft_us,
+        "dtype": "q4 weights, fp16 activations, fp32 accumulate; drafter float64",
+        "data": "synthetic (seeded random-init q4 weights, uniform prompt ids); drafter table: the committed "
+                "subset of the reference's table",
+        "config": {"workload": f"one request, {PREFIX}-token prompt, {n_new} new tokens, learned drafter on "
+                               "the device, adaptive tree / chain", "layers": args.layers},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    d.close()
+    eng.close()
+
+
 def run_cfg34(args, which: str):
     """BASELINE config 3 (q8 group-64 weights, 1024-token cached prefix, 8-row chain passes whose
     draft i equals the true next token with p = 0.5, 64 tokens) or config 4 (f16 weights, a
@@ -813,6 +904,9 @@ def main():
         return
     if args.workload == "batch2":
         run_batch2(args)
+        return
+    if args.workload == "decode_loop":
+        run_decode_loop(args)
         return
     if args.workload == "config5":
         main_config5(args, rank, world)

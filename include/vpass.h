@@ -217,7 +217,8 @@ int vp_debug_logits(vp_ctx* ctx, float* d_out, void* stream);
  * 3 KV cache V (half [layers][2][max_ctx][64]), 4 argmax partial values fp32 [16][parts],
  * 5 argmax partial ids int32 [16][parts] (parts = CTAs of the pass kernel), 6 stage trace of the
  * last launch: uint64 [256] %globaltimer ns (start, after embed, after each of the 5 stages of
- * every layer, after the lm_head, end). */
+ * every layer, after the lm_head, end), 7 the context's tree buffer (int32[VP_TREE_INTS]: a
+ * drafter that writes it directly saves vp_pass its tree copy). */
 int vp_buffer(vp_ctx* ctx, int32_t which, void** ptr, size_t* bytes);
 
 /* ---- greedy lm-head argmax that allocates nothing ----

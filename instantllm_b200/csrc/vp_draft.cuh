@@ -69,6 +69,8 @@ struct DraftReq {
   const int32_t* nb_pos;                 // index after the n-gram's first occurrence with a next token
   const int32_t* as_tok; const double* as_max; const int32_t* as_cnt; int nas;  // association map
   const int32_t* as_cand; int nascand;   // association candidates (sorted)
+  const float* copy_prop;                // per copy id: its copy propensity (k_draft stages it), or null
+  const double* copy_logit;              // and its feature log(p / (1 - p)) / 4, or null
 };
 
 struct DraftOut {
@@ -98,10 +100,35 @@ __device__ __forceinline__ uint32_t dr_rtok(const DrRate& x) { return x.tok; }
 __device__ __forceinline__ unsigned long long dr_r2key(const DrRate2& x) { return x.key; }
 __device__ __forceinline__ int dr_i32(const int32_t& x) { return x; }
 
+// Staging caps: the committed output, the prompt and the distinct prompt ids (with their copy
+// propensities) are copied into shared memory once per launch when they fit, so the per-context
+// scans and searches run on shared memory; longer requests read them from global memory.
+constexpr int DR_OUT_CAP = 2048;
+constexpr int DR_PROMPT_CAP = 2048;
+constexpr int DR_COPY_CAP = 2048;
+constexpr int DR_AS_CAP = 1024;           // association map and candidates
+constexpr int DR_SMALL = 96;   // (token, bits) of the small sources: n-gram lists, self, first prompt match, votes
+
 struct DrShared {
   uint32_t used[DR_WORDS];                 // bitset of the committed output's tokens
-  unsigned long long cand[DR_MAX_CAND];    // (token << 32) | source bits, sorted and merged
+  uint32_t mark[DR_WORDS];                 // candidate tokens of the current context
+  uint32_t prm[DR_WORDS];                  // tokens after a longest prompt match (source DS_PR)
+  int ctok[DR_MAX_CAND];                   // the context's distinct candidates, ascending
+  uint32_t cbits[DR_MAX_CAND];             // their source bits
   double prob[DR_MAX_CAND];
+  unsigned long long small[DR_SMALL];      // (token << 32) | bits of the small sources
+  int nsmall;
+  int outs[DR_OUT_CAP];                    // staged copies (see the caps above)
+  int prs[DR_PROMPT_CAP];
+  int cps[DR_COPY_CAP];
+  float cpp[DR_COPY_CAP];                  // copy propensity (NaN: not in the table)
+  double cplg[DR_COPY_CAP];                // its feature, log(p / (1 - p)) / 4
+  int ast[DR_AS_CAP], ascn[DR_AS_CAP], asc[DR_AS_CAP];
+  double asmx[DR_AS_CAP];
+  double nbs[DR_MAX_NB];
+  double mlpd[DR_H_MAX * DR_F + 2 * DR_H_MAX + 1 + DR_F];  // W1, b1, W2, b2, WL as float64
+  DrPair ngtop[DR_N_MAX + 1][8];           // the context's n-gram next-token lists
+  int nbhit[DR_MAX_NB][DR_MAXM_MAX + 1];   // per document and suffix length: next token or -1
   unsigned long long hsh[DR_MAXM_MAX + 1]; // key of the context's last n tokens
   int dist_tot[DR_N_MAX + 1], dist_first[DR_N_MAX + 1], dist_n[DR_N_MAX + 1];
   int long_n, supp3, supp10, top_long, ent_low;
@@ -111,11 +138,30 @@ struct DrShared {
   double red_d[DR_THREADS / 32];
   int self_n, self_tok, pr_n, pr_first_e, first_unused, ticks0, capped;
   double c1, c2;
+  unsigned long long wtop_k[DR_THREADS / 32][8];  // per-warp top 8 (key, candidate index)
+  int wtop_i[DR_THREADS / 32][8];
   // best-first queue and the tree
   double hk[DR_HEAP]; int hseq[DR_HEAP], hpar[DR_HEAP], htok[DR_HEAP], hn, hctr;
   int npar[16], ntok[16], nodes, cur, go;
   int top_tok[8]; double top_p[8];
+#ifdef VP_DRAFT_TRACE
+  unsigned long long tacc[32], tlast;  // per-phase time summed over the expansions (thread 0)
+#endif
 };
+
+#ifdef VP_DRAFT_TRACE
+__device__ unsigned long long g_dr_trace[32];
+#define DR_T(sh, k)                                       \
+  do {                                                    \
+    if (threadIdx.x == 0) {                               \
+      const unsigned long long t_ = globaltimer();        \
+      (sh).tacc[k] += t_ - (sh).tlast;                    \
+      (sh).tlast = t_;                                    \
+    }                                                     \
+  } while (0)
+#else
+#define DR_T(sh, k) do { } while (0)
+#endif
 
 // source bits of a candidate
 constexpr uint32_t DS_NG = 1, DS_SELF = 2, DS_PR = 4, DS_PRFIRST = 8, DS_NB = 16, DS_COPY = 32, DS_ASC = 64;
@@ -129,10 +175,32 @@ struct DrCtx {  // the context being expanded: TAIL + out0 + path
   __device__ __forceinline__ int L() const { return 5 + lo(); }
 };
 
+// Warp reductions through redux.sync (one instruction per 32-bit word) instead of shuffle trees.
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+  const unsigned hi = (unsigned)(v >> 32);
+  const unsigned mhi = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (unsigned)v : 0u);
+  return ((unsigned long long)mhi << 32) | mlo;
+}
+// The lane holding the largest key (ties: the lowest idx; idx -1 = none, and key 0 marks an empty
+// lane): key and idx of the winner in every lane.
+__device__ __forceinline__ void warp_argmax(unsigned long long& key, int& idx) {
+  const unsigned long long m = warp_max_u64(key);
+  idx = (int)__reduce_min_sync(0xffffffffu, key == m ? (unsigned)idx : 0xffffffffu);
+  key = m;
+}
+// Doubles as unsigned integers of the same order (for max / min through integer reductions).
+__device__ __forceinline__ unsigned long long dr_ord(double d) {
+  const unsigned long long u = (unsigned long long)__double_as_longlong(d);
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+__device__ __forceinline__ double dr_unord(unsigned long long u) {
+  return __longlong_as_double((long long)((u >> 63) ? (u & 0x7fffffffffffffffull) : ~u));
+}
+
 // Block reductions (256 threads) with a fixed combination order.
 __device__ __forceinline__ int dr_max_i(int v, DrShared& sh) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  v = __reduce_max_sync(0xffffffffu, v);
   if ((threadIdx.x & 31) == 0) sh.red_i[threadIdx.x >> 5] = v;
   __syncthreads();
   int r = sh.red_i[0];
@@ -142,9 +210,8 @@ __device__ __forceinline__ int dr_max_i(int v, DrShared& sh) {
 }
 __device__ __forceinline__ int dr_min_i(int v, DrShared& sh) { return -dr_max_i(-v, sh); }
 __device__ __forceinline__ double dr_max_d(double v, DrShared& sh) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if ((threadIdx.x & 31) == 0) sh.red_d[threadIdx.x >> 5] = v;
+  const unsigned long long u = warp_max_u64(dr_ord(v));
+  if ((threadIdx.x & 31) == 0) sh.red_d[threadIdx.x >> 5] = dr_unord(u);
   __syncthreads();
   double r = sh.red_d[0];
   for (int w = 1; w < DR_THREADS / 32; ++w) r = fmax(r, sh.red_d[w]);
@@ -175,6 +242,34 @@ __device__ __forceinline__ double dr_prop(const DraftTab& T, int tok, double dfl
   const int i = dr_find(T.prop, T.n_prop, (uint32_t)tok, dr_rtok);
   return i >= 0 ? (double)T.prop[i].v : dflt;
 }
+// Copy propensity (default 0.2) of the copy id at index i of R.copy: from the staged per-id table
+// when there is one (NaN there: not in the table).
+__device__ __forceinline__ double dr_copy_prop(const DraftTab& T, const DraftReq& R, int i, int tok) {
+  if (R.copy_prop) {
+    const float v = R.copy_prop[i];
+    return v == v ? (double)v : 0.2;
+  }
+  return dr_prop(T, tok, 0.2);
+}
+// Copy propensity of a prompt id.
+__device__ __forceinline__ double dr_prompt_prop(const DraftTab& T, const DraftReq& R, int tok) {
+  if (R.copy_prop) {
+    const int i = dr_find(R.copy, R.ncopy, tok, dr_i32);
+    if (i >= 0) return dr_copy_prop(T, R, i, tok);
+  }
+  return dr_prop(T, tok, 0.2);
+}
+// A candidate token: marked in the context's set (duplicates merge for free).
+__device__ __forceinline__ void dr_mark(DrShared& sh, int tok) {
+  if (tok >= 0 && tok < DR_VOCAB) atomicOr(&sh.mark[tok >> 5], 1u << (tok & 31));
+}
+// A candidate from a small source, whose bits are merged after the compaction.
+__device__ __forceinline__ void dr_push_small(DrShared& sh, int tok, uint32_t bits) {
+  if (tok < 0 || tok >= DR_VOCAB) return;
+  dr_mark(sh, tok);
+  const int k = atomicAdd(&sh.nsmall, 1);
+  if (k < DR_SMALL) sh.small[k] = ((unsigned long long)(uint32_t)tok << 32) | bits;
+}
 
 // Longest common suffix of seq[0..e) and the output (both end-aligned), at most cap.
 template <typename Seq>
@@ -187,10 +282,16 @@ __device__ __forceinline__ int dr_suffix(const Seq& s, int e, const DrCtx& c, in
 
 // Candidates and probabilities of the next token after the context; leaves the top 8 (probability
 // descending, token ascending) in sh.top_tok / top_p (-1: fewer candidates).
+//
+// The candidate set is a bitset over the vocabulary (duplicates from several sources merge by
+// themselves), compacted in ascending token order by a block scan; the source bits of the large
+// sources (prompt matches, copy ids, association candidates) are set membership tests, those of the
+// small ones (n-gram lists, self match, first prompt match, votes) are merged after the compaction.
 __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, DrShared& sh) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int L = c.L(), lo = c.lo();
   const int nmax = max(T.N, T.MAXM);
+  DR_T(sh, 0);
   // keys of the context's last n tokens: FNV-1a 64 over the order byte, then the tokens (u32 LE)
   if (tid >= 1 && tid <= nmax && tid <= L) {
     unsigned long long h = 0xcbf29ce484222325ull;
@@ -202,27 +303,47 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     }
     sh.hsh[tid] = h;
   }
-  if (tid == 0) { sh.ncand = 0; sh.self_n = 0; sh.pr_n = 0; }
+  if (tid == 0) { sh.self_n = 0; sh.pr_n = 0; sh.nsmall = 0; }
   __syncthreads();
-  // n-gram distributions of orders 1..min(N, L)
-  if (tid >= 1 && tid <= T.N) {
-    int tot = -1, first = 0, n = 0;
-    if (tid <= L) {
-      const int i = dr_find(T.ngky, T.n_ng, sh.hsh[tid], dr_u64);
-      if (i >= 0) { tot = (int)T.ngvl[i].a; first = (int)(T.ngvl[i].b >> 3); n = (int)(T.ngvl[i].b & 7u); }
+  DR_T(sh, 1);
+  // the table searches, one work item each: n-gram distributions of orders 1..N (their next-token
+  // lists staged), the copy rates after the last token and after the last pair, and every
+  // (neighbour document, suffix length) key
+  const int mm = min(T.MAXM, L);
+  const int n_items = T.N + 2 + R.nnb * mm;
+  for (int w = tid; w < n_items; w += DR_THREADS) {
+    if (w < T.N) {
+      const int n = w + 1;
+      int tot = -1, first = 0, cnt = 0;
+      if (n <= L) {
+        const int i = dr_find(T.ngky, T.n_ng, sh.hsh[n], dr_u64);
+        if (i >= 0) { tot = (int)T.ngvl[i].a; first = (int)(T.ngvl[i].b >> 3); cnt = (int)(T.ngvl[i].b & 7u); }
+      }
+      sh.dist_tot[n] = tot; sh.dist_first[n] = first; sh.dist_n[n] = cnt;
+      for (int i = 0; i < cnt; ++i) sh.ngtop[n][i] = T.ngnx[first + i];
+    } else if (w == T.N) {
+      const int i1 = dr_find(T.cc1, T.n_cc1, (uint32_t)c.ctx(L - 1), dr_rtok);
+      sh.c1 = i1 >= 0 ? (double)T.cc1[i1].v : 0.1;
+    } else if (w == T.N + 1) {
+      const unsigned long long k2 = ((unsigned long long)(uint32_t)c.ctx(L - 2) << 32) | (uint32_t)c.ctx(L - 1);
+      const int i2 = dr_find(T.cc2, T.n_cc2, k2, dr_r2key);
+      sh.c2 = i2 >= 0 ? (double)T.cc2[i2].v : 0.1;
+    } else {
+      const int r = (w - T.N - 2) / mm, n = 1 + (w - T.N - 2) % mm;
+      const int k0 = R.nb_key_off[r], k1 = R.nb_key_off[r + 1];
+      const int i = dr_find(R.nb_keys + k0, k1 - k0, sh.hsh[n], dr_u64);
+      sh.nbhit[r][n] = i >= 0 ? R.nb_seq[R.nb_seq_off[r] + R.nb_pos[k0 + i]] : -1;
     }
-    sh.dist_tot[tid] = tot; sh.dist_first[tid] = first; sh.dist_n[tid] = n;
   }
-  // neighbours: the longest context suffix in each document's index gives its vote
+  __syncthreads();
+  // each neighbour's vote: the next token after the longest context suffix found in it
   if (tid < R.nnb) {
     int tok = -1, got = 0;
-    const int k0 = R.nb_key_off[tid], k1 = R.nb_key_off[tid + 1];
-    for (int n = min(T.MAXM, L); n >= 1 && tok < 0; --n) {
-      const int i = dr_find(R.nb_keys + k0, k1 - k0, sh.hsh[n], dr_u64);
-      if (i >= 0) { tok = R.nb_seq[R.nb_seq_off[tid] + R.nb_pos[k0 + i]]; got = n; }
-    }
+    for (int n = mm; n >= 1; --n)
+      if (sh.nbhit[tid][n] >= 0) { tok = sh.nbhit[tid][n]; got = n; break; }
     sh.vote_tok[tid] = tok; sh.vote_n[tid] = got;
   }
+  DR_T(sh, 2);
   // self lookup: the longest suffix of the output found earlier in it (k(e) for next index e), the
   // latest such occurrence
   int best = 0;
@@ -236,6 +357,7 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     const int e = dr_max_i(last, sh);
     if (tid == 0) { sh.self_n = self_n; sh.self_tok = c.out(e); }
   }
+  DR_T(sh, 3);
   // prompt lookup: every occurrence of the longest suffix of the output found in the prompt
   best = 0;
   const int capp = min(T.MAXM, lo);
@@ -243,19 +365,22 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     best = max(best, dr_suffix([&](int i) { return R.P[i]; }, e, c, capp));
   const int pr_n = dr_max_i(best, sh);
   if (tid == 0) sh.pr_n = pr_n;
-  __syncthreads();
-  // the candidate list: (token << 32) | source bits, merged after sorting
-  auto push = [&](int tok, uint32_t bits) {
-    const int k = atomicAdd(&sh.ncand, 1);
-    if (k < DR_MAX_CAND) sh.cand[k] = ((unsigned long long)(uint32_t)tok << 32) | bits;
-  };
+  DR_T(sh, 4);
+  // the candidates
   if (pr_n > 0) {
     int first = 0x7fffffff;
     for (int e = 1 + tid; e <= R.np - 1; e += DR_THREADS)
-      if (dr_suffix([&](int i) { return R.P[i]; }, e, c, capp) >= pr_n) { push(R.P[e], DS_PR); first = min(first, e); }
+      if (dr_suffix([&](int i) { return R.P[i]; }, e, c, capp) >= pr_n) {
+        const int t = R.P[e];
+        if (t >= 0 && t < DR_VOCAB) atomicOr(&sh.prm[t >> 5], 1u << (t & 31));
+        dr_mark(sh, t);
+        first = min(first, e);
+      }
     first = dr_min_i(first, sh);
-    if (tid == 0) { sh.pr_first_e = first; push(R.P[first], DS_PRFIRST); }
+    if (tid == 0) { sh.pr_first_e = first; dr_push_small(sh, R.P[first], DS_PRFIRST); }
   }
+  if (tid >= 1 && tid <= T.N && sh.dist_tot[tid] >= 0)
+    for (int i = 0; i < sh.dist_n[tid]; ++i) dr_push_small(sh, (int)sh.ngtop[tid][i].a, DS_NG);
   if (tid == 0) {
     int ln = 0, s3 = 0, s10 = 0;
     for (int n = 1; n <= T.N; ++n)
@@ -267,8 +392,8 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     sh.long_n = ln; sh.supp3 = s3; sh.supp10 = s10;
     sh.top_long = -1; sh.ent_low = 0;
     if (ln) {
-      const DrPair* top = T.ngnx + sh.dist_first[ln];
-      sh.top_long = (int)top[0].a;
+      const DrPair* top = sh.ngtop[ln];
+      sh.top_long = sh.dist_n[ln] > 0 ? (int)top[0].a : -1;
       double ent = 0.0;
       const double tot = (double)sh.dist_tot[ln];
       for (int i = 0; i < sh.dist_n[ln]; ++i) {
@@ -277,59 +402,66 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
       }
       sh.ent_low = -ent < 0.3;
     }
-    for (int n = 1; n <= T.N; ++n)
-      if (sh.dist_tot[n] >= 0)
-        for (int i = 0; i < sh.dist_n[n]; ++i) push((int)T.ngnx[sh.dist_first[n] + i].a, DS_NG);
-    if (sh.self_n > 0) push(sh.self_tok, DS_SELF);
-    for (int r = 0; r < R.nnb; ++r)
-      if (sh.vote_tok[r] >= 0) push(sh.vote_tok[r], DS_NB);
-    const int t1 = c.ctx(L - 1), t2 = c.ctx(L - 2);
-    const int i1 = dr_find(T.cc1, T.n_cc1, (uint32_t)t1, dr_rtok);
-    sh.c1 = i1 >= 0 ? (double)T.cc1[i1].v : 0.1;
-    const int i2 = dr_find(T.cc2, T.n_cc2, ((unsigned long long)(uint32_t)t2 << 32) | (uint32_t)t1, dr_r2key);
-    sh.c2 = i2 >= 0 ? (double)T.cc2[i2].v : 0.1;
+    if (sh.self_n > 0) dr_push_small(sh, sh.self_tok, DS_SELF);
   }
+  if (tid < R.nnb && sh.vote_tok[tid] >= 0) dr_push_small(sh, sh.vote_tok[tid], DS_NB);
+  DR_T(sh, 5);
   // the first prompt id not in the output whose copy propensity exceeds 0.3
   {
     int fu = 0x7fffffff;
     for (int j = tid; j < R.np; j += DR_THREADS)
-      if (!dr_used(sh, c, R.P[j]) && dr_prop(T, R.P[j], 0.2) > 0.3) fu = min(fu, j);
+      if (!dr_used(sh, c, R.P[j]) && dr_prompt_prop(T, R, R.P[j]) > 0.3) fu = min(fu, j);
     fu = dr_min_i(fu, sh);
     if (tid == 0) sh.first_unused = fu < R.np ? R.P[fu] : -1;
   }
-  for (int j = tid; j < R.ncopy; j += DR_THREADS) push(R.copy[j], DS_COPY);
-  for (int j = tid; j < R.nascand; j += DR_THREADS) push(R.as_cand[j], DS_ASC);
+  for (int j = tid; j < R.ncopy; j += DR_THREADS) dr_mark(sh, R.copy[j]);
+  for (int j = tid; j < R.nascand; j += DR_THREADS) dr_mark(sh, R.as_cand[j]);
   __syncthreads();
-  // sort (bitonic, padded with the largest key) and merge equal tokens
-  const int n_raw = sh.ncand;
-  if (tid == 0 && n_raw > DR_MAX_CAND) sh.capped = 1;
-  const int nr = min(n_raw, DR_MAX_CAND);
-  int np2 = 1;
-  while (np2 < nr) np2 <<= 1;
-  for (int i = nr + tid; i < np2; i += DR_THREADS) sh.cand[i] = ~0ull;
+  DR_T(sh, 6);
+  // the distinct candidates in ascending token order: each thread counts the marks of its word
+  // range, a block scan gives its first index, it writes its tokens (and the prompt-match bit) and
+  // clears its words for the next context
+  constexpr int WPT = (DR_WORDS + DR_THREADS - 1) / DR_THREADS;
+  const int w0 = min(DR_WORDS, tid * WPT), w1 = min(DR_WORDS, w0 + WPT);
+  int cnt = 0;
+  for (int w = w0; w < w1; ++w) cnt += __popc(sh.mark[w]);
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sh.red_i[wid] = incl;
   __syncthreads();
-  for (int k = 2; k <= np2; k <<= 1)
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < np2; i += DR_THREADS) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long a = sh.cand[i], b = sh.cand[ixj];
-          if (((i & k) == 0) == (a > b)) { sh.cand[i] = b; sh.cand[ixj] = a; }
-        }
+  int idx = incl - cnt, total = 0;
+  for (int w = 0; w < DR_THREADS / 32; ++w) {
+    if (w < wid) idx += sh.red_i[w];
+    total += sh.red_i[w];
+  }
+  for (int w = w0; w < w1; ++w) {
+    uint32_t m = sh.mark[w];
+    const uint32_t pm = sh.prm[w];
+    while (m) {
+      const int b = __ffs(m) - 1;
+      if (idx < DR_MAX_CAND) {
+        sh.ctok[idx] = w * 32 + b;
+        sh.cbits[idx] = (pm >> b & 1u) ? DS_PR : 0u;
       }
-      __syncthreads();
+      ++idx;
+      m &= m - 1;
     }
-  if (tid == 0) {
-    int m = 0;
-    for (int i = 0; i < nr; ++i) {
-      const unsigned long long v = sh.cand[i];
-      if (m > 0 && (sh.cand[m - 1] >> 32) == (v >> 32)) sh.cand[m - 1] |= v & 0xffffffffull;
-      else sh.cand[m++] = v;
-    }
-    sh.ncand = m;
+    sh.mark[w] = 0u;
+    sh.prm[w] = 0u;
+  }
+  const int nc = min(total, DR_MAX_CAND);  // past the cap: the lowest token ids are kept
+  if (tid == 0 && total > DR_MAX_CAND) sh.capped = 1;
+  __syncthreads();
+  for (int k = tid; k < min(sh.nsmall, DR_SMALL); k += DR_THREADS) {
+    const int i = dr_find(sh.ctok, nc, (int)(sh.small[k] >> 32), dr_i32);
+    if (i >= 0) atomicOr(&sh.cbits[i], (uint32_t)sh.small[k]);
   }
   __syncthreads();
-  const int nc = sh.ncand;
+  DR_T(sh, 7);
   // features and scores, one candidate per thread, float64 (ildraft.py:519-701)
   const double ticks_odd = (double)((sh.ticks0 + [&] {
     int t = 0;
@@ -340,32 +472,38 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   const double open_fence = (out_first == 73594 || out_first == 13874) ? 1.0 : 0.0;
   const double open_tick = out_first == 63 ? 1.0 : 0.0;
   const double st_len = (double)min(lo, 32) / 32.0;
-  const float* W1 = T.mlp;
-  const float* b1 = W1 + T.H * DR_F;
-  const float* W2 = b1 + T.H;
-  const double b2 = (double)W2[T.H];
-  const float* WL = W2 + T.H + 1;
+  const double* W1 = sh.mlpd;
+  const double* b1 = W1 + T.H * DR_F;
+  const double* W2 = b1 + T.H;
+  const double b2 = W2[T.H];
+  const double* WL = W2 + T.H + 1;
   for (int ci = tid; ci < nc; ci += DR_THREADS) {
-    const int tok = (int)(sh.cand[ci] >> 32);
-    const uint32_t src = (uint32_t)sh.cand[ci];
+    const int tok = sh.ctok[ci];
+    const int icopy = dr_find(R.copy, R.ncopy, tok, dr_i32);
+    const bool in_p = icopy >= 0;
+    const bool in_as = R.nascand > 0 && dr_find(R.as_cand, R.nascand, tok, dr_i32) >= 0;
+    const uint32_t src = sh.cbits[ci] | (in_p ? DS_COPY : 0u) | (in_as ? DS_ASC : 0u);
     double x[DR_F];
 #pragma unroll
     for (int f = 0; f < DR_F; ++f) x[f] = 0.0;
     x[F_BIAS] = 1.0;
-    for (int n = 1; n <= T.N; ++n) {
-      if (sh.dist_tot[n] < 0) continue;
-      const DrPair* top = T.ngnx + sh.dist_first[n];
-      int cnt = 0, rank = -1;
+    // (unrolled over the orders, so that every index of x is a constant and x stays in registers)
+#pragma unroll
+    for (int n = 1; n <= DR_N_MAX; ++n) {
+      if (n > T.N || sh.dist_tot[n] < 0) continue;
+      const DrPair* top = sh.ngtop[n];
+      int cnt_n = 0, rank = -1;
       for (int i = 0; i < sh.dist_n[n]; ++i)
-        if ((int)top[i].a == tok) { cnt = (int)top[i].b; rank = i; break; }
-      if (n == sh.long_n && rank >= 1) x[rank == 1 ? F_NG_RANK2 : F_NG_RANK3PLUS] = 1.0;
-      if (cnt) {
-        const double p = (double)cnt / (double)sh.dist_tot[n];
-        if (n <= 6) x[F_NG_P1 + n - 1] = p;
+        if ((int)top[i].a == tok) { cnt_n = (int)top[i].b; rank = i; break; }
+      if (n == sh.long_n && rank == 1) x[F_NG_RANK2] = 1.0;
+      if (n == sh.long_n && rank >= 2) x[F_NG_RANK3PLUS] = 1.0;
+      if (cnt_n) {
+        const double p = (double)cnt_n / (double)sh.dist_tot[n];
+        if (n <= 6) x[F_NG_P1 + (n <= 6 ? n - 1 : 0)] = p;
         if (n == sh.long_n) {
           x[F_NG_P_LONG] = p;
           x[F_NG_ORD_LONG] = (double)n / 6.0 * p;
-          x[F_NG_LCNT_LONG] = log1p((double)cnt);
+          x[F_NG_LCNT_LONG] = log1p((double)cnt_n);
         }
         if (n == sh.supp3) x[F_NG_P_SUPP3] = p;
         if (n == sh.supp10) x[F_NG_P_SUPP10] = p;
@@ -388,31 +526,34 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     }
     if (src & DS_NB) {
       double s1 = 0.0, s2 = 0.0;
-      int cnt = 0, mm = 0;
+      int cv = 0, mx = 0;
       for (int r = 0; r < R.nnb; ++r)
         if (sh.vote_tok[r] == tok) {
           const int m8 = min(sh.vote_n[r], 8);
           s1 = s1 + R.nb_score[r];
           s2 = s2 + R.nb_score[r] * (double)m8 / 8.0;
-          ++cnt;
-          mm = max(mm, m8);
+          ++cv;
+          mx = max(mx, m8);
           if (r == 0) { x[F_NB_TOP1] = 1.0; x[F_NB_TOP1_M] = (double)m8 / 8.0; }
         }
       x[F_NB_SUM] = s1;
       x[F_NB_MSUM] = s2;
-      x[F_NB_CNT] = (double)cnt / (double)max(1, R.nnb);
-      x[F_NB_MAXM] = (double)mm / 8.0;
+      x[F_NB_CNT] = (double)cv / (double)max(1, R.nnb);
+      x[F_NB_MAXM] = (double)mx / 8.0;
     }
-    const bool in_p = dr_find(R.copy, R.ncopy, tok, dr_i32) >= 0;
     const bool used = dr_used(sh, c, tok);
     if (src & DS_COPY) {
-      const double pt = in_p ? dr_prop(T, tok, 0.2) : 0.3;
-      x[F_CP_PROP] = log(pt / (1.0 - pt)) / 4.0;
+      if (R.copy_logit) {
+        x[F_CP_PROP] = R.copy_logit[icopy];
+      } else {
+        const double pt = dr_copy_prop(T, R, icopy, tok);
+        x[F_CP_PROP] = log(pt / (1.0 - pt)) / 4.0;
+      }
       x[F_CP_CTX1] = sh.c1;
       x[F_CP_CTX2] = sh.c2;
       x[F_CP_UNUSED] = used ? 0.0 : 1.0;
       x[F_CP_FIRST_UNUSED] = tok == sh.first_unused ? 1.0 : 0.0;
-      x[F_CP_SPACEVAR] = in_p ? 0.0 : 1.0;
+      x[F_CP_SPACEVAR] = 0.0;
     }
     if (src & DS_ASC) x[F_AS_CAND] = 1.0;
     x[F_IS_STOP] = (tok == 151645 || tok == 151643) ? 1.0 : 0.0;
@@ -432,19 +573,36 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
       x[F_AS_MAX] = R.as_max[ai] / 4.0;
       x[F_AS_CNT] = (double)min(R.as_cnt[ai], 4) / 4.0;
     }
-    // score = W2 . relu(W1 x + b1) + b2 + WL . x
+    DR_T(sh, 11);
+    // score = W2 . relu(W1 x + b1) + b2 + WL . x; eight hidden units at a time (each one its own
+    // chain in feature order, the units summed in order)
     double s = 0.0;
-    for (int h = 0; h < T.H; ++h) {
+    int h = 0;
+    for (; h + 8 <= T.H; h += 8) {
+      double a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = 0.0;
+#pragma unroll
+      for (int f = 0; f < DR_F; ++f)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] = fma(W1[(h + j) * DR_F + f], x[f], a[j]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s = fma(W2[h + j], fmax(a[j] + b1[h + j], 0.0), s);
+    }
+    for (; h < T.H; ++h) {
       double a = 0.0;
-      for (int f = 0; f < DR_F; ++f) a = fma((double)W1[h * DR_F + f], x[f], a);
-      a += (double)b1[h];
-      s = fma((double)W2[h], fmax(a, 0.0), s);
+#pragma unroll
+      for (int f = 0; f < DR_F; ++f) a = fma(W1[h * DR_F + f], x[f], a);
+      s = fma(W2[h], fmax(a + b1[h], 0.0), s);
     }
     double lin = 0.0;
-    for (int f = 0; f < DR_F; ++f) lin = fma((double)WL[f], x[f], lin);
+#pragma unroll
+    for (int f = 0; f < DR_F; ++f) lin = fma(WL[f], x[f], lin);
     sh.prob[ci] = s + b2 + lin;
+    DR_T(sh, 13);
   }
   __syncthreads();
+  DR_T(sh, 8);
   // softmax with a null option of score 0
   double m = -INFINITY;
   for (int ci = tid; ci < nc; ci += DR_THREADS) m = fmax(m, sh.prob[ci]);
@@ -454,38 +612,63 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   z = dr_sum_d(z, sh) + exp(-m);
   for (int ci = tid; ci < nc; ci += DR_THREADS) sh.prob[ci] = exp(sh.prob[ci] - m) / z;
   __syncthreads();
-  // the 8 most probable, probability descending then token ascending
+  DR_T(sh, 9);
+  // the 8 most probable, probability descending then token (= index) ascending: each warp picks
+  // the 8 best of its candidates, then warp 0 the 8 best of those 64. A probability's key is its
+  // bit pattern plus one (monotonic for non-negative doubles); 0 marks none (taken entries hold
+  // -2.0, which is not a probability).
+#pragma unroll 1
   for (int k = 0; k < 8; ++k) {
-    double bp = -1.0;
+    unsigned long long bk = 0;
     int bi = -1;
-    for (int ci = tid; ci < nc; ci += DR_THREADS)
-      if (sh.prob[ci] > bp) { bp = sh.prob[ci]; bi = ci; }  // ascending ci = ascending token
-    // reduce (p desc, index asc) across the block through packed keys on the warp, then thread 0
-    for (int o = 16; o > 0; o >>= 1) {
-      const double op = __shfl_xor_sync(0xffffffffu, bp, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (op > bp || (op == bp && oi >= 0 && (bi < 0 || oi < bi))) { bp = op; bi = oi; }
+    for (int ci = tid; ci < nc; ci += DR_THREADS) {
+      const long long kb = __double_as_longlong(sh.prob[ci]);
+      if (kb >= 0 && (unsigned long long)kb + 1 > bk) { bk = (unsigned long long)kb + 1; bi = ci; }
     }
-    if ((tid & 31) == 0) { sh.red_d[tid >> 5] = bp; sh.red_i[tid >> 5] = bi; }
-    __syncthreads();
-    if (tid == 0) {
-      double p = sh.red_d[0];
-      int i = sh.red_i[0];
-      for (int w = 1; w < DR_THREADS / 32; ++w)
-        if (sh.red_d[w] > p || (sh.red_d[w] == p && sh.red_i[w] >= 0 && (i < 0 || sh.red_i[w] < i))) {
-          p = sh.red_d[w]; i = sh.red_i[w];
+    warp_argmax(bk, bi);
+    if (lane == 0) {
+      sh.wtop_k[wid][k] = bk;
+      sh.wtop_i[wid][k] = bi;
+      if (bi >= 0) sh.prob[bi] = -2.0;  // taken
+    }
+    __syncwarp();
+  }
+  DR_T(sh, 14);
+  __syncthreads();
+  DR_T(sh, 15);
+  if (wid == 0) {
+    constexpr int NW = DR_THREADS / 32;  // 8 warps x 8 entries: two per lane
+    unsigned long long k0 = sh.wtop_k[lane >> 3][lane & 7], k1 = sh.wtop_k[(NW / 2) + (lane >> 3)][lane & 7];
+    int i0 = sh.wtop_i[lane >> 3][lane & 7], i1 = sh.wtop_i[(NW / 2) + (lane >> 3)][lane & 7];
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) {
+#ifdef VP_DRAFT_TRACE
+      if (tid == 0) sh.tacc[16 + k] = clock64();
+#endif
+      unsigned long long bk = k0;
+      int bi = i0;
+      if (k1 > bk || (k1 == bk && k1 != 0 && i1 < bi)) { bk = k1; bi = i1; }
+      warp_argmax(bk, bi);
+      if (bi >= 0) {
+        if (i0 == bi) { k0 = 0; i0 = -1; }
+        if (i1 == bi) { k1 = 0; i1 = -1; }
+      }
+      if (lane == 0) {
+        if (bi >= 0 && bk != 0) {
+          sh.top_tok[k] = sh.ctok[bi];
+          sh.top_p[k] = __longlong_as_double((long long)(bk - 1));
+        } else {
+          sh.top_tok[k] = -1;
+          sh.top_p[k] = 0.0;
         }
-      if (i >= 0 && p >= 0.0) {
-        sh.top_tok[k] = (int)(sh.cand[i] >> 32);
-        sh.top_p[k] = p;
-        sh.prob[i] = -2.0;  // taken
-      } else {
-        sh.top_tok[k] = -1;
-        sh.top_p[k] = 0.0;
       }
     }
-    __syncthreads();
+#ifdef VP_DRAFT_TRACE
+    if (tid == 0) sh.tacc[24] = clock64();
+#endif
   }
+  __syncthreads();
+  DR_T(sh, 10);
 }
 
 // One draft tree of at most B nodes (B <= 15) with `branch` (<= 8) children per expansion, after
@@ -498,12 +681,62 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_draft(DraftTab T, DraftReq R,
   const int tid = threadIdx.x;
   const int lo0 = st ? __ldcg(&st->step) : lo0_given;
   const bool done = st ? __ldcg(&st->done) != 0 : false;
-  for (int i = tid; i < DR_WORDS; i += DR_THREADS) sh.used[i] = 0u;
+  for (int i = tid; i < DR_WORDS; i += DR_THREADS) {
+    sh.used[i] = 0u;
+    sh.mark[i] = 0u;
+    sh.prm[i] = 0u;
+  }
   if (tid == 0) { sh.capped = 0; sh.hn = 0; sh.hctr = 0; sh.nodes = 0; }
+#ifdef VP_DRAFT_TRACE
+  if (tid < 32) sh.tacc[tid] = 0ull;
+  if (tid == 0) sh.tlast = globaltimer();
+#endif
+  // stage what every context reads: the output, the prompt, the distinct prompt ids with their
+  // copy propensities, the MLP
+  const bool st_out = lo0 <= DR_OUT_CAP, st_pr = R.np <= DR_PROMPT_CAP, st_cp = R.ncopy <= DR_COPY_CAP;
+  if (st_out)
+    for (int i = tid; i < lo0; i += DR_THREADS) sh.outs[i] = out0[i];
+  if (st_pr)
+    for (int i = tid; i < R.np; i += DR_THREADS) sh.prs[i] = R.P[i];
+  if (st_cp)
+    for (int i = tid; i < R.ncopy; i += DR_THREADS) {
+      const int t = R.copy[i];
+      sh.cps[i] = t;
+      const int j = dr_find(T.prop, T.n_prop, (uint32_t)t, dr_rtok);
+      sh.cpp[i] = j >= 0 ? T.prop[j].v : __int_as_float(0x7fc00000);  // NaN: not in the table
+      const double pt = j >= 0 ? (double)T.prop[j].v : 0.2;
+      sh.cplg[i] = log(pt / (1.0 - pt)) / 4.0;
+    }
+  const bool st_as = R.nas <= DR_AS_CAP && R.nascand <= DR_AS_CAP;
+  if (st_as) {
+    for (int i = tid; i < R.nas; i += DR_THREADS) {
+      sh.ast[i] = R.as_tok[i];
+      sh.asmx[i] = R.as_max[i];
+      sh.ascn[i] = R.as_cnt[i];
+    }
+    for (int i = tid; i < R.nascand; i += DR_THREADS) sh.asc[i] = R.as_cand[i];
+  }
+  if (tid < R.nnb) sh.nbs[tid] = R.nb_score[tid];
+  const int n_mlp = T.H * DR_F + 2 * T.H + 1 + DR_F;
+  for (int i = tid; i < n_mlp; i += DR_THREADS) sh.mlpd[i] = (double)T.mlp[i];
   __syncthreads();
+  if (st_pr) R.P = sh.prs;
+  if (st_cp) {
+    R.copy = sh.cps;
+    R.copy_prop = sh.cpp;
+    R.copy_logit = sh.cplg;
+  }
+  if (st_as) {
+    R.as_tok = sh.ast;
+    R.as_max = sh.asmx;
+    R.as_cnt = sh.ascn;
+    R.as_cand = sh.asc;
+  }
+  R.nb_score = sh.nbs;
+  const int32_t* outp = st_out ? sh.outs : out0;
   int ticks = 0;  // backticks of the committed output (integer sum: any order)
   for (int i = tid; i < lo0; i += DR_THREADS) {
-    const int t = out0[i];
+    const int t = outp[i];
     if (t >= 0 && t < DR_VOCAB) atomicOr(&sh.used[t >> 5], 1u << (t & 31));
     ticks += dr_flag(T, t) & 7;
   }
@@ -518,75 +751,83 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_draft(DraftTab T, DraftReq R,
   }
   __syncthreads();
   DrCtx c;
-  c.out0 = out0;
+  c.out0 = outp;
   c.lo0 = lo0;
   c.path = sh.path;
-  // the root's candidates, then best first: pop, record, expand unless a stop token or full
-  int exp_i = 0;
+  // the root's candidates, then best first: pop, record, expand unless a stop token or full. One
+  // call site of dr_expand (the root is the expansion of node -1 with key -1: its children's keys
+  // are -p exactly), so the kernel's code holds one copy of it.
   if (!done) {
+    int exp_i = 0;
+    double key = -1.0;
+    int node = -1;
     c.np = 0;
-    dr_expand(T, R, c, sh);
-    if (tid == 0) {
-      for (int k = 0; k < branch; ++k)
-        if (sh.top_tok[k] >= 0) {
-          const int h = sh.hn++;
-          sh.hk[h] = -sh.top_p[k]; sh.hseq[h] = sh.hctr++; sh.hpar[h] = -1; sh.htok[h] = sh.top_tok[k];
-        }
-      if (O.exp_tok)
-        for (int k = 0; k < 8; ++k) { O.exp_tok[k] = sh.top_tok[k]; O.exp_p[k] = sh.top_p[k]; }
-    }
-    ++exp_i;
-    __syncthreads();
     for (;;) {
+      dr_expand(T, R, c, sh);
       if (tid == 0) {
-        sh.go = 0;
-        if (sh.hn > 0 && sh.nodes < B) {
-          // pop the smallest (key, seq)
-          int b = 0;
-          for (int h = 1; h < sh.hn; ++h)
-            if (sh.hk[h] < sh.hk[b] || (sh.hk[h] == sh.hk[b] && sh.hseq[h] < sh.hseq[b])) b = h;
-          const double key = sh.hk[b];
-          const int par = sh.hpar[b], tok = sh.htok[b];
-          --sh.hn;
-          sh.hk[b] = sh.hk[sh.hn]; sh.hseq[b] = sh.hseq[sh.hn]; sh.hpar[b] = sh.hpar[sh.hn]; sh.htok[b] = sh.htok[sh.hn];
-          const int node = sh.nodes++;
-          sh.npar[node] = par; sh.ntok[node] = tok;
-          sh.cur = node;
-          sh.red_d[0] = key;
-          if (tok != 151645 && tok != 151643 && sh.nodes < B) {
-            // the node's path from the root
-            int d = 0, v = node;
-            int rev[16];
-            while (v >= 0) { rev[d++] = sh.ntok[v]; v = sh.npar[v]; }
-            for (int i = 0; i < d; ++i) sh.path[i] = rev[d - 1 - i];
-            sh.npath = d;
-            sh.go = 2;
-          } else {
-            sh.go = 1;
+        for (int k = 0; k < branch; ++k)
+          if (sh.top_tok[k] >= 0 && sh.hn < DR_HEAP) {
+            const int h = sh.hn++;
+            sh.hk[h] = key * sh.top_p[k]; sh.hseq[h] = sh.hctr++; sh.hpar[h] = node; sh.htok[h] = sh.top_tok[k];
+          }
+        if (O.exp_tok && exp_i < 16)
+          for (int k = 0; k < 8; ++k) { O.exp_tok[exp_i * 8 + k] = sh.top_tok[k]; O.exp_p[exp_i * 8 + k] = sh.top_p[k]; }
+      }
+      ++exp_i;
+      __syncthreads();
+      int go = 1;
+      while (go == 1) {
+        if (tid < 32) {
+          // warp 0 finds the smallest (key, seq) of the queue; thread 0 pops it
+          const bool can = sh.hn > 0 && sh.nodes < B;
+          int b = -1;
+          if (can) {
+            // smallest key first, then the smallest sequence number: as the largest complemented
+            // order-preserving key, then the lowest sequence among the lanes that hold it
+            unsigned long long bk = 0;
+            int bs = 0x7fffffff, bl = -1;
+            for (int h = tid; h < sh.hn; h += 32) {
+              const unsigned long long u = ~dr_ord(sh.hk[h]);
+              if (bl < 0 || u > bk || (u == bk && sh.hseq[h] < bs)) { bl = h; bk = u; bs = sh.hseq[h]; }
+            }
+            const unsigned long long m = warp_max_u64(bl >= 0 ? bk : 0ull);
+            const bool at = bl >= 0 && bk == m;
+            const unsigned smin = __reduce_min_sync(0xffffffffu, at ? (unsigned)bs : 0xffffffffu);
+            b = __reduce_max_sync(0xffffffffu, (at && (unsigned)bs == smin) ? bl : -1);
+          }
+          if (tid == 0) sh.go = 0;
+          if (tid == 0 && can) {
+            const double kb = sh.hk[b];
+            const int par = sh.hpar[b], tok = sh.htok[b];
+            --sh.hn;
+            sh.hk[b] = sh.hk[sh.hn]; sh.hseq[b] = sh.hseq[sh.hn]; sh.hpar[b] = sh.hpar[sh.hn]; sh.htok[b] = sh.htok[sh.hn];
+            const int nd = sh.nodes++;
+            sh.npar[nd] = par; sh.ntok[nd] = tok;
+            sh.cur = nd;
+            sh.red_d[0] = kb;
+            if (tok != 151645 && tok != 151643 && sh.nodes < B) {
+              // the node's path from the root
+              int d = 0, v = nd;
+              int rev[16];
+              while (v >= 0) { rev[d++] = sh.ntok[v]; v = sh.npar[v]; }
+              for (int i = 0; i < d; ++i) sh.path[i] = rev[d - 1 - i];
+              sh.npath = d;
+              sh.go = 2;
+            } else {
+              sh.go = 1;
+            }
           }
         }
-      }
-      __syncthreads();
-      const int go = sh.go;
-      if (go == 0) break;
-      if (go == 2) {
-        const double key = sh.red_d[0];
-        const int node = sh.cur;
         __syncthreads();
-        c.np = sh.npath;
-        dr_expand(T, R, c, sh);
-        if (tid == 0) {
-          for (int k = 0; k < branch; ++k)
-            if (sh.top_tok[k] >= 0 && sh.hn < DR_HEAP) {
-              const int h = sh.hn++;
-              sh.hk[h] = key * sh.top_p[k]; sh.hseq[h] = sh.hctr++; sh.hpar[h] = node; sh.htok[h] = sh.top_tok[k];
-            }
-          if (O.exp_tok && exp_i < 16)
-            for (int k = 0; k < 8; ++k) { O.exp_tok[exp_i * 8 + k] = sh.top_tok[k]; O.exp_p[exp_i * 8 + k] = sh.top_p[k]; }
+        go = sh.go;
+        if (go == 2) {
+          key = sh.red_d[0];
+          node = sh.cur;
+          c.np = sh.npath;
         }
-        ++exp_i;
+        __syncthreads();
       }
-      __syncthreads();
+      if (go == 0) break;
     }
   }
   // the tree buffer: row 0 the last committed token, row i + 1 node i
@@ -614,6 +855,10 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_draft(DraftTab T, DraftReq R,
       }
     if (O.status) *O.status = sh.capped;
   }
+#ifdef VP_DRAFT_TRACE
+  DR_T(sh, 12);
+  if (tid < 32) g_dr_trace[tid] = sh.tacc[tid];
+#endif
 }
 
 }  // namespace vp

@@ -456,7 +456,8 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
   if (r) return r;
   if (!tree) return fail(VP_ERR_ARG, "null tree");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
+  if (tree != c->s.tree)  // a drafter may have written the context's own tree buffer (vp_buffer 7)
+    VP_CUDA(cudaMemcpyAsync(c->s.tree, tree, VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
   MegaParams p = mega_params(c);
   p.do_lm = 1;
   p.do_commit = 1;
@@ -599,6 +600,7 @@ int vp_buffer(vp_ctx* c, int32_t which, void** ptr, size_t* bytes) {
     case 4: *ptr = c->lm_pval; *bytes = pv; break;
     case 5: *ptr = c->lm_pidx; *bytes = pv; break;
     case 6: *ptr = c->trace; *bytes = MK_TRACE * sizeof(unsigned long long); break;
+    case 7: *ptr = c->s.tree; *bytes = VP_TREE_INTS * sizeof(int32_t); break;
     default: return fail(VP_ERR_ARG, "unknown buffer");
   }
   return VP_OK;

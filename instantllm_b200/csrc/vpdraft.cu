@@ -97,6 +97,9 @@ int vp_drafter_create(const void* table, size_t bytes, int32_t device, vp_drafte
   vp_drafter* d = new vp_drafter();
   d->device = device;
   cudaError_t e = cudaSetDevice(device);
+  // k_draft keeps the staged request and the candidate bitsets in ~150 KB of shared memory
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_draft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(DrShared));
   if (e != cudaSuccess) { delete d; return dfail(VP_ERR_CUDA, cudaGetErrorString(e)); }
   auto upload = [&](const void* src, size_t n, void** dst) -> int {
     void* p = nullptr;
@@ -229,5 +232,12 @@ int vp_draft(vp_drafter* d, const int32_t* d_out_tokens, const vp_state* d_state
   VD_CUDA(cudaGetLastError());
   return VP_OK;
 }
+
+#ifdef VP_DRAFT_TRACE
+// Per-phase time of the last k_draft launch, ns summed over its expansions (trace builds only).
+int vp_draft_trace(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, vp::g_dr_trace, sizeof(unsigned long long) * 32) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 }  // extern "C"

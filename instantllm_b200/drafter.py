@@ -144,9 +144,9 @@ class DeviceDrafter:
     def draft(self, tree_out: torch.Tensor, out_tokens: torch.Tensor, n_out: Optional[int] = None,
               state_ptr: Optional[int] = None, B: int = 15, branch: int = 8, debug: bool = False,
               stream=None) -> Optional[dict]:
-        """One drafting step on the device: the tree (VP_TREE_INTS int32, device tensor tree_out)
-        after the output tokens out_tokens (device int32; n_out of them, or the step count of the
-        device state at state_ptr). With debug, waits and returns the nodes and every expansion's
+        """One drafting step on the device: the tree (VP_TREE_INTS int32, device tensor or pointer
+        tree_out) after the output tokens out_tokens (device int32 tensor or pointer; n_out of them,
+        or the step count of the device state at state_ptr). With debug, waits and returns the nodes and every expansion's
         top 8."""
         dbg = None
         if debug:
@@ -161,8 +161,13 @@ class DeviceDrafter:
             d = self._dbg
             dbg = _Debug(*[d[k].data_ptr() for k in ("parents", "tokens", "exp_tokens", "exp_probs", "status")])
         s = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
-        _lib.check(self.lib.vp_draft(self.h, out_tokens.data_ptr() if out_tokens is not None else None, state_ptr,
-                                     -1 if n_out is None else int(n_out), B, branch, tree_out.data_ptr(),
+        if out_tokens is None or isinstance(out_tokens, int):
+            out_ptr = out_tokens
+        else:
+            out_ptr = out_tokens.data_ptr()
+        tree_ptr = tree_out if isinstance(tree_out, int) else tree_out.data_ptr()
+        _lib.check(self.lib.vp_draft(self.h, out_ptr, state_ptr,
+                                     -1 if n_out is None else int(n_out), B, branch, tree_ptr,
                                      ctypes.byref(dbg) if dbg is not None else None, s), "vp_draft")
         if not debug:
             return None

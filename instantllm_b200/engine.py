@@ -41,6 +41,42 @@ def _np_to_dev(a: np.ndarray, device) -> torch.Tensor:
     return torch.from_numpy(a.view(np.uint8).reshape(-1)).to(device)
 
 
+class PassShape:
+    """Adaptive speculation (Engine.nextPassShape, Engine.swift:878-898): the next pass verifies the
+    configured best-first tree (tree_b drafts, 8 children per expansion) while at least adapt_hi
+    drafts per pass were accepted over the last few committed passes, and an 8-row chain below
+    that rate (unpredictable text). A chain is the drafter's tree search with one child per
+    expansion. Both shapes run through the same pass kernel, whose numerics agree for every row
+    count, so the output stays that of plain greedy decoding. (The reference's adaptLo tier of
+    3-row shader passes has no counterpart: one kernel serves every row count here.)"""
+
+    def __init__(self, tree_b: int = 15, chain_rows: int = 8, adaptive: bool = True, adapt_hi: float = 1.5):
+        if not 1 <= tree_b <= 15 or not 2 <= chain_rows <= 16:
+            raise ValueError("tree_b must be 1..15 and chain_rows 2..16")
+        self.tree_b, self.chain_rows, self.adaptive, self.adapt_hi = tree_b, chain_rows, adaptive, adapt_hi
+        self.hist = []
+
+    def reset(self) -> None:
+        self.hist.clear()
+
+    def next(self, passes: int, accepted: int):
+        """(drafts B, children per expansion) of the next pass, from the request's committed pass
+        and accepted-draft counters as last seen by the host."""
+        tree = (self.tree_b, 8)
+        if not self.adaptive:
+            return tree
+        if not self.hist or self.hist[-1][0] != passes:
+            self.hist.append((passes, accepted))
+        if len(self.hist) < 3:
+            return tree
+        p0, a0 = self.hist[-4:][0]
+        if passes - p0 < 2:
+            return tree
+        if (accepted - a0) / (passes - p0) >= self.adapt_hi:
+            return tree
+        return (self.chain_rows - 1, 1)
+
+
 class VerifyEngine:
     def __init__(self, weights: dict, max_ctx: int = 4096, max_steps: int = 4096, device: int = 0):
         self.lib = _lib.load()
@@ -339,3 +375,81 @@ class VerifyEngine:
                 raise _lib.VpError(f"device error bits {st['err']}")
         assert len(out) == st["step"], (len(out), st["step"])
         return {"tokens": out, "passes": passes, "state": st}
+
+    def generate_drafted(self, prompt, max_new: int, drafter, pids=None, text: str = "", eos=STOP_IDS,
+                         cached: int = 0, depth: int = 1, shape: Optional[PassShape] = None) -> dict:
+        """Engine.generate with the learned drafter (Engine.swift:922-1030), device-resident: after
+        the prefill, every step is k_draft (the next tree from the committed tokens and the device
+        state, written into a device tree buffer) followed by one pass, both on this engine's
+        stream, so no token or tree goes through the host. As the reference does, the host keeps
+        `depth` steps enqueued ahead of the last one it has seen finish (encode-ahead), reads each
+        finished step's state from a pinned copy made on the stream (no synchronisation while the
+        GPU has work queued), and picks every new step's shape from those counters (PassShape).
+        Steps enqueued past the stop run as early exits: every kernel of a finished request
+        returns at once. drafter: a DeviceDrafter on this engine's device; pids / text: the
+        request context of Drafter.begin (the prompt's ids and its text), built on the host while
+        the GPU prefills. Returns the tokens (as generate), the passes, the shapes enqueued, the
+        host waits and the final state (passes: the verify passes that committed, as generate
+        counts them)."""
+        if drafter.device != self.device:
+            raise ValueError("the drafter's table must be on the engine's device")
+        if depth < 0:
+            raise ValueError("depth must be >= 0")
+        shape = shape if shape is not None else PassShape()
+        shape.reset()
+        prompt = list(prompt)
+        self.begin(cached, max_new, eos)
+        self.prefill(prompt[cached:])
+        drafter.begin(prompt if pids is None else list(pids), text)  # overlaps the prefill
+        tree_ptr = self.buffer(7, (TREE_INTS,), "<i4").data_ptr()  # the pass reads it in place
+        slots = depth + 2  # at most depth + 1 copies in flight
+        host = getattr(self, "_loop_host", None)
+        if host is None or host.shape[0] < slots:
+            host = self._loop_host = torch.zeros((slots, len(_lib.STATE_FIELDS)), dtype=torch.int32).pin_memory()
+        st_ptr = self.lib.vp_device_state(self.ctx)
+        tok_ptr = self.lib.vp_device_tokens(self.ctx)
+        st_dev = torch.as_tensor(_DevArray(st_ptr, (len(_lib.STATE_FIELDS),), "<i4"), device=self.device)
+        i_passes = _lib.STATE_FIELDS.index("passes")
+        i_acc = _lib.STATE_FIELDS.index("accepted")
+        i_done = _lib.STATE_FIELDS.index("done")
+        from collections import deque
+
+        pending = deque()
+        seen_passes = seen_acc = seen_done = 0
+        shapes = []
+        waits = 0
+        encoded = 1  # the prefill (as Engine.generate counts it)
+        with torch.cuda.stream(self.stream):
+            while True:
+                while pending and pending[0][0].query():
+                    _, k = pending.popleft()
+                    row = host[k].tolist()
+                    seen_passes, seen_acc, seen_done = row[i_passes], row[i_acc], row[i_done]
+                if seen_done:
+                    break
+                # the prefill yields one token and every pass at least one, so max_new - 1 passes
+                # always reach the stop; `passes` counts the prefill's commit too, and the prefill
+                # counts as seen from the start (Engine.generate's `done = 1 + passes`)
+                if encoded < max_new and encoded - max(seen_passes, 1) <= depth:
+                    B, branch = shape.next(seen_passes, seen_acc)
+                    shapes.append((B, branch))
+                    drafter.draft(tree_ptr, tok_ptr, state_ptr=st_ptr, B=B, branch=branch, stream=self._s)
+                    check(self.lib.vp_pass(self.ctx, tree_ptr, self._s), "vp_pass")
+                    k = encoded % slots
+                    host[k].copy_(st_dev, non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(self.stream)
+                    pending.append((ev, k))
+                    encoded += 1
+                    continue
+                if not pending:
+                    break
+                pending[0][0].synchronize()
+                waits += 1
+        st = self.state()
+        if st["err"]:
+            raise _lib.VpError(f"device error bits {st['err']}")
+        if not st["done"]:
+            raise _lib.VpError("decode loop ended before the request's stop")
+        out = self.tokens(st["step"])
+        return {"tokens": out, "passes": st["passes"] - 1, "state": st, "shapes": shapes, "host_waits": waits}

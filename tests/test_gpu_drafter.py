@@ -57,3 +57,42 @@ def test_device_drafter_reproduces_the_reference_trees():
             n_steps += 1
     assert n_steps == sum(len(c["steps"]) for c in GOLD["cases"])
     d.close()
+
+
+def test_drafted_decode_loop_equals_greedy_decoding():
+    """VerifyEngine.generate_drafted: every step is k_draft (the tree from the device's committed
+    tokens and state, written into the pass's own tree buffer) and one pass, enqueued `depth`
+    steps ahead with the shape chosen by PassShape from the counters the host has seen; no token
+    or tree goes through the host. Its output must be plain greedy decoding (1-row passes through
+    the same kernels) token for token, at every depth. The model is random-init, so few drafts are
+    accepted and the adaptive rule must fall back to 8-row chains after the first passes."""
+    from instantllm_b200 import synth
+    from instantllm_b200.drafter import DeviceDrafter
+    from instantllm_b200.engine import PassShape, VerifyEngine
+
+    w = synth.make_weights("q4", seed=3)
+    eng = VerifyEngine(w, max_ctx=1024, max_steps=256)
+    d = DeviceDrafter(os.path.join(HERE, "golden", "draft_subset.ildraft"))
+    try:
+        for i, case in enumerate(GOLD["cases"]):
+            depth = i % 3
+            prompt = list(case["pids"])
+            ref = eng.generate(prompt, 40)
+            got = eng.generate_drafted(prompt, 40, d, pids=prompt, text=case["text"], depth=depth)
+            assert got["tokens"] == ref["tokens"], (i, depth)
+            assert got["state"]["err"] == 0
+            shapes = got["shapes"]
+            assert shapes[0] == (15, 8)
+            rate = got["state"]["accepted"] / max(1, got["passes"])
+            if rate < 1.5 and got["passes"] >= 4:
+                assert (7, 1) in shapes, (i, shapes)
+            assert got["passes"] <= len(shapes) <= got["passes"] + depth + 1
+        # the non-adaptive tree loop gives the same tokens too
+        prompt = list(GOLD["cases"][0]["pids"])
+        fixed = eng.generate_drafted(prompt, 40, d, pids=prompt, text=GOLD["cases"][0]["text"],
+                                     shape=PassShape(adaptive=False))
+        assert fixed["tokens"] == eng.generate(prompt, 40)["tokens"]
+        assert set(fixed["shapes"]) == {(15, 8)}
+    finally:
+        d.close()
+        eng.close()

@@ -53,3 +53,33 @@ def test_synthetic_distributions():
     assert (s >= 0).all() and np.allclose(mn, -7.5 * s, rtol=1e-3, atol=1e-7)
     q8 = synth.make_matrix("q8", 64, 128, rng)
     assert q8["codes"].min() >= -127 and q8["codes"].max() <= 127
+
+
+def test_adaptive_pass_shape_follows_the_reference_rule():
+    """PassShape mirrors Engine.nextPassShape (Engine.swift:887-898): the configured tree until at
+    least 3 samples of (passes, accepted) span 2 or more passes, then the tree while the accepted
+    drafts per pass over the oldest of the last 4 samples reach adaptHi (1.5), else an 8-row chain
+    (7 drafts, one child per expansion)."""
+    from instantllm_b200.engine import PassShape
+
+    TREE, CHAIN = (15, 8), (7, 1)
+    s = PassShape()
+    assert s.next(1, 0) == TREE and s.next(1, 0) == TREE  # the same sample is recorded once
+    assert s.hist == [(1, 0)]
+    assert s.next(2, 0) == TREE                            # 2 samples
+    assert s.next(3, 0) == CHAIN                           # 3 samples over 2 passes, rate 0
+    assert s.next(4, 6) == TREE                            # (6 - 0) / (4 - 1) = 2.0
+    assert s.next(5, 6) == TREE                            # window (2, 0): 6 / 3 = 2.0
+    assert s.next(6, 6) == TREE                            # window (3, 0): 6 / 3 = 2.0
+    assert s.next(7, 6) == CHAIN                           # window (4, 6): 0 / 3
+    s = PassShape()
+    for p, a in [(1, 0), (2, 2), (3, 3)]:
+        s.next(p, a)
+    assert s.next(4, 4) == CHAIN                           # window (1, 0): 4 / 3 = 1.33 < 1.5
+    assert s.next(5, 7) == TREE                            # window (2, 2): 5 / 3 = 1.67
+    s = PassShape(adaptive=False)
+    assert all(s.next(p, 0) == TREE for p in range(1, 10))
+    s = PassShape(tree_b=9, chain_rows=4, adapt_hi=0.5)
+    assert [s.next(p, 0) for p in (1, 2, 3)] == [(9, 8), (9, 8), (3, 1)]
+    s.reset()
+    assert s.hist == [] and s.next(7, 0) == (9, 8)
