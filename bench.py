@@ -601,7 +601,8 @@ def run_decode_loop(args):
     256-token prompt decoded 64 tokens, every step k_draft (the learned drafter on the device, on
     the committed table subset tests/golden/draft_subset.ildraft) + one verify pass, enqueued one
     step ahead, the shape from the adaptive rule. Against it: the same request by plain greedy
-    decoding (1-row passes) and by the loop with fixed trees; and k_draft alone. The weights are
+    decoding (1-row passes), by the loop with fixed trees and by the loop replaying each step as a
+    CUDA graph; and k_draft alone. The weights are
     random-init, so the drafter's candidates (trained on real text) are rarely accepted: the line
     measures the loop's overhead, not a speed-up. One JSON line of its own, 1 GPU."""
     import os
@@ -640,6 +641,8 @@ def run_decode_loop(args):
     clk = clocks.stop()
     ms_tree, rt = timed(lambda: eng.generate_drafted(prompt, n_new, d, pids=prompt, text="", depth=1,
                                                      shape=PassShape(adaptive=False)))
+    ms_graph, rg = timed(lambda: eng.generate_drafted(prompt, n_new, d, pids=prompt, text="", depth=1,
+                                                      graphs=True))
     ms_greedy, g = timed(lambda: eng.generate(prompt, n_new))
     # k_draft alone, after the request's last committed token (device state as the loop left it)
     tree_ptr = eng.buffer(7, (synth.TREE_INTS,), "<i4").data_ptr()
@@ -670,8 +673,9 @@ def run_decode_loop(args):
         "shapes": {f"B{b}_branch{br}": r["shapes"].count((b, br)) for b, br in sorted(set(r["shapes"]))},
         "host_waits": r["host_waits"],
         "fixed_tree_loop_tok_s": len(rt["tokens"]) / (ms_tree * 1e-3),
+        "graph_loop_tok_s": len(rg["tokens"]) / (ms_graph * 1e-3),
         "greedy_tok_s": len(g["tokens"]) / (ms_greedy * 1e-3),
-        "tokens_equal_greedy": r["tokens"] == g["tokens"] == rt["tokens"],
+        "tokens_equal_greedy": r["tokens"] == g["tokens"] == rt["tokens"] == rg["tokens"],
         "k_draft_us": draft_us,
         "dtype": "q4 weights, fp16 activations, fp32 accumulate; drafter float64",
         "data": "synthetic (seeded random-init q4 weights, uniform prompt ids); drafter table: the committed "

@@ -317,6 +317,21 @@ int vp_drafter_begin(vp_drafter* d, const vp_draft_request* req);
 int vp_draft(vp_drafter* d, const int32_t* d_out_tokens, const vp_state* d_state, int32_t n_out, int32_t B,
              int32_t branch, int32_t* d_tree, const vp_draft_debug* dbg, void* stream);
 
+/* ---- CUDA graphs: the pass encoder as a replayable graph (the proposed vp_pass_graph) ----
+ * vp_pass_graph captures one fused pass (vp_pass with the device tree d_tree; the context's own
+ * tree buffer, vp_buffer 7, needs no copy node). vp_step_graph captures one step of the
+ * device-resident decode loop: vp_draft from the context's device tokens and state into its tree
+ * buffer, then vp_pass. vp_graph_launch replays a graph on a stream (stream-ordered, no
+ * synchronisation). A graph holds the context's and the drafter request's device pointers by value:
+ * a step graph refuses to launch once vp_drafter_begin has replaced its request (VP_ERR_STATE:
+ * capture again), and graphs must be destroyed before their context or drafter. Errors: VP_ERR_ARG
+ * (null argument, host tree), VP_ERR_STATE, VP_ERR_CUDA (capture or launch failed). */
+typedef struct vp_graph vp_graph;
+int vp_pass_graph(vp_ctx* ctx, const int32_t* d_tree, vp_graph** out);
+int vp_step_graph(vp_ctx* ctx, vp_drafter* d, int32_t B, int32_t branch, vp_graph** out);
+int vp_graph_launch(vp_graph* g, void* stream);
+void vp_graph_destroy(vp_graph* g);
+
 #ifdef __cplusplus
 }
 #endif

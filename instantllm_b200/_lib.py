@@ -23,6 +23,7 @@ EXPORTS = (
     "vp_debug_logits", "vp_buffer", "vp_head_argmax_noalloc",
     "vp_sketch_bytes", "vp_pack_sketch", "vp_sketch_work_bytes", "vp_sketch_bounds_offset",
     "vp_head_argmax_sketch", "vp_drafter_create", "vp_drafter_destroy", "vp_drafter_begin", "vp_draft",
+    "vp_pass_graph", "vp_step_graph", "vp_graph_launch", "vp_graph_destroy",
 )
 
 
@@ -103,6 +104,10 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_drafter_destroy": (None, [vp]),
         "vp_drafter_begin": (ctypes.c_int, [vp, vp]),
         "vp_draft": (ctypes.c_int, [vp, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "vp_pass_graph": (ctypes.c_int, [vp, vp, ctypes.POINTER(vp)]),
+        "vp_step_graph": (ctypes.c_int, [vp, vp, i32, i32, ctypes.POINTER(vp)]),
+        "vp_graph_launch": (ctypes.c_int, [vp, vp]),
+        "vp_graph_destroy": (None, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

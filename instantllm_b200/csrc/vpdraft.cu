@@ -47,6 +47,15 @@ struct vp_drafter {
   DraftReq req{};
   bool have_req = false;
   int knb = 0;
+  uint64_t gen = 0;  // requests begun so far: a step graph captured one request's pointers
+};
+
+// A replayable CUDA graph of a pass or of a decode step (see vpass.h).
+struct vp_graph {
+  cudaGraphExec_t exec = nullptr;
+  const vp_drafter* d = nullptr;  // step graphs: the drafter and the request they captured
+  uint64_t gen = 0;
+  int device = 0;
 };
 
 extern "C" {
@@ -208,6 +217,7 @@ int vp_drafter_begin(vp_drafter* d, const vp_draft_request* q) {
   R.nas = q->n_as;
   R.nascand = q->n_as_cand;
   d->have_req = true;
+  ++d->gen;
   return VP_OK;
 }
 
@@ -231,6 +241,97 @@ int vp_draft(vp_drafter* d, const int32_t* d_out_tokens, const vp_state* d_state
       d->tab, d->req, d_out_tokens, d_state, n_out, B, branch, o);
   VD_CUDA(cudaGetLastError());
   return VP_OK;
+}
+
+// ---- CUDA graphs ----
+
+}  // extern "C"
+
+namespace {
+// Captures what `enqueue` puts on a private stream and instantiates it.
+template <typename F>
+int capture(int device, F enqueue, cudaGraphExec_t* out) {
+  *out = nullptr;
+  VD_CUDA(cudaSetDevice(device));
+  cudaStream_t st = nullptr;
+  VD_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  int r = VP_OK;
+  if (e == cudaSuccess) {
+    r = enqueue(st);
+    const cudaError_t e2 = cudaStreamEndCapture(st, &g);  // ends the capture whatever enqueue did
+    if (r == VP_OK) e = e2;
+  }
+  if (r == VP_OK && e == cudaSuccess) e = cudaGraphInstantiate(out, g, 0);
+  if (g) cudaGraphDestroy(g);
+  cudaStreamDestroy(st);
+  if (r != VP_OK) return r;
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return dfail(VP_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  }
+  return VP_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int vp_pass_graph(vp_ctx* ctx, const int32_t* d_tree, vp_graph** out) {
+  if (!ctx || !d_tree || !out) return dfail(VP_ERR_ARG, "null argument");
+  *out = nullptr;
+  cudaPointerAttributes pa{};
+  if (cudaPointerGetAttributes(&pa, d_tree) != cudaSuccess || pa.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return dfail(VP_ERR_ARG, "the tree of a pass graph must be device memory");
+  }
+  vp_graph* g = new vp_graph();
+  g->device = pa.device;
+  const int r = capture(pa.device, [&](cudaStream_t st) { return vp_pass(ctx, d_tree, st); }, &g->exec);
+  if (r != VP_OK) { delete g; return r; }
+  *out = g;
+  return VP_OK;
+}
+
+int vp_step_graph(vp_ctx* ctx, vp_drafter* d, int32_t B, int32_t branch, vp_graph** out) {
+  if (!ctx || !d || !out) return dfail(VP_ERR_ARG, "null argument");
+  *out = nullptr;
+  if (!d->have_req) return dfail(VP_ERR_STATE, "vp_drafter_begin first");
+  void* tree = nullptr;
+  size_t bytes = 0;
+  int r = vp_buffer(ctx, 7, &tree, &bytes);
+  if (r) return r;
+  const int32_t* toks = vp_device_tokens(ctx);
+  const vp_state* st_dev = vp_device_state(ctx);
+  if (!toks || !st_dev) return dfail(VP_ERR_ARG, "context without device buffers");
+  vp_graph* g = new vp_graph();
+  g->device = d->device;
+  g->d = d;
+  g->gen = d->gen;
+  r = capture(d->device, [&](cudaStream_t st) {
+    const int rd = vp_draft(d, toks, st_dev, -1, B, branch, static_cast<int32_t*>(tree), nullptr, st);
+    return rd ? rd : vp_pass(ctx, static_cast<const int32_t*>(tree), st);
+  }, &g->exec);
+  if (r != VP_OK) { delete g; return r; }
+  *out = g;
+  return VP_OK;
+}
+
+int vp_graph_launch(vp_graph* g, void* stream) {
+  if (!g || !g->exec) return dfail(VP_ERR_ARG, "null graph");
+  if (g->d && g->d->gen != g->gen) return dfail(VP_ERR_STATE, "the drafter began another request: capture again");
+  VD_CUDA(cudaSetDevice(g->device));
+  VD_CUDA(cudaGraphLaunch(g->exec, static_cast<cudaStream_t>(stream)));
+  return VP_OK;
+}
+
+void vp_graph_destroy(vp_graph* g) {
+  if (!g) return;
+  if (g->exec) {
+    cudaSetDevice(g->device);
+    cudaGraphExecDestroy(g->exec);
+  }
+  delete g;
 }
 
 #ifdef VP_DRAFT_TRACE

@@ -41,6 +41,29 @@ def _np_to_dev(a: np.ndarray, device) -> torch.Tensor:
     return torch.from_numpy(a.view(np.uint8).reshape(-1)).to(device)
 
 
+class Graph:
+    """A replayable CUDA graph made by the library (vp_pass_graph, vp_step_graph): launch() replays
+    it on a stream; close() (or garbage collection) destroys it. Destroy it before its engine or
+    drafter."""
+
+    def __init__(self, lib, handle: ctypes.c_void_p):
+        self.lib, self.h = lib, handle
+
+    def launch(self, stream: int) -> None:
+        check(self.lib.vp_graph_launch(self.h, stream), "vp_graph_launch")
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.vp_graph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class PassShape:
     """Adaptive speculation (Engine.nextPassShape, Engine.swift:878-898): the next pass verifies the
     configured best-first tree (tree_b drafts, 8 children per expansion) while at least adapt_hi
@@ -223,6 +246,21 @@ class VerifyEngine:
         """Graph pass with a device-resident tree buffer (no host round trip)."""
         check(self.lib.vp_pass(self.ctx, tree_dev.data_ptr(), self._s), "vp_pass")
 
+    def pass_graph(self, tree_dev: torch.Tensor) -> Graph:
+        """One fused pass reading the device tree buffer tree_dev, captured as a CUDA graph
+        (vp_pass_graph): Graph.launch(stream) replays it."""
+        h = ctypes.c_void_p()
+        check(self.lib.vp_pass_graph(self.ctx, tree_dev.data_ptr(), ctypes.byref(h)), "vp_pass_graph")
+        return Graph(self.lib, h)
+
+    def step_graph(self, drafter, B: int, branch: int) -> Graph:
+        """One step of the device-resident decode loop (the drafter's tree for the committed
+        tokens, written into this context's tree buffer, then the pass) captured as a CUDA graph
+        (vp_step_graph), for the drafter's current request."""
+        h = ctypes.c_void_p()
+        check(self.lib.vp_step_graph(self.ctx, drafter.h, int(B), int(branch), ctypes.byref(h)), "vp_step_graph")
+        return Graph(self.lib, h)
+
     @staticmethod
     def pass_multi(engines, trees_dev) -> None:
         """One verify pass + commit of each engine's request in one launch (vp_pass_multi), each
@@ -377,7 +415,8 @@ class VerifyEngine:
         return {"tokens": out, "passes": passes, "state": st}
 
     def generate_drafted(self, prompt, max_new: int, drafter, pids=None, text: str = "", eos=STOP_IDS,
-                         cached: int = 0, depth: int = 1, shape: Optional[PassShape] = None) -> dict:
+                         cached: int = 0, depth: int = 1, shape: Optional[PassShape] = None,
+                         graphs: bool = False) -> dict:
         """Engine.generate with the learned drafter (Engine.swift:922-1030), device-resident: after
         the prefill, every step is k_draft (the next tree from the committed tokens and the device
         state, written into a device tree buffer) followed by one pass, both on this engine's
@@ -388,7 +427,8 @@ class VerifyEngine:
         Steps enqueued past the stop run as early exits: every kernel of a finished request
         returns at once. drafter: a DeviceDrafter on this engine's device; pids / text: the
         request context of Drafter.begin (the prompt's ids and its text), built on the host while
-        the GPU prefills. Returns the tokens (as generate), the passes, the shapes enqueued, the
+        the GPU prefills. graphs: each step is the replay of a CUDA graph of the two launches
+        (step_graph, captured once per shape for this request) instead of two library calls. Returns the tokens (as generate), the passes, the shapes enqueued, the
         host waits and the final state (passes: the verify passes that committed, as generate
         counts them)."""
         if drafter.device != self.device:
@@ -419,6 +459,7 @@ class VerifyEngine:
         shapes = []
         waits = 0
         encoded = 1  # the prefill (as Engine.generate counts it)
+        step_graphs = {}
         with torch.cuda.stream(self.stream):
             while True:
                 while pending and pending[0][0].query():
@@ -433,8 +474,13 @@ class VerifyEngine:
                 if encoded < max_new and encoded - max(seen_passes, 1) <= depth:
                     B, branch = shape.next(seen_passes, seen_acc)
                     shapes.append((B, branch))
-                    drafter.draft(tree_ptr, tok_ptr, state_ptr=st_ptr, B=B, branch=branch, stream=self._s)
-                    check(self.lib.vp_pass(self.ctx, tree_ptr, self._s), "vp_pass")
+                    if graphs:
+                        if (B, branch) not in step_graphs:
+                            step_graphs[(B, branch)] = self.step_graph(drafter, B, branch)
+                        step_graphs[(B, branch)].launch(self._s)
+                    else:
+                        drafter.draft(tree_ptr, tok_ptr, state_ptr=st_ptr, B=B, branch=branch, stream=self._s)
+                        check(self.lib.vp_pass(self.ctx, tree_ptr, self._s), "vp_pass")
                     k = encoded % slots
                     host[k].copy_(st_dev, non_blocking=True)
                     ev = torch.cuda.Event()
@@ -447,6 +493,8 @@ class VerifyEngine:
                 pending[0][0].synchronize()
                 waits += 1
         st = self.state()
+        for g in step_graphs.values():
+            g.close()
         if st["err"]:
             raise _lib.VpError(f"device error bits {st['err']}")
         if not st["done"]:

@@ -80,3 +80,16 @@ def test_step_and_sketch_argument_errors_without_device(lib):
     assert lib.vp_head_argmax_sketch(4096, d, d, d, d, 1, ctypes.c_float(6.0), d, 16, tok, None, None) == -1
     assert b"work buffer" in lib.vp_last_error()
     assert lib.vp_head_argmax_noalloc(2, 4100, d, d, d, 1, tok, None) == -1
+
+
+def test_graph_argument_errors_without_device(lib):
+    """The CUDA-graph entry points reject null arguments before any CUDA call."""
+    out = ctypes.c_void_p()
+    d = ctypes.c_void_p(256)  # never dereferenced
+    assert lib.vp_pass_graph(None, d, ctypes.byref(out)) == -1 and out.value is None
+    assert lib.vp_pass_graph(d, None, ctypes.byref(out)) == -1
+    assert lib.vp_step_graph(None, d, 15, 8, ctypes.byref(out)) == -1
+    assert lib.vp_step_graph(d, None, 15, 8, ctypes.byref(out)) == -1
+    assert lib.vp_graph_launch(None, None) == -1
+    assert b"null graph" in lib.vp_last_error()
+    lib.vp_graph_destroy(None)  # no-op

@@ -87,6 +87,19 @@ def test_drafted_decode_loop_equals_greedy_decoding():
             if rate < 1.5 and got["passes"] >= 4:
                 assert (7, 1) in shapes, (i, shapes)
             assert got["passes"] <= len(shapes) <= got["passes"] + depth + 1
+        # the same loop with each step replayed as a CUDA graph (vp_step_graph)
+        case = GOLD["cases"][1]
+        prompt = list(case["pids"])
+        ref = eng.generate(prompt, 40)
+        got = eng.generate_drafted(prompt, 40, d, pids=prompt, text=case["text"], depth=1, graphs=True)
+        assert got["tokens"] == ref["tokens"]
+        # a step graph captured for one request refuses to run after the drafter began another
+        g = eng.step_graph(d, 15, 8)
+        d.begin(prompt, case["text"])
+        from instantllm_b200 import _lib
+        with pytest.raises(_lib.VpError):
+            g.launch(eng._s)
+        g.close()
         # the non-adaptive tree loop gives the same tokens too
         prompt = list(GOLD["cases"][0]["pids"])
         fixed = eng.generate_drafted(prompt, 40, d, pids=prompt, text=GOLD["cases"][0]["text"],

@@ -263,6 +263,29 @@ def test_fused_pass_equals_separate_launches(full_q4):
     assert a["passes"] == b["passes"]
 
 
+def test_pass_graph_replays_the_pass(full_q4):
+    """vp_pass_graph: the fused pass captured once as a CUDA graph over the context's own tree
+    buffer and replayed per pass (the tree written into that buffer before each replay) commits
+    the tokens the library call does."""
+    w, eng = full_q4
+    prompt = synth.make_prompt(48, seed=78).tolist()
+    seq = eng.generate(prompt, 24)
+    tree_buf = eng.buffer(7, (synth.TREE_INTS,), "<i4")
+    g = eng.pass_graph(tree_buf)
+    try:
+        fn = _tree_fn(seq["tokens"], np.random.default_rng(5))
+        eng.begin(0, 24)
+        eng.prefill(prompt)
+        out = eng.tokens(1)
+        while not eng.state()["done"]:
+            tree_buf.copy_(torch.from_numpy(synth.tree_to_buffer(fn(out))).to(eng.device))
+            g.launch(eng._s)
+            out = eng.tokens()
+        assert out == seq["tokens"]
+    finally:
+        g.close()
+
+
 def test_config2_logits_match_oracle_full_size(full_q4):
     """Config 2 shape at full size: 256-token prefix, one 16-row tree pass."""
     w, eng = full_q4
