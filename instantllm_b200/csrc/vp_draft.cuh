@@ -30,6 +30,8 @@ constexpr int DR_N_MAX = 8;            // highest n-gram order supported
 constexpr int DR_HEAP = 8 + 16 * 8;    // best-first queue capacity (root + 15 expansions of 8)
 constexpr int DR_VOCAB = 151936;
 constexpr int DR_WORDS = (DR_VOCAB + 31) / 32;
+constexpr int DR_SUMW = (DR_WORDS + 31) / 32;  // summary bitset: which words of a token bitset are set
+static_assert(DR_SUMW <= DR_THREADS, "one thread per summary word");
 
 // feature indices (ildraft.py FEATS order)
 enum DrFeat {
@@ -112,6 +114,7 @@ constexpr int DR_SMALL = 96;   // (token, bits) of the small sources: n-gram lis
 struct DrShared {
   uint32_t used[DR_WORDS];                 // bitset of the committed output's tokens
   uint32_t mark[DR_WORDS];                 // candidate tokens of the current context
+  uint32_t msum[DR_SUMW];                  // its nonzero words
   uint32_t prm[DR_WORDS];                  // tokens after a longest prompt match (source DS_PR)
   int ctok[DR_MAX_CAND];                   // the context's distinct candidates, ascending
   uint32_t cbits[DR_MAX_CAND];             // their source bits
@@ -261,7 +264,9 @@ __device__ __forceinline__ double dr_prompt_prop(const DraftTab& T, const DraftR
 }
 // A candidate token: marked in the context's set (duplicates merge for free).
 __device__ __forceinline__ void dr_mark(DrShared& sh, int tok) {
-  if (tok >= 0 && tok < DR_VOCAB) atomicOr(&sh.mark[tok >> 5], 1u << (tok & 31));
+  if (tok < 0 || tok >= DR_VOCAB) return;
+  atomicOr(&sh.mark[tok >> 5], 1u << (tok & 31));
+  atomicOr(&sh.msum[tok >> 10], 1u << ((tok >> 5) & 31));
 }
 // A candidate from a small source, whose bits are merged after the compaction.
 __device__ __forceinline__ void dr_push_small(DrShared& sh, int tok, uint32_t bits) {
@@ -280,14 +285,15 @@ __device__ __forceinline__ int dr_suffix(const Seq& s, int e, const DrCtx& c, in
   return k;
 }
 
-// Candidates and probabilities of the next token after the context; leaves the top 8 (probability
-// descending, token ascending) in sh.top_tok / top_p (-1: fewer candidates).
+// Candidates and probabilities of the next token after the context; leaves the top ntop (<= 8;
+// probability descending, token ascending) in sh.top_tok / top_p (-1: fewer candidates or past
+// ntop).
 //
 // The candidate set is a bitset over the vocabulary (duplicates from several sources merge by
 // themselves), compacted in ascending token order by a block scan; the source bits of the large
 // sources (prompt matches, copy ids, association candidates) are set membership tests, those of the
 // small ones (n-gram lists, self match, first prompt match, votes) are merged after the compaction.
-__device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, DrShared& sh) {
+__device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, DrShared& sh, int ntop) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int L = c.L(), lo = c.lo();
   const int nmax = max(T.N, T.MAXM);
@@ -418,13 +424,12 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   for (int j = tid; j < R.nascand; j += DR_THREADS) dr_mark(sh, R.as_cand[j]);
   __syncthreads();
   DR_T(sh, 6);
-  // the distinct candidates in ascending token order: each thread counts the marks of its word
-  // range, a block scan gives its first index, it writes its tokens (and the prompt-match bit) and
-  // clears its words for the next context
-  constexpr int WPT = (DR_WORDS + DR_THREADS - 1) / DR_THREADS;
-  const int w0 = min(DR_WORDS, tid * WPT), w1 = min(DR_WORDS, w0 + WPT);
+  // the distinct candidates in ascending token order: thread t takes the set words of summary word
+  // t (32 words of the bitset), counts their marks, a block scan gives its first index, it writes
+  // its tokens (and the prompt-match bit) and clears its words for the next context
+  const uint32_t sw = tid < DR_SUMW ? sh.msum[tid] : 0u;
   int cnt = 0;
-  for (int w = w0; w < w1; ++w) cnt += __popc(sh.mark[w]);
+  for (uint32_t m = sw; m; m &= m - 1) cnt += __popc(sh.mark[tid * 32 + __ffs(m) - 1]);
   int incl = cnt;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -438,7 +443,8 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     if (w < wid) idx += sh.red_i[w];
     total += sh.red_i[w];
   }
-  for (int w = w0; w < w1; ++w) {
+  for (uint32_t sm_ = sw; sm_; sm_ &= sm_ - 1) {
+    const int w = tid * 32 + __ffs(sm_) - 1;
     uint32_t m = sh.mark[w];
     const uint32_t pm = sh.prm[w];
     while (m) {
@@ -453,6 +459,7 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     sh.mark[w] = 0u;
     sh.prm[w] = 0u;
   }
+  if (tid < DR_SUMW) sh.msum[tid] = 0u;
   const int nc = min(total, DR_MAX_CAND);  // past the cap: the lowest token ids are kept
   if (tid == 0 && total > DR_MAX_CAND) sh.capped = 1;
   __syncthreads();
@@ -618,7 +625,7 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   // bit pattern plus one (monotonic for non-negative doubles); 0 marks none (taken entries hold
   // -2.0, which is not a probability).
 #pragma unroll 1
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < ntop; ++k) {
     unsigned long long bk = 0;
     int bi = -1;
     for (int ci = tid; ci < nc; ci += DR_THREADS) {
@@ -638,10 +645,17 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   DR_T(sh, 15);
   if (wid == 0) {
     constexpr int NW = DR_THREADS / 32;  // 8 warps x 8 entries: two per lane
-    unsigned long long k0 = sh.wtop_k[lane >> 3][lane & 7], k1 = sh.wtop_k[(NW / 2) + (lane >> 3)][lane & 7];
-    int i0 = sh.wtop_i[lane >> 3][lane & 7], i1 = sh.wtop_i[(NW / 2) + (lane >> 3)][lane & 7];
+    const bool used_k = (lane & 7) < ntop;  // entries past ntop were not filled
+    unsigned long long k0 = used_k ? sh.wtop_k[lane >> 3][lane & 7] : 0ull;
+    unsigned long long k1 = used_k ? sh.wtop_k[(NW / 2) + (lane >> 3)][lane & 7] : 0ull;
+    int i0 = used_k ? sh.wtop_i[lane >> 3][lane & 7] : -1, i1 = used_k ? sh.wtop_i[(NW / 2) + (lane >> 3)][lane & 7] : -1;
+    if (lane < 8) {
+      sh.top_tok[lane] = -1;
+      sh.top_p[lane] = 0.0;
+    }
+    __syncwarp();
 #pragma unroll 1
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < ntop; ++k) {
 #ifdef VP_DRAFT_TRACE
       if (tid == 0) sh.tacc[16 + k] = clock64();
 #endif
@@ -686,6 +700,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_draft(DraftTab T, DraftReq R,
     sh.mark[i] = 0u;
     sh.prm[i] = 0u;
   }
+  if (tid < DR_SUMW) sh.msum[tid] = 0u;
   if (tid == 0) { sh.capped = 0; sh.hn = 0; sh.hctr = 0; sh.nodes = 0; }
 #ifdef VP_DRAFT_TRACE
   if (tid < 32) sh.tacc[tid] = 0ull;
@@ -758,12 +773,13 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_draft(DraftTab T, DraftReq R,
   // call site of dr_expand (the root is the expansion of node -1 with key -1: its children's keys
   // are -p exactly), so the kernel's code holds one copy of it.
   if (!done) {
+    const int ntop = O.exp_tok ? 8 : branch;  // the debug block records all 8
     int exp_i = 0;
     double key = -1.0;
     int node = -1;
     c.np = 0;
     for (;;) {
-      dr_expand(T, R, c, sh);
+      dr_expand(T, R, c, sh, ntop);
       if (tid == 0) {
         for (int k = 0; k < branch; ++k)
           if (sh.top_tok[k] >= 0 && sh.hn < DR_HEAP) {
