@@ -109,3 +109,56 @@ def test_drafted_decode_loop_equals_greedy_decoding():
     finally:
         d.close()
         eng.close()
+
+
+def test_device_drafter_long_request_matches_the_oracle():
+    """A request past the kernel's shared-memory staging caps for the prompt and the committed
+    output (both longer than 2,048 tokens; the distinct prompt ids stay under the 1,024-candidate
+    cap) takes the global-memory paths of k_draft; every expansion's 8 probabilities and the
+    probability of each token it ranks must equal the CPU oracle's (oracle/drafter.py, pinned to
+    the reference's golden record)."""
+    from instantllm_b200 import draft_table as dt
+    from instantllm_b200.drafter import DeviceDrafter
+    from oracle import drafter as D
+
+    table = os.path.join(HERE, "golden", "draft_subset.ildraft")
+    ot = D.OracleTable(dt.DraftTable.load(table))
+    d = DeviceDrafter(table)
+    rng = np.random.default_rng(11)
+    case = GOLD["cases"][0]
+    pool = rng.integers(0, 151643, size=800).tolist()
+    prompt = []
+    while len(prompt) < 4000:
+        prompt += list(case["pids"]) + [pool[i] for i in rng.integers(0, len(pool), size=60)]
+    prompt = prompt[:4000]
+    out = (list(case["steps"][-1]["out"]) * 400)[:2300]
+    assert len(set(prompt)) < 1000
+    try:
+        d.begin(prompt, case["text"])
+        req = D.Request(ot, prompt, case["text"])
+        tree = torch.zeros(65, dtype=torch.int32, device=d.device)
+        o = torch.tensor(out, dtype=torch.int32, device=d.device)
+        got = d.draft(tree, o, n_out=len(out), B=15, branch=8, debug=True)
+        assert got["status"] == 0
+        par, tok = got["parents"], got["tokens"]
+        # expansion order: the root, then every node that was neither a stop token nor the last
+        paths = [[]]
+        for i in range(len(tok)):
+            if tok[i] not in (151645, 151643) and i + 1 < 15:
+                p, v = [], i
+                while v >= 0:
+                    p.append(tok[v])
+                    v = par[v]
+                paths.append(p[::-1])
+        assert len(paths) >= 2
+        for k, path in enumerate(paths[:16]):
+            ref = req.probs(out + path)
+            gt = [int(x) for x in got["exp_tokens"][k] if x >= 0]
+            gp = got["exp_probs"][k][:len(gt)]
+            want = [p for _, p in ref[:8]]
+            assert len(gt) == len(want), (k, path)
+            assert np.allclose(gp, want, rtol=1e-9, atol=0), (k, path)
+            rd = dict(ref)
+            assert np.allclose([rd[x] for x in gt], gp, rtol=1e-9, atol=0), (k, path)
+    finally:
+        d.close()
