@@ -82,6 +82,8 @@ struct Scratch {
   uint64_t* att_ll;     // attention output for O: act blocks as (half2, flag) words [H * 16 / 2]
   uint64_t* dn_ll;      // down output for the next QKV: normed x as act blocks of (half2, flag) words
   uint64_t* dn_ss_ll;   // and its RMSNorm partials as (float, flag) words [HRB][16]
+  uint64_t* dnp_ll;     // split down projection: the second CTA's partial tile of each row-block
+                        // as (float, flag) words [HRB][128][2]
   uint32_t flag_q;      // flag of q_ll / kv_ll in this launch and layer
   float* part;          // split-K partial tiles [max units][16*16]
   int* tickets;         // split-K / attention arrival counters (self-resetting)

@@ -78,6 +78,8 @@ struct GemmParams {
   uint32_t flag;         // flag of this launch and layer
   const unsigned* gate;  // persistent kernel: flagged inputs are polled once this arrival counter
   unsigned gate_target;  // reaches gate_target (every producer CTA wrote its words), or null
+  uint64_t* part_ll_out;       // RESID, split down projection: this CTA's partial tile goes out as
+  const uint64_t* part_ll_in;  // flagged words (second CTA) / is added to the one polled here (first)
   Scratch s;
 };
 

@@ -85,12 +85,14 @@ __host__ __device__ constexpr int mk_tiles_per_slot(int fmt) { return MK_SLOT / 
 // go to CTAs 0..55 (which also keep their slice of x), QKV to the last 72 CTAs, gate/up and the
 // lm_head in equal contiguous shares over every CTA. Weights stream ahead of the stages that use
 // them, so the split balances each stage's work rather than each CTA's bytes.
+__host__ __device__ constexpr bool mk_down_split(int G) { return G >= 2 * (H / 16); }
 __host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
   rb0 = 0;
   n = 0;
   const int nh = H / 16, nq = QKV / 16, ngu = 2 * F / 16;
   if (st == MK_O || st == MK_DOWN) {
     if (cta < nh) { rb0 = cta; n = 1; }
+    else if (st == MK_DOWN && mk_down_split(G) && cta < 2 * nh) { rb0 = cta - nh; n = 1; }
   } else if (st == MK_QKV) {
     if (cta >= G - nq) { rb0 = cta - (G - nq); n = 1; }
   } else if (st == MK_GU) {
@@ -104,8 +106,26 @@ __host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int
   }
 }
 
-__host__ __device__ inline int mk_pieces(int fmt, int st, int nrb) {
-  const int tiles = nrb * mk_groups(st);
+// K-group window [g0, g0 + gn) of the row-blocks a CTA owns in stage st. The down projection is
+// the longest stage (K = 4864: 76 tiles and 152 KB of activations per row-block); when the launch
+// has 2 x 56 CTAs it runs on two CTAs per row-block: CTA r, which keeps row-block r's slice of x,
+// takes groups 0..37, CTA 56 + r groups 38..75 and hands its partial tile to CTA r as flagged words
+// (the first CTA adds it to its own: a fixed order).
+__host__ __device__ inline void mk_window(int st, int cta, int G, int& g0, int& gn) {
+  g0 = 0;
+  gn = mk_groups(st);
+  if (st == MK_DOWN && mk_down_split(G)) {
+    const int half = (F / GS) / 2;
+    if (cta < H / 16) {
+      gn = half;
+    } else {
+      g0 = half;
+      gn = F / GS - half;
+    }
+  }
+}
+__host__ __device__ inline int mk_pieces(int fmt, int nrb, int gn) {
+  const int tiles = nrb * gn;
   const int tp = mk_tiles_per_slot(fmt);
   return (tiles + tp - 1) / tp;
 }
@@ -268,12 +288,13 @@ __device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sS
   const int nst = p.n_layers * 4 + (p.do_lm ? 1 : 0);
   for (int si = 0; si < nst && ok; ++si) {
     const int l = si / 4, st = si < p.n_layers * 4 ? si % 4 : MK_LM;
-    int rb0, nrb;
+    int rb0, nrb, g0, gn;
     mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
     if (nrb == 0) continue;
+    mk_window(st, cta, G, g0, gn);
     const int ng = mk_groups(st);
-    const int tiles = nrb * ng;
-    const uint8_t* src = mk_weights(p, st, l) + (size_t)rb0 * ng * TB;
+    const int tiles = nrb * gn;  // a window narrower than the row-block only when nrb == 1
+    const uint8_t* src = mk_weights(p, st, l) + ((size_t)rb0 * ng + g0) * TB;
     for (int t0 = 0; t0 < tiles && ok; t0 += tp, ++k) {
       const int slot = k % MK_NSLOT;
       if (k >= MK_NSLOT) {
@@ -642,6 +663,27 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
       s0 += part[q * 256 + t * 8 + rp];
       s1 += part[q * 256 + 128 + t * 8 + rp];
     }
+    if constexpr (MODE == MODE_RESID) {
+      if (gp.part_ll_out) {  // second CTA of a split down projection: its partial goes to the first
+        st_flagged(gp.part_ll_out + (size_t)rb * 256 + lt * 2, __float_as_uint(s0), gp.flag);
+        st_flagged(gp.part_ll_out + (size_t)rb * 256 + lt * 2 + 1, __float_as_uint(s1), gp.flag);
+        continue;  // uniform over the CTA
+      }
+      if (gp.part_ll_in) {  // first CTA: add the second CTA's partial (bounded poll)
+        const uint64_t* w = gp.part_ll_in + (size_t)rb * 256 + lt * 2;
+        uint64_t a = 0, b = 0;
+        bool got = false;
+        const unsigned long long t0 = globaltimer();
+        for (uint32_t it = 0; it < (1u << 26); ++it) {
+          ld_flagged2(w, a, b);
+          if ((uint32_t)(a >> 32) == gp.flag && (uint32_t)(b >> 32) == gp.flag) { got = true; break; }
+          if ((it & 15) == 15 && globaltimer() - t0 > WAIT_NS) break;
+        }
+        if (!got) set_error(s.st, VP_DEV_ERR_TIMEOUT);
+        s0 = s0 + (got ? __uint_as_float((uint32_t)a) : 0.f);
+        s1 = s1 + (got ? __uint_as_float((uint32_t)b) : 0.f);
+      }
+    }
     if constexpr (MODE == MODE_QKV) {
       const int head = rb >> 2, d = (rb & 3) * 8 + rp;
       float a = 0.f, b = 0.f;
@@ -785,10 +827,11 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   float* sX = reinterpret_cast<float*>(smem + MK_OFF_X);
   float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
   float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
-  int rb0, nrb;
+  int rb0, nrb, g0, ng;
   mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
   if (nrb == 0) return true;
-  const int P = mk_parts(st, nrb), ng = mk_groups(st);
+  mk_window(st, cta, G, g0, ng);
+  const int P = mk_parts(st, nrb);
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
   constexpr bool down = DOWN;
@@ -868,7 +911,7 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
 
   const int npieces = (nrb * ng + tp - 1) / tp;
   MkJobs J;
-  J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.actg = gp.act;
+  J.piece0 = piece0; J.rb0 = rb0; J.nrb = nrb; J.P = P; J.ng = ng; J.actg = gp.act + (size_t)g0 * 1024;
   float* const sJobPart = sPart + (MODE == MODE_QKV || MODE == MODE_SILU ? MK_SS_SLOTS * 256 : 0);
   J.part = sJobPart;
   J.gsum = (kGsums && MODE != MODE_ARGMAX) ? rg.gsum : nullptr;
@@ -988,9 +1031,10 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     rg.gs_phase = 0;
     int piece0 = 0;
     auto pieces = [&](int st) {
-      int rb0, nrb;
+      int rb0, nrb, g0, gn;
       mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
-      return mk_pieces(FMT, st, nrb);
+      mk_window(st, cta, G, g0, gn);
+      return mk_pieces(FMT, nrb, gn);
     };
 
     if (live) {
@@ -1063,10 +1107,15 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
         gp.w = p.wd[l]; gp.act = s.act_f; gp.nrb = H / 16; gp.ng = F / GS;
         gp.wnext = last ? p.final_norm : p.ln1[l + 1];
         const bool to_lm = last && p.do_lm;
+        gp.flag = flag0 + l;
         if (to_lm) {
           gp.ss_out = s.ss; gp.act_out = s.act_h;
         } else {
-          gp.act_ll_out = s.dn_ll; gp.ss_ll_out = s.dn_ss_ll; gp.flag = flag0 + l;
+          gp.act_ll_out = s.dn_ll; gp.ss_ll_out = s.dn_ss_ll;
+        }
+        if (mk_down_split(G)) {
+          if (own_x) gp.part_ll_in = s.dnp_ll;
+          else gp.part_ll_out = s.dnp_ll;
         }
         gp.xs = own_x ? sXrb : nullptr;
         ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G);

@@ -293,6 +293,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
       (r = dalloc(c, &s.att_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
       (r = dalloc(c, &s.dn_ll, (size_t)H * ROWS / 2 * sizeof(uint64_t))) ||
       (r = dalloc(c, &s.dn_ss_ll, (size_t)HRB * ROWS * sizeof(uint64_t))) ||
+      (r = dalloc(c, &s.dnp_ll, (size_t)HRB * 256 * sizeof(uint64_t))) ||
       (r = dalloc(c, &c->gate, MK_GATES * sizeof(unsigned))) ||
       (r = dalloc(c, &c->lm_pval, (size_t)ROWS * sms * sizeof(float))) ||
       (r = dalloc(c, &c->lm_pidx, (size_t)ROWS * sms * sizeof(int))) ||
