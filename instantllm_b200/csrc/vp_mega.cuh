@@ -60,12 +60,14 @@ enum MkStage { MK_QKV = 0, MK_O = 1, MK_GU = 2, MK_DOWN = 3, MK_LM = 4 };
 // down-projection CTAs that have written their flagged outputs.
 enum MkGate { MK_GATE_ATT = 0, MK_GATE_DOWN = 1, MK_GATES = 2 };
 // Arrival count at which the consumers of a stage with `count` producers per layer start polling
-// the flagged words of layer l: half of the producers. The producers of a stage finish within a
-// fraction of a microsecond of each other, so by then the rest of the words are landing; polling
-// the words directly from there saves the second L2 round trip of a full gate (counter, then
-// data), and waiting for half keeps the polls from loading L2 while the producer stage runs.
+// the flagged words of layer l: every producer of the layers before, which is always true by then,
+// so the wait is one L2 round trip and a CTA barrier before the first poll. Measured on the
+// config-2 pass (same box, interleaved runs): this 21.4 us per layer; waiting for 1/8, 1/4, 1/2 or
+// all of layer l's producers 22.0, 22.1, 22.1 and 22.7; no counter at all 22.1; the producers'
+// arrivals without the consumers' wait 21.9, the consumers' wait without arrivals 21.8. Both the
+// producer's CTA barrier + add and the consumer's round trip + barrier before it polls help.
 __device__ __forceinline__ unsigned mk_gate_target(int l, int count) {
-  return (unsigned)((l + 1) * count - count / 2);
+  return (unsigned)(l * count);
 }
 
 // Parts per row-block (K split across the warps of one CTA) of a GEMM stage whose CTA owns nrb
@@ -204,9 +206,8 @@ __device__ bool grid_barrier(const MegaParams& p, unsigned long long target, int
 
 // Gated flagged transport: a producer CTA writes its outputs as flagged words, then (after a CTA
 // barrier) adds one to the stage's arrival counter with a relaxed atomic: no fence, since every
-// word carries its own flag. A consumer CTA polls that one counter (one thread) until enough
-// producers arrived (mk_gate_target) and only then polls the words themselves, so that the
-// consumers do not flood L2 with polls of the data while the producer stage still runs.
+// word carries its own flag. A consumer CTA polls that one counter (one thread) until the target
+// of mk_gate_target and only then polls the words themselves.
 __device__ __forceinline__ void gate_arrive(unsigned* ctr) {
   asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
 }
