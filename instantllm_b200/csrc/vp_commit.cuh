@@ -73,26 +73,34 @@ __device__ void commit_body(const Scratch& s, const float* pval, const int* pidx
         cur = c;
       }
     }
-    st->passes += 1;
-    st->accepted += m;
-    bool stop = false;
-    int last = st->last_token, nc = 0;
+    // the state is read once and written back once: the serial part runs on registers (through
+    // the pointer every field access would be a dependent round trip, since the token stores
+    // below may alias it)
+    const int pos = __ldcg(&st->pos), step0 = __ldcg(&st->step), eos0 = __ldcg(&st->eos0);
+    const int eos1 = __ldcg(&st->eos1), maxsteps = __ldcg(&st->maxsteps), advance = __ldcg(&st->advance);
+    const int passes = __ldcg(&st->passes), accepted = __ldcg(&st->accepted);
+    bool stop = false, overflow = false;
+    int last = __ldcg(&st->last_token), nc = 0, step = step0;
     for (int i = 0; i <= m && !stop; ++i) {
       const int tok = g[i == 0 ? 0 : path[i - 1]];
-      if (st->step >= s.max_steps) { atomicOr(&st->err, VP_DEV_ERR_STEPS); stop = true; break; }
-      s.out_tokens[st->step] = tok;
+      if (step >= s.max_steps) { overflow = true; stop = true; break; }
+      s.out_tokens[step] = tok;
       if (s.pass_tok) s.pass_tok[nc] = tok;
       ++nc;
-      st->step += 1;
+      ++step;
       last = tok;
-      if (tok == st->eos0 || tok == st->eos1 || st->step >= st->maxsteps) stop = true;
+      if (tok == eos0 || tok == eos1 || step >= maxsteps) stop = true;
     }
     if (s.pass_tok)
       for (int i = nc; i < ROWS; ++i) s.pass_tok[i] = -1;
-    sPos0 = st->pos;
+    sPos0 = pos;
     sNpath = tree ? m : 0;
-    st->pos += ri->mode == 1 ? st->advance : m + 1;
+    st->passes = passes + 1;
+    st->accepted = accepted + m;
+    st->step = step;
+    st->pos = pos + (ri->mode == 1 ? advance : m + 1);
     st->last_token = last;
+    if (overflow) atomicOr(&st->err, VP_DEV_ERR_STEPS);
     if (stop) st->done = 1;
   }
   cons_sync();
