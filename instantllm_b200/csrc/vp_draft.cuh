@@ -285,6 +285,28 @@ __device__ __forceinline__ int dr_suffix(const Seq& s, int e, const DrCtx& c, in
   return k;
 }
 
+// acc[j] += W[(h + j) * DR_F + f] * x[f] for the features f in [F0, F1), in feature order.
+template <int F0, int F1, int J>
+__device__ __forceinline__ void dr_dot(const double* W, int h, const double (&x)[DR_F], double (&acc)[J]) {
+#pragma unroll
+  for (int f = F0; f < F1; ++f)
+#pragma unroll
+    for (int j = 0; j < J; ++j) acc[j] = fma(W[(h + j) * DR_F + f], x[f], acc[j]);
+}
+// The same over every feature group that can be nonzero (see the MLP in dr_expand).
+template <int J>
+__device__ __forceinline__ void dr_dot_groups(const double* W, int h, const double (&x)[DR_F], double (&acc)[J],
+                                              bool has_nb, bool has_as) {
+  dr_dot<0, F_NB_SUM, J>(W, h, x, acc);
+  if (has_nb) dr_dot<F_NB_SUM, F_IS_STOP, J>(W, h, x, acc);
+  dr_dot<F_IS_STOP, F_AGREE_NG_NB, J>(W, h, x, acc);
+  if (has_nb) dr_dot<F_AGREE_NG_NB, F_CP_PROP, J>(W, h, x, acc);
+  dr_dot<F_CP_PROP, F_AS_MAX, J>(W, h, x, acc);
+  if (has_as) dr_dot<F_AS_MAX, F_ED_SUM, J>(W, h, x, acc);
+}
+static_assert(F_NB_SUM < F_IS_STOP && F_IS_STOP < F_AGREE_NG_NB && F_AGREE_NG_NB < F_CP_PROP &&
+              F_CP_PROP < F_AS_MAX && F_AS_MAX < F_ED_SUM && F_ED_SUM + 4 == DR_F, "feature groups in order");
+
 // Candidates and probabilities of the next token after the context; leaves the top ntop (<= 8;
 // probability descending, token ascending) in sh.top_tok / top_p (-1: fewer candidates or past
 // ntop).
@@ -479,6 +501,7 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
   const double open_fence = (out_first == 73594 || out_first == 13874) ? 1.0 : 0.0;
   const double open_tick = out_first == 63 ? 1.0 : 0.0;
   const double st_len = (double)min(lo, 32) / 32.0;
+  const bool has_nb = R.nnb > 0, has_as = R.nas > 0 || R.nascand > 0;
   const double* W1 = sh.mlpd;
   const double* b1 = W1 + T.H * DR_F;
   const double* W2 = b1 + T.H;
@@ -582,30 +605,29 @@ __device__ void dr_expand(const DraftTab& T, const DraftReq& R, const DrCtx& c, 
     }
     DR_T(sh, 11);
     // score = W2 . relu(W1 x + b1) + b2 + WL . x; eight hidden units at a time (each one its own
-    // chain in feature order, the units summed in order)
+    // chain in feature order, the units summed in order). Feature groups that are zero for every
+    // candidate of the request are left out of the chains (a zero term leaves an fma chain's value
+    // unchanged): the neighbour votes and their agreements without neighbours, the association
+    // features without an association map, and the edited-neighbour features always (they need the
+    // tokenizer, which this build does not have, so they are zero as in the oracle).
     double s = 0.0;
     int h = 0;
     for (; h + 8 <= T.H; h += 8) {
       double a[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) a[j] = 0.0;
-#pragma unroll
-      for (int f = 0; f < DR_F; ++f)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a[j] = fma(W1[(h + j) * DR_F + f], x[f], a[j]);
+      dr_dot_groups<8>(W1, h, x, a, has_nb, has_as);
 #pragma unroll
       for (int j = 0; j < 8; ++j) s = fma(W2[h + j], fmax(a[j] + b1[h + j], 0.0), s);
     }
     for (; h < T.H; ++h) {
-      double a = 0.0;
-#pragma unroll
-      for (int f = 0; f < DR_F; ++f) a = fma(W1[h * DR_F + f], x[f], a);
-      s = fma(W2[h], fmax(a + b1[h], 0.0), s);
+      double a[1] = {0.0};
+      dr_dot_groups<1>(W1, h, x, a, has_nb, has_as);
+      s = fma(W2[h], fmax(a[0] + b1[h], 0.0), s);
     }
-    double lin = 0.0;
-#pragma unroll
-    for (int f = 0; f < DR_F; ++f) lin = fma(WL[f], x[f], lin);
-    sh.prob[ci] = s + b2 + lin;
+    double lin[1] = {0.0};
+    dr_dot_groups<1>(WL, 0, x, lin, has_nb, has_as);
+    sh.prob[ci] = s + b2 + lin[0];
     DR_T(sh, 13);
   }
   __syncthreads();
