@@ -2,15 +2,18 @@
 //
 // Replaces the reference's per-dispatch pass encoder (Engine.encodeWidePass, Engine.swift:567-579:
 // 171 Metal dispatches per pass) with one cooperative kernel, one CTA per SM:
-//  * stages are separated by a grid barrier (64-bit arrival counter, bounded spin);
+//  * a stage hands its outputs to the next as flagged words (data and flag in one 8-byte store)
+//    that the consumers poll; one grid barrier per layer (64-bit arrival counter, bounded spin)
+//    remains, after gate/up;
 //  * a producer warp streams the CTA's weights for the whole pass, in consumption order, as
 //    contiguous pieces of up to 28 KiB (cp.async.bulk) into a 5-slot shared-memory ring with
 //    full / empty mbarriers. Weights never depend on activations, so the stream runs up to the
 //    ring's depth ahead, across stage boundaries, and overlaps the barrier and activation latency
 //    of the dependent chain. Copies are few and large: each bulk-copy issue occupies the SM's copy
 //    path for a few hundred cycles whatever its size;
-//  * each CTA owns a contiguous row-block range of every GEMM, chosen so that all SMs stream about
-//    the same bytes per layer; a row-block's K groups are split into a fixed number of parts that
+//  * each CTA owns a contiguous row-block range of every GEMM stage it takes part in (the down
+//    projection's row-blocks split in two K halves over two CTAs); a row-block's K groups are
+//    split into a fixed number of parts that
 //    different consumer warps process and that are summed in part order in shared memory;
 //  * per-row arithmetic is a fixed function of the inputs (fixed parts, fixed group order, fixed
 //    attention chunks), so tree rows reproduce 1-row passes bit for bit.
