@@ -286,9 +286,14 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
     """BASELINE config 5 on this rank: its share of the requests (prefixes uniform in 128-2048,
     shard.assign), each prefilled, decoded sequentially with 1-row passes (untimed: the true
     continuation the seeded trees draft from), then decoded again with 16-row tree passes to 64
-    tokens. Only the tree passes are timed (CUDA events around each request's passes, all enqueued
-    at once from device-resident trees); the committed tokens are checked against the sequential
-    run (tree == sequential)."""
+    tokens in two serving modes over the same requests and trees:
+    - one request per launch (vp_pass on all SMs);
+    - two per launch (vp_pass_multi over the pairs of shard.pairs, each request on half of the
+      SMs to its end: once one request of a pair has its tokens, the other's remaining passes run
+      alone on their half; the odd request out of a rank runs on all SMs).
+    Only the tree passes are timed (CUDA events around each request's or pair's passes, all enqueued
+    at once from device-resident trees); the committed tokens of each mode are checked against the
+    sequential 1-row passes of the same mode (tree == sequential)."""
     import torch
 
     from instantllm_b200 import shard, synth
@@ -300,19 +305,12 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
     mine = shard.assign(prefixes, world)[rank]
     if w is None:
         w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
-    eng = VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local)
+    engs = [VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local) for _ in range(2)]
     no_eos = (-1, -1)
     tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
-    s = eng.stream
-    dev_ms, tokens, passes, kv_slots, ok = 0.0, 0, 0, 0, True
-    for i in mine:
-        prompt = synth.make_prompt(prefixes[i], seed=5000 + i)
-        eng.begin(0, GEN + 9, no_eos)
-        eng.prefill(prompt)
-        snap = eng.snapshot()
-        for _ in range(GEN + 8):
-            eng.pass_device(tree1)
-        y = eng.tokens(GEN + 9)
+    s = engs[0].stream  # both engines run on the device's current stream
+
+    def plan(i, y):
         # trees planned from the true continuation; the device follows the planned acceptances
         trees, counts, pos = plan_trees(y, 1, 1, args.seed * 7 + i)
         bufs, cnts = [trees[0]], [counts[0]]
@@ -320,35 +318,104 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
             t, c, _ = plan_trees(y, 1 + sum(cnts), 1, args.seed * 7 + i * 1009 + len(bufs))
             bufs.append(t[0])
             cnts.append(c[0])
-        tb = torch.tensor(np.stack(bufs), device=dev)
-        eng.restore(snap)  # back to the post-prefill state over the same cached prefix
+        return dict(i=i, y=y, tb=torch.tensor(np.stack(bufs), device=dev), cnts=cnts)
+
+    def prepare(eng, i):
+        prompt = synth.make_prompt(prefixes[i], seed=5000 + i)
+        eng.begin(0, GEN + 9, no_eos)
+        eng.prefill(prompt)
+        snap = eng.snapshot()
+        for _ in range(GEN + 8):
+            eng.pass_device(tree1)
+        return dict(plan(i, eng.tokens(GEN + 9)), snap=snap)
+
+    def timed(fn):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
-        for k in range(len(bufs)):
-            eng.pass_device(tb[k])
+        fn()
         e1.record(s)
         torch.cuda.synchronize()
-        dev_ms += e0.elapsed_time(e1)
+        return e0.elapsed_time(e1)
+
+    def check_out(eng, rq):
         st = eng.state()
-        got = eng.tokens(st["step"])
-        ok = ok and got == y[:st["step"]] and st["step"] >= GEN
-        tokens += st["step"] - 1  # the first token comes from the prefill
-        passes += len(bufs)
-        kv_slots += sum(prefixes[i] + 1 + sum(cnts[:k]) + ROWS for k in range(len(bufs)))
-    eng.close()
-    return dict(ms=dev_ms, tok=tokens, passes=passes, kv_slots=kv_slots, ok=ok, n=len(mine))
+        return eng.tokens(st["step"]) == rq["y"][:st["step"]] and st["step"] >= GEN, st["step"] - 1
+
+    ms1, ms2, tokens, tokens2, passes, launches2, kv_slots, ok, differ = 0.0, 0.0, 0, 0, 0, 0, 0, True, 0
+    for pair in shard.pairs(mine, prefixes):
+        reqs = [prepare(engs[k], i) for k, i in enumerate(pair)]
+        # one request per launch
+        for eng, rq in zip(engs, reqs):
+            eng.restore(rq["snap"])  # back to the post-prefill state over the same cached prefix
+            tb = rq["tb"]
+            ms1 += timed(lambda: [eng.pass_device(tb[k]) for k in range(len(tb))])
+            good, tok = check_out(eng, rq)
+            ok = ok and good
+            tokens += tok  # the first token comes from the prefill
+            passes += len(tb)
+            n, p = len(rq["cnts"]), prefixes[rq["i"]]
+            kv_slots += sum(p + 1 + sum(rq["cnts"][:k]) + ROWS for k in range(n))
+        # two per launch
+        if len(reqs) == 1:  # the odd request out runs alone on all SMs, as above
+            ms2 += timed(lambda: [engs[0].pass_device(reqs[0]["tb"][k]) for k in range(len(reqs[0]["tb"]))])
+            launches2 += len(reqs[0]["tb"])
+            good, tok = check_out(engs[0], reqs[0])
+            ok = ok and good
+            tokens2 += tok
+            continue
+        # A request of a pair stays on its half of the SMs to its end (vp_pass_multi with n = 1 once
+        # its partner is done): the half-SM pass sums the down projection's K halves in another
+        # order than the whole-GPU pass, so its truth is its own 1-row passes on its half.
+        for eng, rq in zip(engs, reqs):
+            eng.restore(rq["snap"])
+        for _ in range(GEN + 8):
+            VerifyEngine.pass_multi(engs, [tree1, tree1])
+        halves = []
+        for eng, rq in zip(engs, reqs):
+            y2 = eng.tokens(GEN + 9)
+            differ += y2 != rq["y"]
+            halves.append(rq if y2 == rq["y"] else plan(rq["i"], y2))
+            eng.restore(rq["snap"])
+        a, b = halves[0]["tb"], halves[1]["tb"]
+
+        def run_pair():
+            for k in range(max(len(a), len(b))):
+                if k < len(a) and k < len(b):
+                    VerifyEngine.pass_multi(engs, [a[k], b[k]])
+                elif k < len(a):
+                    VerifyEngine.pass_multi(engs[:1], [a[k]])
+                else:
+                    VerifyEngine.pass_multi(engs[1:], [b[k]])
+
+        ms2 += timed(run_pair)
+        launches2 += max(len(a), len(b))
+        for eng, rq in zip(engs, halves):
+            good, tok = check_out(eng, rq)
+            ok = ok and good
+            tokens2 += tok
+    for e in engs:
+        e.close()
+    return dict(ms=ms1, ms2=ms2, tok=tokens, tok2=tokens2, passes=passes, launches2=launches2,
+                kv_slots=kv_slots, ok=ok, n=len(mine), differ=differ)
 
 
 def config5_table(args, r, world):
-    """Per-rank config-5 figures gathered on every rank: [device ms, tokens, passes, ok, GB/s]."""
+    """Per-rank config-5 figures gathered on every rank: [device ms one request per launch, tokens,
+    passes, ok, GB/s, device ms two per launch, GB/s two per launch, launches two per launch,
+    tokens two per launch, requests whose half-SM truth differs from the whole-GPU one]."""
     import torch
 
     from instantllm_b200 import synth
 
     wbytes = synth.weight_bytes("q4", args.layers)
-    gbs = (r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24) / (max(r["ms"], 1e-9) * 1e-3) / 1e9
-    vals = [r["ms"], float(r["tok"]), float(r["passes"]), 1.0 if r["ok"] else 0.0, gbs]
+    # every request's pass streams the weights once in both modes (each half of a two-request
+    # launch streams its own copy), so both modes move the same bytes
+    nbytes = r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24
+    gbs = nbytes / (max(r["ms"], 1e-9) * 1e-3) / 1e9
+    gbs2 = nbytes / (max(r["ms2"], 1e-9) * 1e-3) / 1e9
+    vals = [r["ms"], float(r["tok"]), float(r["passes"]), 1.0 if r["ok"] else 0.0, gbs, r["ms2"], gbs2,
+            float(r["launches2"]), float(r["tok2"]), float(r["differ"])]
     if world > 1:
         rows = [torch.zeros(len(vals), dtype=torch.float64) for _ in range(world)]
         torch.distributed.all_gather(rows, torch.tensor(vals, dtype=torch.float64))
@@ -357,11 +424,21 @@ def config5_table(args, r, world):
 
 
 def config5_summary(table, n_requests) -> dict:
-    ms = max(t[0] for t in table)
+    """Two requests per launch is the serving mode of the headline value; one request per launch,
+    on the same requests and trees, is reported beside it."""
     tok = sum(t[1] for t in table)
-    return {"value": tok / (ms * 1e-3), "unit": "tok/s", "requests": n_requests, "tokens": int(tok),
-            "passes": int(sum(t[2] for t in table)), "ms_per_rank": [round(t[0], 3) for t in table],
-            "per_gpu_hbm_gbs": [round(t[4], 1) for t in table],
+    tok2 = sum(t[8] for t in table)
+    ms1 = max(t[0] for t in table)
+    ms2 = max(t[5] for t in table)
+    return {"value": tok2 / (ms2 * 1e-3), "unit": "tok/s", "requests": n_requests, "tokens": int(tok2),
+            "requests_per_launch": 2, "launches": int(sum(t[7] for t in table)),
+            "half_sm_truth_differs": int(sum(t[9] for t in table)),
+            "ms_per_rank": [round(t[5], 3) for t in table],
+            "per_gpu_hbm_gbs": [round(t[6], 1) for t in table],
+            "one_request_per_launch": {"value": tok / (ms1 * 1e-3), "unit": "tok/s", "tokens": int(tok),
+                                       "passes": int(sum(t[2] for t in table)),
+                                       "ms_per_rank": [round(t[0], 3) for t in table],
+                                       "per_gpu_hbm_gbs": [round(t[4], 1) for t in table]},
             "tree_equals_sequential": all(t[3] > 0 for t in table)}
 
 
@@ -369,19 +446,14 @@ def main_config5(args, rank, world):
     r = run_config5(args, rank, world, int(os.environ.get("LOCAL_RANK", str(rank))))
     table = config5_table(args, r, world)
     if rank == 0:
-        ms = max(t[0] for t in table)
-        tok = sum(t[1] for t in table)
         line = {
             "metric": "config 5: aggregate accepted tok/s of independent q4 requests (16-row tree passes)",
-            "value": tok / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
-            "scaling": "strong", "requests": args.requests, "tokens": int(tok),
-            "passes": int(sum(t[2] for t in table)),
-            "ms_per_rank": [round(t[0], 3) for t in table],
-            "per_gpu_hbm_gbs": [round(t[4], 1) for t in table],
-            "tree_equals_sequential": all(t[3] > 0 for t in table),
+            "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            **config5_summary(table, args.requests),
             "config": {"workload": "BASELINE config 5: requests with prefixes uniform in [128, 2048], "
                                    "64 tokens each, seeded 16-row trees as in config 2, "
-                                   "longest-processing-time-first sharding (no collective)",
+                                   "longest-processing-time-first sharding (no collective), two "
+                                   "requests per launch (vp_pass_multi) and one per launch",
                        "layers": args.layers, "timed": "tree passes only (device time, max over ranks)"},
             "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
         }
@@ -991,8 +1063,9 @@ def main():
         if rank == 0:
             line["config5"] = dict(config5_summary(table, args.c5_requests), scaling="strong",
                                    workload="BASELINE config 5: prefixes uniform in [128, 2048], 64 tokens "
-                                            "each, seeded 16-row trees; device time of the tree passes, "
-                                            "max over ranks")
+                                            "each, seeded 16-row trees; two requests per launch "
+                                            "(vp_pass_multi) and one per launch on the same requests; "
+                                            "device time of the tree passes, max over ranks")
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -45,3 +45,13 @@ def config5_requests(n: int = 256, seed: int = 5, lo: int = 128, hi: int = 2048)
     """Prefix lengths of config 5: n requests with prefixes uniform in [lo, hi]."""
     rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, 55])))
     return [int(v) for v in rng.integers(lo, hi + 1, size=n)]
+
+
+def pairs(indices, prefixes) -> list:
+    """A rank's requests grouped two per launch (vp_pass_multi puts each request of a pair on half
+    of the SMs, and the launch lasts as long as its slower half): sorted by prefix length, longest
+    first, and paired with their neighbours, so the two halves of a launch read KV prefixes of
+    similar length. An odd request out is the last, shortest one, alone. Deterministic: ties broken
+    by index."""
+    order = sorted(indices, key=lambda i: (-prefixes[i], i))
+    return [tuple(order[k:k + 2]) for k in range(0, len(order), 2)]

@@ -74,6 +74,48 @@ def test_two_requests_per_launch_tree_equals_sequential():
     eb.close()
 
 
+def test_long_prefixes_two_per_launch_then_one_on_its_half():
+    """Rows past the 320 positions of one attention segment (the segmented path), two requests of
+    different prefix lengths per launch, then the survivor alone on its half: tree == sequential."""
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=2, vocab=V, seed=63)
+    engs, snaps = [], []
+    for k, n in enumerate((700, 1400)):
+        eng = VerifyEngine(w, max_ctx=1600, max_steps=96)
+        eng.begin(0, 64, (-1, -1))
+        eng.prefill((synth.make_prompt(n, seed=70 + k) % V).tolist())
+        engs.append(eng)
+        snaps.append(eng.snapshot())
+    ea, eb = engs
+    root = _root(ea)
+    for _ in range(56):  # enough truth for 5 passes of up to 9 committed tokens each
+        VerifyEngine.pass_multi(engs, [root, root])
+    ys = [e.tokens(57) for e in engs]
+    for e, sn in zip(engs, snaps):
+        assert e.state()["err"] == 0
+        e.restore(sn)
+    rng = np.random.default_rng(63)
+
+    def step(which):
+        st0 = [engs[i].state() for i in which]
+        trees = [synth.seeded_tree(rng, ys[i][s["step"]:s["step"] + 9], n=16, vocab=V) for i, s in zip(which, st0)]
+        VerifyEngine.pass_multi([engs[i] for i in which],
+                                [torch.tensor(synth.tree_to_buffer(t), device=ea.device) for t in trees])
+        for i, s, t in zip(which, st0, trees):
+            st = engs[i].state()
+            parents, tokens = A.to_python_numbering(t)
+            assert st["step"] == s["step"] + A.accept_tree(parents, tokens, ys[i], s["step"]) + 1
+            assert engs[i].tokens(st["step"]) == ys[i][:st["step"]]
+
+    for _ in range(3):
+        step([0, 1])
+    for _ in range(2):
+        step([1])
+    for e in engs:
+        e.close()
+
+
 def test_pass_multi_rejects_bad_arguments():
     import ctypes
 

@@ -83,3 +83,19 @@ def test_adaptive_pass_shape_follows_the_reference_rule():
     assert [s.next(p, 0) for p in (1, 2, 3)] == [(9, 8), (9, 8), (3, 1)]
     s.reset()
     assert s.hist == [] and s.next(7, 0) == (9, 8)
+
+
+def test_config5_summary_takes_the_max_over_ranks_in_each_mode():
+    import bench
+
+    # [ms one per launch, tokens, passes, ok, GB/s, ms two per launch, GB/s two, launches two,
+    #  tokens two, half-SM truths that differ]
+    table = [[100.0, 500.0, 200.0, 1.0, 300.0, 70.0, 430.0, 110.0, 501.0, 1.0],
+             [120.0, 520.0, 210.0, 1.0, 290.0, 80.0, 435.0, 115.0, 520.0, 0.0]]
+    s = bench.config5_summary(table, 16)
+    assert s["value"] == 1021 / 0.080 and s["requests_per_launch"] == 2 and s["launches"] == 225
+    assert s["half_sm_truth_differs"] == 1 and s["tokens"] == 1021
+    assert s["one_request_per_launch"]["value"] == 1020 / 0.120
+    assert s["one_request_per_launch"]["passes"] == 410 and s["tree_equals_sequential"]
+    table[1][3] = 0.0
+    assert not bench.config5_summary(table, 16)["tree_equals_sequential"]

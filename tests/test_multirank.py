@@ -67,6 +67,18 @@ def test_assignment_is_a_balanced_partition():
         assert max(loads) - min(loads) <= max(shard.request_cost(p) for p in prefixes)
 
 
+def test_pairs_cover_a_rank_and_match_neighbouring_lengths():
+    prefixes = shard.config5_requests(n=64)
+    for world in (1, 2, 8):
+        for mine in shard.assign(prefixes, world):
+            ps = shard.pairs(mine, prefixes)
+            assert sorted(i for p in ps for i in p) == sorted(mine)
+            assert all(len(p) == 2 for p in ps[:-1]) and len(ps[-1]) == (2 if len(mine) % 2 == 0 else 1)
+            lens = [prefixes[i] for p in ps for i in p]
+            assert lens == sorted(lens, reverse=True)  # longest first, neighbours together
+    assert shard.pairs([3, 1, 2], [10, 30, 30, 20]) == [(1, 2), (3,)]
+
+
 def test_two_gloo_ranks_agree_on_the_partition():
     res = _run(2)
     (r0, g0, s0), (r1, g1, s1) = res
