@@ -42,11 +42,13 @@ static_assert(MK_SS_SLOTS * 256 >= HRB * 16 && MK_SS_SLOTS + 16 <= MK_PART_SLOTS
 // events 8 * stage + step for the GEMM stages (step 0 entry, 1 inputs in shared memory, 2 group
 // sums, 3 jobs done, 4 pieces released, 5 epilogue done), 40 / 41 / 42 attention unit start /
 // records done / combined, 48 + 2k / 49 + 2k arrival at / exit from the k-th grid barrier of the
-// layer, 56 layer start.
+// layer, 56 layer start, 64.. the attention units' steps, 192.. the down projection's tiles, and
+// 288 + (warp * 5 + round) * 3 + s the lm_head jobs of each warp (s = 0 start, 1 first piece in
+// the ring, 2 folded).
 constexpr int MK_TRACE_BASE = 2048;
 constexpr int MK_TRACE_LAYER = 5;
 #ifdef VP_TRACE_DETAIL
-constexpr int MK_TRACE = MK_TRACE_BASE + (64 + 16 * 8 + 96) * 256;
+constexpr int MK_TRACE = MK_TRACE_BASE + (64 + 16 * 8 + 96 + 16 * 5 * 3) * 256;
 #define MK_CSTAMP(p, cond, ev)                                                                   \
   do {                                                                                           \
     if ((p).trace && threadIdx.x == 0 && (cond) && blockIdx.x < 256)                             \
@@ -509,6 +511,12 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
     const int i = j / P, q = j % P;
     const int ga = q * ng / P, gb = (q + 1) * ng / P;
     float acc[2][4] = {};
+#ifdef VP_TRACE_DETAIL
+    unsigned long long* ltr = (KIND == JOB_ARGMAX && J.trace && j / MK_WARPS < 5 && lane == 0)
+                                  ? J.trace + MK_TRACE_BASE + (size_t)(288 + (warp * 5 + j / MK_WARPS) * 3) * 256 + blockIdx.x
+                                  : nullptr;
+    if (ltr) ltr[0] = globaltimer();
+#endif
     if constexpr (down) {
       // one tile per step, software-pipelined: the act blocks of tiles g + 1 and g + 2 stream from
       // L2 into this warp's two staging buffers (cp.async, each lane its own fragments) while tile
@@ -567,6 +575,9 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
         if (!mk_release(rg, k, lane)) { ok = false; break; }
         const uint8_t* base = mk_piece(rg, k);
         if (!base) { ok = false; break; }
+#ifdef VP_TRACE_DETAIL
+        if (ltr && g == ga) ltr[256] = globaltimer();
+#endif
         const uint8_t* t0 = base + (size_t)(idx % tp) * TB;
         if (g + 1 < gb) {
           const int k1 = piece0 + (idx + 1) / tp;
@@ -606,6 +617,9 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
             if (bv > mv || (bv == mv && bi < mi)) { mv = bv; mi = bi; }
           }
         }
+#ifdef VP_TRACE_DETAIL
+      if (ltr) ltr[512] = globaltimer_after(sLmV[warp * 16]);
+#endif
     } else {
       float* part = sPart + j * 256;
 #pragma unroll
@@ -920,7 +934,11 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   J.part = sJobPart;
   J.gsum = (kGsums && MODE != MODE_ARGMAX) ? rg.gsum : nullptr;
   J.gs_parity = rg.gs_phase & 1u;
-  J.trace = (gp.layer == MK_TRACE_LAYER && MODE != MODE_ARGMAX) ? p.trace : nullptr;
+#ifdef VP_TRACE_DETAIL
+  J.trace = (gp.layer == MK_TRACE_LAYER || MODE == MODE_ARGMAX) ? p.trace : nullptr;
+#else
+  J.trace = nullptr;
+#endif
   constexpr int KIND = DOWN ? JOB_DOWN : MODE == MODE_ARGMAX ? JOB_ARGMAX : JOB_SMEM;
 #ifdef VP_TRACE_TWICE
   // performance experiment: the QKV jobs once more on the same data (idempotent: one piece per

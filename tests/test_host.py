@@ -1,5 +1,6 @@
 """Host-side logic: algorithmic byte counts, tree buffers, seeded trees and prompts."""
 import numpy as np
+import pytest
 
 from instantllm_b200 import synth
 from oracle import accept as A
@@ -99,3 +100,33 @@ def test_config5_summary_takes_the_max_over_ranks_in_each_mode():
     assert s["one_request_per_launch"]["passes"] == 410 and s["tree_equals_sequential"]
     table[1][3] = 0.0
     assert not bench.config5_summary(table, 16)["tree_equals_sequential"]
+
+
+def test_trace_timeline_reads_the_stamp_layout():
+    from instantllm_b200 import trace as T
+
+    G = 4
+    buf = np.zeros(T.TRACE_LEN, dtype=np.int64)
+
+    def put(ev, cta, ns):
+        buf[T.TRACE_BASE + 256 * ev + cta] = ns
+
+    for c in range(G):
+        put(56, c, 10_000 + 100 * c)                      # layer start
+        put(T.stage_event(0, 0), c, 11_000 + 100 * c)     # QKV entry
+        put(T.stage_event(4, 0), c, 100_000 + 500 * c)    # lm_head entry
+        for w in range(16):
+            put(T.lm_job_event(w, 0, 0), c, 101_000)
+            put(T.lm_job_event(w, 0, 1), c, 102_000)
+            put(T.lm_job_event(w, 0, 2), c, 106_000)
+    put(48, 2, 30_000)
+    put(49, 2, 31_000)
+    t = T.timeline(buf, G)
+    assert t["layer"]["QKV"]["entry"] == pytest.approx((1.15, 1.3))  # median, max over the stamping CTAs
+    assert "inputs" not in t["layer"]["QKV"]                # no CTA stamped it
+    assert t["layer"]["barriers"][0] == (20.0, 21.0)
+    (r,) = t["lm_head"]["rounds"]
+    assert r["jobs"] == 16 * G and r["wait_mean"] == 1.0 and r["compute_mean"] == 4.0 and r["done_max"] == 6.0
+    t["pass_us"] = [580.0]
+    text = T.report(t)
+    assert "round 0: 64 jobs" in text and "grid barrier 0: last arrival 20.00" in text
