@@ -51,10 +51,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--workload", choices=["config2", "batch2", "config3", "config4", "config5",
+    ap.add_argument("--workload", choices=["config2", "batch2", "batch3", "batch4", "config3", "config4", "config5",
                                            "sketch_head", "decode_loop"],
                     default="config2",
-                    help="batch2: two config-2 requests per launch (vp_pass_multi), aggregate tok/s (1 GPU); "
+                    help="batch2 / batch3 / batch4: two, three or four config-2 requests per launch "
+                         "(vp_pass_batch, each on 1/k of the SMs), aggregate tok/s (1 GPU); "
                          "config3 / config4: the q8 8-row chain and f16 16-row tree workloads (1 GPU, "
                          "their own line); config5: BASELINE config 5, independent requests sharded "
                          "over the ranks; sketch_head: the optional two-stage lm_head against the full "
@@ -571,20 +572,20 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_batch2(args):
-    """Two config-2 requests per launch (vp_pass_multi, each on half of the SMs): each request
-    prefilled with its own 256-token prompt, decoded with 1-row passes two per launch (the truth),
-    then every step = both requests' seeded 16-row tree passes + commits from their post-prefill
-    states in one launch. Also times one request alone on its half (n = 1) and the plain
-    whole-GPU pass. One JSON line of its own, 1 GPU."""
+def run_batch(args, k: int):
+    """k config-2 requests per launch (vp_pass_batch with k shares: each request on 1/k of the SMs):
+    each request prefilled with its own 256-token prompt, decoded with 1-row passes k per launch (the
+    truth), then every step = all k requests' seeded 16-row tree passes + commits from their
+    post-prefill states in one launch. Also times one request alone on its share (n = 1) and the
+    plain whole-GPU pass. One JSON line of its own, 1 GPU."""
     import torch
 
     from instantllm_b200 import synth
     from instantllm_b200.engine import VerifyEngine
 
     w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
-    engs, snaps, ys = [], [], []
-    for r in range(2):
+    engs, snaps = [], []
+    for r in range(k):
         eng = VerifyEngine(w, max_ctx=4096, max_steps=4096, device=0)
         eng.begin(0, 24, (-1, -1))
         eng.prefill(synth.make_prompt(PREFIX, seed=1000 + r))
@@ -593,12 +594,12 @@ def run_batch2(args):
     dev, s = engs[0].device, engs[0].stream
     root = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
     for _ in range(23):
-        VerifyEngine.pass_multi(engs, [root, root])
+        VerifyEngine.pass_multi(engs, [root] * k, shares=k)
     ys = [e.tokens(24) for e in engs]
     n_steps = args.warmup + args.steps
-    plans = [[plan_trees(ys[r], 1, 1, (args.seed + r) * 100003 + i) for i in range(n_steps)] for r in range(2)]
-    trees = [torch.tensor(np.stack([p[0][0] for p in plans[r]]), device=dev) for r in range(2)]
-    counts = [[p[1][0] for p in plans[r]] for r in range(2)]
+    plans = [[plan_trees(ys[r], 1, 1, (args.seed + r) * 100003 + i) for i in range(n_steps)] for r in range(k)]
+    trees = [torch.tensor(np.stack([p[0][0] for p in plans[r]]), device=dev) for r in range(k)]
+    counts = [[p[1][0] for p in plans[r]] for r in range(k)]
 
     def timed(fn):
         for i in range(args.warmup):
@@ -612,14 +613,14 @@ def run_batch2(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
 
-    def both(i):
+    def all_k(i):
         for e, sn in zip(engs, snaps):
             e.restore(sn)
-        VerifyEngine.pass_multi(engs, [trees[0][i], trees[1][i]])
+        VerifyEngine.pass_multi(engs, [trees[r][i] for r in range(k)], shares=k)
 
     def one(i):
         engs[0].restore(snaps[0])
-        VerifyEngine.pass_multi(engs[:1], [trees[0][i]])
+        VerifyEngine.pass_multi(engs[:1], [trees[0][i]], shares=k)
 
     def whole(i):
         engs[0].restore(snaps[0])
@@ -628,38 +629,39 @@ def run_batch2(args):
     clocks = ClockSampler(0)
     clocks.start()
     clocks.mark_start()
-    ms2 = timed(both)
+    msk = timed(all_k)
     clk = clocks.stop()
     ms1 = timed(one)
     msw = timed(whole)
     ok = True
-    for i in range(n_steps):  # every step's committed tokens against the truth, both requests
-        both(i)
-        for r in range(2):
+    for i in range(n_steps):  # every step's committed tokens against the truth, all requests
+        all_k(i)
+        for r in range(k):
             st = engs[r].state()
             ok = ok and st["step"] == 1 + counts[r][i] and engs[r].tokens(st["step"]) == ys[r][:st["step"]]
-    tok2 = sum(counts[0][args.warmup:]) + sum(counts[1][args.warmup:])
+    tokk = sum(sum(counts[r][args.warmup:]) for r in range(k))
     hbm_peak, peak_kind = peaks()
     wbytes = synth.weight_bytes("q4", args.layers)
     kv = 12288 * (PREFIX + ROWS) * args.layers / 24 + 12288 * ROWS * args.layers / 24
-    launch_ms = ms2 / args.steps
-    achieved = 2 * (wbytes + kv) / (launch_ms * 1e-3) / 1e9
+    launch_ms = msk / args.steps
+    achieved = k * (wbytes + kv) / (launch_ms * 1e-3) / 1e9
+    words = {2: "two", 3: "three", 4: "four"}
     line = {
-        "metric": "batched verify: two requests per launch, aggregate accepted tok/s (q4 16-row trees)",
-        "value": tok2 / (ms2 * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "requests_per_launch": 2,
-        "launch_us": 1000 * launch_ms, "one_request_half_us": 1000 * ms1 / args.steps,
+        "metric": f"batched verify: {words.get(k, k)} requests per launch, aggregate accepted tok/s (q4 16-row trees)",
+        "value": tokk / (msk * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "requests_per_launch": k,
+        "launch_us": 1000 * launch_ms, "one_request_share_us": 1000 * ms1 / args.steps,
         "one_request_whole_us": 1000 * msw / args.steps,
         "single_request_tok_s": sum(counts[0][args.warmup:]) / (msw * 1e-3),
         "tree_equals_sequential": bool(ok),
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "bytes_per_launch": 2 * (wbytes + kv), "peak_kind": peak_kind,
+                     "frac": achieved / hbm_peak, "bytes_per_launch": k * (wbytes + kv), "peak_kind": peak_kind,
                      "note": "each request streams its own copy of the weights (no shared weight stream)"},
         "dtype": "q4 weights, fp16 activations, fp32 accumulate",
         "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
-        "config": {"workload": "two BASELINE config 2 requests (256-token cached prefixes, seeded 16-row "
-                               "trees) per launch, each on half of the SMs", "layers": args.layers},
+        "config": {"workload": f"{k} BASELINE config 2 requests (256-token cached prefixes, seeded 16-row "
+                               f"trees) per launch, each on 1/{k} of the SMs", "layers": args.layers},
         "gpu_launches": args.steps,
         "clocks": clk,
     }
@@ -978,8 +980,8 @@ def main():
     if args.workload in ("config3", "config4"):
         run_cfg34(args, args.workload)
         return
-    if args.workload == "batch2":
-        run_batch2(args)
+    if args.workload in ("batch2", "batch3", "batch4"):
+        run_batch(args, int(args.workload[-1]))
         return
     if args.workload == "decode_loop":
         run_decode_loop(args)

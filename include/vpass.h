@@ -184,6 +184,12 @@ int vp_pass(vp_ctx* ctx, const int32_t* tree, void* stream);
  * sequential) only if all of them run with the same share. Stream-ordered; contexts not used by
  * this call are untouched. */
 int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, void* stream);
+/* The same with an explicit share: every request runs on gridDim / shares CTAs (shares 1..4,
+ * 1 <= n <= shares), with the same bit-identity rule: a request's passes must all run with one share.
+ * vp_pass_multi(ctxs, trees, n, s) = vp_pass_batch(ctxs, trees, n, 2, s). With three or four shares
+ * (37 to 49 CTAs per request on a B200) the QKV, O and down projections run one or two row-blocks per
+ * CTA. Returns VP_ERR_ARG for a bad n / shares, VP_ERR_DEVICE if a share is below 36 SMs. */
+int vp_pass_batch(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, int32_t shares, void* stream);
 
 /* One step of the host's decode loop (the body of Engine.generate's loop, Engine.swift:937-1015:
  * fill State, encode the pass, wait, read State and the committed tokens) in one call from host

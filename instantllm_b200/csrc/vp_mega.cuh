@@ -78,10 +78,22 @@ __device__ __forceinline__ unsigned mk_gate_target(int l, int count) {
 // Parts per row-block (K split across the warps of one CTA) of a GEMM stage whose CTA owns nrb
 // row-blocks, and K groups of each GEMM stage. Gate/up fills the 16 warps once: 4 row-blocks x 4
 // parts or 5 x 3.
-__host__ __device__ constexpr int mk_parts(int st, int nrb) {
-  return st == MK_QKV ? 14 : st == MK_O ? 14 : st == MK_DOWN ? 16
-       : st == MK_GU ? (nrb >= 16 ? 1 : nrb <= 1 ? 14 : 16 / nrb) : 1;
+// SMALL: code for groups of fewer CTAs than a stage has row-blocks (three or four requests per
+// launch, `k_pass_groups<FMT, true>`); the single-request kernel is compiled without it, so that
+// its code stays as small as the one-row-block-per-CTA layout needs.
+template <bool SMALL>
+__host__ __device__ constexpr int mk_parts_g(int st, int nrb) {
+  // QKV, O and down hold one row-block per CTA, or two in a small group: then half the parts each,
+  // so the partial tiles still fit
+  if constexpr (!SMALL) {
+    return st == MK_QKV ? 14 : st == MK_O ? 14 : st == MK_DOWN ? 16
+         : st == MK_GU ? (nrb >= 16 ? 1 : nrb <= 1 ? 14 : 16 / nrb) : 1;
+  } else {
+    return st == MK_QKV ? (nrb <= 1 ? 14 : 7) : st == MK_O ? (nrb <= 1 ? 14 : 7) : st == MK_DOWN ? (nrb <= 1 ? 16 : 8)
+         : st == MK_GU ? (nrb >= 16 ? 1 : nrb <= 1 ? 14 : 16 / nrb) : 1;
+  }
 }
+__host__ __device__ constexpr int mk_parts(int st, int nrb) { return mk_parts_g<true>(st, nrb); }
 __host__ __device__ constexpr int mk_groups(int st) { return st == MK_DOWN ? F / GS : H / GS; }
 __host__ __device__ constexpr int mk_chunk_groups(int fmt) {
   return fmt == VP_FMT_Q4 ? 7 : fmt == VP_FMT_Q8 ? 4 : 2;  // stand-alone k_gemm chunking
@@ -91,17 +103,22 @@ __host__ __device__ constexpr int mk_tiles_per_slot(int fmt) { return MK_SLOT / 
 // Contiguous row-block range [rb0, rb0 + n) of GEMM stage `st` owned by CTA `cta` of G. O and down
 // go to CTAs 0..55 (which also keep their slice of x), QKV to the last 72 CTAs, gate/up and the
 // lm_head in equal contiguous shares over every CTA. Weights stream ahead of the stages that use
-// them, so the split balances each stage's work rather than each CTA's bytes.
+// them, so the split balances each stage's work rather than each CTA's bytes. A group of fewer
+// CTAs than a stage has row-blocks (36 to 71 CTAs: three or four requests per launch) takes QKV,
+// O and down in equal contiguous shares too, one or two row-blocks per CTA.
 __host__ __device__ constexpr bool mk_down_split(int G) { return G >= 2 * (H / 16); }
-__host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
+template <bool SMALL>
+__host__ __device__ inline void mk_range_g(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
   rb0 = 0;
   n = 0;
   const int nh = H / 16, nq = QKV / 16, ngu = 2 * F / 16;
   if (st == MK_O || st == MK_DOWN) {
-    if (cta < nh) { rb0 = cta; n = 1; }
+    if (SMALL && G < nh) { rb0 = cta * nh / G; n = (cta + 1) * nh / G - rb0; }
+    else if (cta < nh) { rb0 = cta; n = 1; }
     else if (st == MK_DOWN && mk_down_split(G) && cta < 2 * nh) { rb0 = cta - nh; n = 1; }
   } else if (st == MK_QKV) {
-    if (cta >= G - nq) { rb0 = cta - (G - nq); n = 1; }
+    if (SMALL && G < nq) { rb0 = cta * nq / G; n = (cta + 1) * nq / G - rb0; }
+    else if (cta >= G - nq) { rb0 = cta - (G - nq); n = 1; }
   } else if (st == MK_GU) {
     {
       rb0 = cta * ngu / G;  // < 2^31: 148 x 608
@@ -111,6 +128,9 @@ __host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int
     rb0 = cta * nrb_lm / G;  // < 2^31 for every vocab the context accepts
     n = (cta + 1) * nrb_lm / G - rb0;
   }
+}
+__host__ __device__ inline void mk_range(int st, int cta, int G, int nrb_lm, int& rb0, int& n) {
+  mk_range_g<true>(st, cta, G, nrb_lm, rb0, n);
 }
 
 // K-group window [g0, g0 + gn) of the row-blocks a CTA owns in stage st. The down projection is
@@ -281,7 +301,7 @@ struct MkRing {
 // ---------------------------------------------------------------------------------------------
 // producer warp: issues every piece of the pass in order (lane 0)
 
-template <int FMT>
+template <int FMT, bool SMALL>
 __device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sStop, int cta, int G) {
   if ((threadIdx.x & 31) != 0) return;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + MK_OFF_BAR);
@@ -295,7 +315,7 @@ __device__ void mk_producer(const MegaParams& p, uint8_t* smem, volatile int* sS
   for (int si = 0; si < nst && ok; ++si) {
     const int l = si / 4, st = si < p.n_layers * 4 ? si % 4 : MK_LM;
     int rb0, nrb, g0, gn;
-    mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+    mk_range_g<SMALL>(st, cta, G, p.nrb_lm, rb0, nrb);
     if (nrb == 0) continue;
     mk_window(st, cta, G, g0, gn);
     const int ng = mk_groups(st);
@@ -638,7 +658,7 @@ __device__ __forceinline__ int2 mk_jobs(const MkJobs J, MkRing rg, uint8_t* smem
 // (row-block i, token t, row pair rp) sums the K parts of output rows rp and rp + 8 (the RoPE pair
 // of QKV, gate and up of gate/up, two dims of O / down) in part order and applies the stage's
 // epilogue. The 8 lanes of a token sit in one warp (RMSNorm partial of the down / O output).
-template <int MODE>
+template <int MODE, bool SMALL>
 __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int nrb, int P, const float* sPart,
                                             const float* rs, const float* sEpc) {
   const Scratch& s = gp.s;
@@ -706,11 +726,14 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
       const int head = rb >> 2, d = (rb & 3) * 8 + rp;
       float a = 0.f, b = 0.f;
       if (t < n) {
-        // nrb == 1 for QKV (one CTA per row-block): bias and rotations are in shared memory
-        a = s0 * rs[t] + sEpc[rp];
-        b = s1 * rs[t] + sEpc[8 + rp];
+        // bias and rotations of the CTA's first row-block are in shared memory; a second one
+        // (groups of fewer than 72 CTAs) reads them from global memory
+        const bool first = !SMALL || i == 0;
+        a = s0 * rs[t] + (first ? sEpc[rp] : gp.bias[head * HD + d]);
+        b = s1 * rs[t] + (first ? sEpc[8 + rp] : gp.bias[head * HD + d + 32]);
         if (head < NQ + NKV) {
-          const float2 cs = reinterpret_cast<const float2*>(sEpc + 16)[lt];
+          const float2 cs = first ? reinterpret_cast<const float2*>(sEpc + 16)[lt]
+                                  : s.rope[(ri->pos + ri->depth[t]) * 32 + d];
           const float a2 = a * cs.x - b * cs.y;
           const float b2 = b * cs.x + a * cs.y;
           a = a2; b = b2;
@@ -718,7 +741,7 @@ __device__ __forceinline__ void mk_epilogue(const GemmParams& gp, int rb0, int n
       }
       // the attention polls flagged copies (no grid barrier between QKV and attention); the
       // plain q and the KV cache stay the record that later passes and the debug buffers read
-      if (head < NQ) {  // uniform over the CTA (one row-block)
+      if (head < NQ) {  // uniform over each warp (4 warps per row-block)
         if (t < n) {
           s.q[t * H + head * HD + d] = a;
           s.q[t * H + head * HD + d + 32] = b;
@@ -836,7 +859,7 @@ __device__ __noinline__ void mk_poll_flagged(const uint64_t* act_ll, const uint6
 
 // One GEMM stage of the pass for this CTA. piece0: global index of the stage's first piece.
 // Returns false if a wait timed out.
-template <int FMT, int MODE, bool DOWN = false>
+template <int FMT, int MODE, bool DOWN = false, bool SMALL = false>
 __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int piece0, MkRing& rg,
                         uint8_t* smem, volatile int* sAbort, int cta, int G) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -846,10 +869,10 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   float* sPart = reinterpret_cast<float*>(smem + MK_OFF_PART);
   float* sRs = reinterpret_cast<float*>(smem + MK_OFF_RS);
   int rb0, nrb, g0, ng;
-  mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+  mk_range_g<SMALL>(st, cta, G, p.nrb_lm, rb0, nrb);
   if (nrb == 0) return true;
   mk_window(st, cta, G, g0, ng);
-  const int P = mk_parts(st, nrb);
+  const int P = mk_parts_g<SMALL>(st, nrb);
   const int tp = mk_tiles_per_slot(FMT);
   constexpr int TB = tile_bytes(FMT);
   constexpr bool down = DOWN;
@@ -965,13 +988,13 @@ __device__ bool mk_gemm(const MegaParams& p, const GemmParams& gp, int st, int p
   mk_sync();
   MK_CSTAMP(p, dtr, 8 * st + 4);
   if (*sAbort) return false;  // uniform across the CTA: every warp skips the next barrier
-  if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE>(gp, rb0, nrb, P, sJobPart, sRs, sEpc);
+  if constexpr (MODE != MODE_ARGMAX) mk_epilogue<MODE, SMALL>(gp, rb0, nrb, P, sJobPart, sRs, sEpc);
   MK_CSTAMP(p, dtr, 8 * st + 5);
   return true;
 }
 
 // One pass of one request on the G CTAs of its group; this CTA is number cta of them.
-template <int FMT>
+template <int FMT, bool SMALL>
 __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int sAbort;
@@ -993,7 +1016,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
   cta_sync();
 
   if (warp == MK_WARPS) {
-    mk_producer<FMT>(p, smem, &sAbort, cta, G);
+    mk_producer<FMT, SMALL>(p, smem, &sAbort, cta, G);
     __syncwarp();
   } else {
     unsigned long long target = 0;
@@ -1034,7 +1057,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     // the CTA that owns row-block `cta` of the hidden dimension (O and down epilogues) keeps its
     // 16 x 16 slice of x in shared memory for the whole pass
     float* sXrb = reinterpret_cast<float*>(smem + MK_OFF_XRB);
-    const bool own_x = cta < H / 16;
+    const bool own_x = (!SMALL || G >= H / 16) && cta < H / 16;
     if (ok && own_x)
       for (int i = threadIdx.x; i < 256; i += MK_CONS)
         sXrb[i] = __ldcg(p.s.x + (i >> 4) * H + cta * 16 + (i & 15));
@@ -1054,7 +1077,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
     int piece0 = 0;
     auto pieces = [&](int st) {
       int rb0, nrb, g0, gn;
-      mk_range(st, cta, G, p.nrb_lm, rb0, nrb);
+      mk_range_g<SMALL>(st, cta, G, p.nrb_lm, rb0, nrb);
       mk_window(st, cta, G, g0, gn);
       return mk_pieces(FMT, nrb, gn);
     };
@@ -1080,11 +1103,11 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
         gp.bias = p.bqkv[l]; gp.ss_in = s.ss;
         if (l > 0) {
           gp.act_ll_in = s.dn_ll; gp.ss_ll_in = s.dn_ss_ll; gp.flag = flag0 + l - 1;
-          gp.gate = p.gate + MK_GATE_DOWN; gp.gate_target = mk_gate_target(l - 1, HRB);
+          gp.gate = p.gate + MK_GATE_DOWN; gp.gate_target = mk_gate_target(l - 1, SMALL ? min(G, HRB) : HRB);
         }
         gp.s.flag_q = flag0 + l;
         // the attention units poll the flagged q and K / V rows they need
-        ok = mk_gemm<FMT, MODE_QKV>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, cta, G);
+        ok = mk_gemm<FMT, MODE_QKV, false, SMALL>(p, gp, MK_QKV, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_QKV);
         if (!ok) break;
         s.flag_q = flag0 + l;
@@ -1110,7 +1133,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
         gp.wnext = p.ln2[l];
         gp.act_ll_out = s.act_ll; gp.ss_ll_out = s.ss_ll;
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID>(p, gp, MK_O, piece0, rg, smem, &sAbort, cta, G);
+        ok = mk_gemm<FMT, MODE_RESID, false, SMALL>(p, gp, MK_O, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_O);
         if (!ok) break;
         // gate/up + SiLU: polls O's outputs directly (no gate: the O stage is short, and the
@@ -1119,7 +1142,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
         gp.s = s; gp.layer = l;
         gp.w = p.wgu[l]; gp.nrb = 2 * F / 16; gp.ng = H / GS;
         gp.act_ll_in = s.act_ll; gp.ss_ll_in = s.ss_ll; gp.flag = flag0 + l; gp.act_out = s.act_f;
-        ok = mk_gemm<FMT, MODE_SILU>(p, gp, MK_GU, piece0, rg, smem, &sAbort, cta, G) && barrier();
+        ok = mk_gemm<FMT, MODE_SILU, false, SMALL>(p, gp, MK_GU, piece0, rg, smem, &sAbort, cta, G) && barrier();
         piece0 += pieces(MK_GU);
         if (!ok) break;
         // down + residual: flagged words for the next QKV; the last layer's output feeds the
@@ -1140,12 +1163,12 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
           else gp.part_ll_out = s.dnp_ll;
         }
         gp.xs = own_x ? sXrb : nullptr;
-        ok = mk_gemm<FMT, MODE_RESID, true>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G);
+        ok = mk_gemm<FMT, MODE_RESID, true, SMALL>(p, gp, MK_DOWN, piece0, rg, smem, &sAbort, cta, G);
         piece0 += pieces(MK_DOWN);
         if (!ok) break;
         if (to_lm) {
           ok = barrier();
-        } else if (cta < HRB) {  // the down CTAs
+        } else if (cta < (SMALL ? min(G, HRB) : HRB)) {  // the down CTAs (the owners of split row-blocks)
           mk_sync();
           if (threadIdx.x == 0) gate_arrive(p.gate + MK_GATE_DOWN);
         }
@@ -1158,7 +1181,7 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
           reinterpret_cast<float*>(smem + MK_OFF_LMV)[warp * 16 + lane] = -INFINITY;
           reinterpret_cast<int*>(smem + MK_OFF_LMI)[warp * 16 + lane] = 0x7fffffff;
         }
-        ok = mk_gemm<FMT, MODE_ARGMAX>(p, gp, MK_LM, piece0, rg, smem, &sAbort, cta, G);
+        ok = mk_gemm<FMT, MODE_ARGMAX, false, SMALL>(p, gp, MK_LM, piece0, rg, smem, &sAbort, cta, G);
         // per-CTA best per token from the warps' running bests
         float* sLmV = reinterpret_cast<float*>(smem + MK_OFF_LMV);
         int* sLmI = reinterpret_cast<int*>(smem + MK_OFF_LMI);
@@ -1198,22 +1221,22 @@ __device__ __forceinline__ void pass_body(const MegaParams& p, int cta, int G) {
 // One verify pass (or prefill chunk) of one request on every CTA of the launch.
 template <int FMT>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_pass(const __grid_constant__ MegaParams p) {
-  pass_body<FMT>(p, blockIdx.x, gridDim.x);
+  pass_body<FMT, false>(p, blockIdx.x, gridDim.x);
 }
 
-// Passes of MK_MAX_GROUPS requests in one launch, each on its own contiguous group of
+// Passes of up to MK_MAX_GROUPS requests in one launch, each on its own contiguous group of
 // gridDim.x / groups CTAs with its own context (barrier counters, state, scratch, KV cache): a
-// single pass is bound by the latency of its dependent stages, not by the SMs or HBM, so a second
-// request on the other half of the SMs costs little time.
-constexpr int MK_MAX_GROUPS = 2;
+// single pass is bound by the latency of its dependent stages, not by the SMs or HBM, so more
+// requests on shares of the SMs cost little time each. SMALL: groups of fewer than 72 CTAs.
+constexpr int MK_MAX_GROUPS = 4;
 struct BatchParams {
   MegaParams p[MK_MAX_GROUPS];
   int groups;
 };
-template <int FMT>
+template <int FMT, bool SMALL>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_pass_groups(const __grid_constant__ BatchParams bp) {
   const int per = gridDim.x / bp.groups, g = blockIdx.x / per;
-  pass_body<FMT>(bp.p[g], blockIdx.x - g * per, per);
+  pass_body<FMT, SMALL>(bp.p[g], blockIdx.x - g * per, per);
 }
 
 }  // namespace vp

@@ -133,7 +133,8 @@ int set_attrs(vp_ctx* c) {
   VP_CUDA(cudaFuncSetAttribute(k_gemm<FMT, MODE_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)c->lm.smem));
   VP_CUDA(cudaFuncSetAttribute(k_pass<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
-  VP_CUDA(cudaFuncSetAttribute(k_pass_groups<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+  VP_CUDA(cudaFuncSetAttribute(k_pass_groups<FMT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+  VP_CUDA(cudaFuncSetAttribute(k_pass_groups<FMT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
   int per_sm = 0;
   VP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pass<FMT>, MK_THREADS, MK_SMEM));
   if (per_sm < 1) return fail(VP_ERR_CUDA, "pass kernel does not fit on an SM");
@@ -187,15 +188,18 @@ int launch_commit(vp_ctx* c, cudaStream_t st) {
   return VP_OK;
 }
 
-// Whether a pass fits G CTAs: QKV / O / down take one CTA per row-block (72 / 56 / 56), and every
-// CTA keeps its row-blocks' partial tiles of a stage in MK_PART_SLOTS shared-memory slots.
+// Whether a pass fits G CTAs: QKV / O / down take one or two row-blocks per CTA (72 / 56 / 56
+// row-blocks), and every CTA keeps its row-blocks' partial tiles of a stage in the MK_PART_SLOTS
+// shared-memory slots (QKV and gate/up past the MK_SS_SLOTS of staged RMSNorm partials).
 bool split_fits(int G, int vocab) {
-  if (G < QKV / 16) return false;
+  if (G < (QKV / 16 + 1) / 2) return false;
   for (int st = MK_QKV; st <= MK_DOWN; ++st)
     for (int cta = 0; cta < G; ++cta) {
       int rb0, n;
       mk_range(st, cta, G, vocab / 16, rb0, n);
-      if (n * mk_parts(st, n) > MK_PART_SLOTS) return false;
+      const int slots = MK_PART_SLOTS - (st == MK_QKV || st == MK_GU ? MK_SS_SLOTS : 0);
+      if (n > 2 && st != MK_GU) return false;
+      if (n * mk_parts(st, n) > slots) return false;
     }
   return true;
 }
@@ -254,7 +258,7 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
   VP_CUDA(cudaSetDevice(cfg->device));
   int sms = 0;
   VP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device));
-  if (!split_fits(sms, cfg->vocab)) return fail(VP_ERR_DEVICE, "the pass kernel needs at least 72 SMs");
+  if (!split_fits(sms, cfg->vocab)) return fail(VP_ERR_DEVICE, "the pass kernel needs at least 36 SMs");
   vp_ctx* c = new vp_ctx();
   c->cfg = *cfg;
   const int fmt = cfg->format;
@@ -465,8 +469,9 @@ int vp_pass(vp_ctx* c, const int32_t* tree, void* stream) {
   return launch_pass(c, p, st);
 }
 
-int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, void* stream) {
-  if (!ctxs || !trees || n < 1 || n > MK_MAX_GROUPS) return fail(VP_ERR_ARG, "n must be 1 or 2");
+int vp_pass_batch(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, int32_t shares, void* stream) {
+  if (!ctxs || !trees || shares < 1 || shares > MK_MAX_GROUPS || n < 1 || n > shares)
+    return fail(VP_ERR_ARG, "need 1 <= n <= shares <= 4");
   int r = VP_OK;
   for (int i = 0; i < n; ++i) {
     if ((r = check_ctx(ctxs[i]))) return r;
@@ -477,9 +482,9 @@ int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, v
       return fail(VP_ERR_ARG, "contexts on different devices or formats");
   }
   vp_ctx* c0 = ctxs[0];
-  const int per = c0->grid / MK_MAX_GROUPS;  // every request gets the same share, whatever n is
+  const int per = c0->grid / shares;  // every request gets its share, whatever n is
   for (int i = 0; i < n; ++i)
-    if (!split_fits(per, ctxs[i]->cfg.vocab)) return fail(VP_ERR_DEVICE, "too few SMs for two pass groups");
+    if (!split_fits(per, ctxs[i]->cfg.vocab)) return fail(VP_ERR_DEVICE, "too few SMs for that many pass groups");
   VP_CUDA(cudaSetDevice(c0->cfg.device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   BatchParams bp = {};
@@ -490,13 +495,31 @@ int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, v
     bp.p[i].do_lm = 1;
     bp.p[i].do_commit = 1;
   }
+  const bool small = per < QKV / 16;  // fewer CTAs per request than QKV row-blocks
   switch (c0->cfg.format) {
-    case VP_FMT_Q4: VP_CUDA(launch(k_pass_groups<VP_FMT_Q4>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
-    case VP_FMT_Q8: VP_CUDA(launch(k_pass_groups<VP_FMT_Q8>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
-    case VP_FMT_Q8G32: VP_CUDA(launch(k_pass_groups<VP_FMT_Q8G32>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
-    default: VP_CUDA(launch(k_pass_groups<VP_FMT_F16>, per * n, MK_THREADS, MK_SMEM, st, true, bp)); break;
+    case VP_FMT_Q4:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q4, true> : k_pass_groups<VP_FMT_Q4, false>, per * n, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
+    case VP_FMT_Q8:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8, true> : k_pass_groups<VP_FMT_Q8, false>, per * n, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
+    case VP_FMT_Q8G32:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8G32, true> : k_pass_groups<VP_FMT_Q8G32, false>, per * n,
+                     MK_THREADS, MK_SMEM, st, true, bp));
+      break;
+    default:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_F16, true> : k_pass_groups<VP_FMT_F16, false>, per * n, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
   }
   return VP_OK;
+}
+
+int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, void* stream) {
+  if (n < 1 || n > 2) return fail(VP_ERR_ARG, "n must be 1 or 2");
+  return vp_pass_batch(ctxs, trees, n, 2, stream);
 }
 
 int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* state_out,

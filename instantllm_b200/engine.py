@@ -262,16 +262,20 @@ class VerifyEngine:
         return Graph(self.lib, h)
 
     @staticmethod
-    def pass_multi(engines, trees_dev) -> None:
-        """One verify pass + commit of each engine's request in one launch (vp_pass_multi), each
-        request on half of the SMs; trees_dev: one device int32[65] tree buffer per engine."""
+    def pass_multi(engines, trees_dev, shares: int = 2) -> None:
+        """One verify pass + commit of each engine's request in one launch, each request on
+        1/shares of the SMs (vp_pass_batch; shares 2 is vp_pass_multi); trees_dev: one device
+        int32[65] tree buffer per engine. A request's passes must all use one share."""
         if not engines or len(engines) != len(trees_dev):
             raise ValueError("one tree per engine")
         n = len(engines)
         ctxs = (ctypes.c_void_p * n)(*[e.ctx.value for e in engines])
         trees = (ctypes.c_void_p * n)(*[t.data_ptr() for t in trees_dev])
         e0 = engines[0]
-        check(e0.lib.vp_pass_multi(ctxs, trees, n, e0._s), "vp_pass_multi")
+        if shares == 2:
+            check(e0.lib.vp_pass_multi(ctxs, trees, n, e0._s), "vp_pass_multi")
+        else:
+            check(e0.lib.vp_pass_batch(ctxs, trees, n, shares, e0._s), "vp_pass_batch")
 
     # ---- results ----
     def state(self) -> dict:

@@ -74,6 +74,53 @@ def test_two_requests_per_launch_tree_equals_sequential():
     eb.close()
 
 
+def test_four_requests_per_launch_tree_equals_sequential():
+    """Four shares of the SMs (37 CTAs per request on a B200: QKV, O and down one or two row-blocks
+    per CTA): the sequential truth of four requests, one of them again alone and three together on
+    their shares, then 16-row trees; every committed token checked, and one request's logits against
+    the fp32 oracle."""
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=2, vocab=V, seed=64)
+    es = [_engine(w, 10 + k) for k in range(4)]
+    engs = [e for e, _, _ in es]
+    root = _root(engs[0])
+    for _ in range(40):
+        VerifyEngine.pass_multi(engs, [root] * 4, shares=4)
+    ys = [e.tokens(41) for e in engs]
+    assert all(e.state()["err"] == 0 for e in engs)
+    # the first alone and the other three together, on the same shares: the same tokens
+    for e, (_, _, sn) in zip(engs, es):
+        e.restore(sn)
+    for _ in range(40):
+        VerifyEngine.pass_multi(engs[:1], [root], shares=4)
+        VerifyEngine.pass_multi(engs[1:], [root] * 3, shares=4)
+    assert [e.tokens(41) for e in engs] == ys
+    rng = np.random.default_rng(64)
+    for e, (_, _, sn) in zip(engs, es):
+        e.restore(sn)
+    for _ in range(4):
+        st0 = [e.state() for e in engs]
+        trees = [synth.seeded_tree(rng, y[s["step"]:s["step"] + 9], n=16, vocab=V) for y, s in zip(ys, st0)]
+        VerifyEngine.pass_multi(engs, [torch.tensor(synth.tree_to_buffer(t), device=engs[0].device) for t in trees],
+                                shares=4)
+        for e, y, s, tree in zip(engs, ys, st0, trees):
+            st = e.state()
+            parents, tokens = A.to_python_numbering(tree)
+            assert st["step"] == s["step"] + A.accept_tree(parents, tokens, y, s["step"]) + 1
+            assert e.tokens(st["step"]) == y[:st["step"]]
+    _, p3, _ = es[3]
+    y3, s3 = ys[3], st0[3]
+    m = Q.model_from_weights(w)
+    cache = Q.KVCache(2, 512)
+    Q.forward_causal(m, cache, p3 + y3[:s3["step"] - 1], 0)
+    ref = Q.tree_pass(m, cache, len(p3) + s3["step"] - 1, y3[s3["step"] - 1], trees[3])
+    got = engs[3].logits().cpu().numpy()[:16]
+    assert float(np.abs(got - ref).max()) < 0.05
+    for e in engs:
+        e.close()
+
+
 def test_long_prefixes_two_per_launch_then_one_on_its_half():
     """Rows past the 320 positions of one attention segment (the segmented path), two requests of
     different prefix lengths per launch, then the survivor alone on its half: tree == sequential."""
@@ -130,4 +177,7 @@ def test_pass_multi_rejects_bad_arguments():
     assert lib.vp_pass_multi(one, trees, 2, None) == -1  # the same context twice
     assert lib.vp_pass_multi(one, trees, 3, None) == -1
     assert lib.vp_pass_multi(one, trees, 0, None) == -1
+    assert lib.vp_pass_batch(one, trees, 2, 1, None) == -1  # more requests than shares
+    assert lib.vp_pass_batch(one, trees, 1, 5, None) == -1
+    assert lib.vp_pass_batch(one, trees, 1, 0, None) == -1
     eng.close()
