@@ -283,18 +283,21 @@ def run_ours(args, rank, world, local):
 GEN = 64  # config 5: tokens generated per request
 
 
+C5_MODES = (1, 2, 4)  # requests per launch measured in config 5 (each request on 1/k of the SMs)
+C5_HEADLINE = 4       # the serving mode of the config-5 headline value
+
+
 def run_config5(args, rank, world, local, w=None, n_requests=None):
     """BASELINE config 5 on this rank: its share of the requests (prefixes uniform in 128-2048,
-    shard.assign), each prefilled, decoded sequentially with 1-row passes (untimed: the true
-    continuation the seeded trees draft from), then decoded again with 16-row tree passes to 64
-    tokens in two serving modes over the same requests and trees:
-    - one request per launch (vp_pass on all SMs);
-    - two per launch (vp_pass_multi over the pairs of shard.pairs, each request on half of the
-      SMs to its end: once one request of a pair has its tokens, the other's remaining passes run
-      alone on their half; the odd request out of a rank runs on all SMs).
-    Only the tree passes are timed (CUDA events around each request's or pair's passes, all enqueued
-    at once from device-resident trees); the committed tokens of each mode are checked against the
-    sequential 1-row passes of the same mode (tree == sequential)."""
+    shard.assign), each prefilled, then decoded with 16-row tree passes to 64 tokens in three serving
+    modes over the same requests: one request per launch (vp_pass on all SMs), two and four per
+    launch (vp_pass_batch over the groups of shard.groups, each request on 1/k of the SMs to its end:
+    once a request of a group has its tokens, the others go on without it). In each mode the
+    requests are first decoded with 1-row passes of that mode (untimed: the true continuation that
+    the seeded trees draft from; a share of the SMs sums some projections in another order than the
+    whole GPU, so each mode has its own truth), and the committed tokens are checked against it
+    (tree == sequential). Only the tree passes are timed (CUDA events around each group's passes,
+    all enqueued at once from device-resident trees)."""
     import torch
 
     from instantllm_b200 import shard, synth
@@ -306,10 +309,11 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
     mine = shard.assign(prefixes, world)[rank]
     if w is None:
         w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
-    engs = [VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local) for _ in range(2)]
+    kmax = max(C5_MODES)
+    engs = [VerifyEngine(w, max_ctx=2048 + GEN + 16 + 32, max_steps=GEN + 16, device=local) for _ in range(kmax)]
     no_eos = (-1, -1)
     tree1 = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=dev)
-    s = engs[0].stream  # both engines run on the device's current stream
+    s = engs[0].stream  # every engine runs on the device's current stream
 
     def plan(i, y):
         # trees planned from the true continuation; the device follows the planned acceptances
@@ -319,16 +323,7 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
             t, c, _ = plan_trees(y, 1 + sum(cnts), 1, args.seed * 7 + i * 1009 + len(bufs))
             bufs.append(t[0])
             cnts.append(c[0])
-        return dict(i=i, y=y, tb=torch.tensor(np.stack(bufs), device=dev), cnts=cnts)
-
-    def prepare(eng, i):
-        prompt = synth.make_prompt(prefixes[i], seed=5000 + i)
-        eng.begin(0, GEN + 9, no_eos)
-        eng.prefill(prompt)
-        snap = eng.snapshot()
-        for _ in range(GEN + 8):
-            eng.pass_device(tree1)
-        return dict(plan(i, eng.tokens(GEN + 9)), snap=snap)
+        return dict(y=y, tb=torch.tensor(np.stack(bufs), device=dev), cnts=cnts)
 
     def timed(fn):
         torch.cuda.synchronize()
@@ -339,84 +334,79 @@ def run_config5(args, rank, world, local, w=None, n_requests=None):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
 
-    def check_out(eng, rq):
-        st = eng.state()
-        return eng.tokens(st["step"]) == rq["y"][:st["step"]] and st["step"] >= GEN, st["step"] - 1
+    res = {k: dict(ms=0.0, tok=0, passes=0, launches=0, nbytes=0.0, ok=True, differ=0) for k in C5_MODES}
+    wbytes = synth.weight_bytes("q4", args.layers)
 
-    ms1, ms2, tokens, tokens2, passes, launches2, kv_slots, ok, differ = 0.0, 0.0, 0, 0, 0, 0, 0, True, 0
-    for pair in shard.pairs(mine, prefixes):
-        reqs = [prepare(engs[k], i) for k, i in enumerate(pair)]
-        # one request per launch
-        for eng, rq in zip(engs, reqs):
-            eng.restore(rq["snap"])  # back to the post-prefill state over the same cached prefix
-            tb = rq["tb"]
-            ms1 += timed(lambda: [eng.pass_device(tb[k]) for k in range(len(tb))])
-            good, tok = check_out(eng, rq)
-            ok = ok and good
-            tokens += tok  # the first token comes from the prefill
-            passes += len(tb)
-            n, p = len(rq["cnts"]), prefixes[rq["i"]]
-            kv_slots += sum(p + 1 + sum(rq["cnts"][:k]) + ROWS for k in range(n))
-        # two per launch
-        if len(reqs) == 1:  # the odd request out runs alone on all SMs, as above
-            ms2 += timed(lambda: [engs[0].pass_device(reqs[0]["tb"][k]) for k in range(len(reqs[0]["tb"]))])
-            launches2 += len(reqs[0]["tb"])
-            good, tok = check_out(engs[0], reqs[0])
-            ok = ok and good
-            tokens2 += tok
-            continue
-        # A request of a pair stays on its half of the SMs to its end (vp_pass_multi with n = 1 once
-        # its partner is done): the half-SM pass sums the down projection's K halves in another
-        # order than the whole-GPU pass, so its truth is its own 1-row passes on its half.
-        for eng, rq in zip(engs, reqs):
-            eng.restore(rq["snap"])
+    def run_mode(sub, k):
+        """Requests sub = [(engine, request)] decoded together with k shares (k = 1: alone on the
+        whole GPU)."""
+        r = res[k]
+        for e, rq in sub:
+            e.restore(rq["snap"])  # back to the post-prefill state over the same cached prefix
+        es = [e for e, _ in sub]
         for _ in range(GEN + 8):
-            VerifyEngine.pass_multi(engs, [tree1, tree1])
-        halves = []
-        for eng, rq in zip(engs, reqs):
-            y2 = eng.tokens(GEN + 9)
-            differ += y2 != rq["y"]
-            halves.append(rq if y2 == rq["y"] else plan(rq["i"], y2))
-            eng.restore(rq["snap"])
-        a, b = halves[0]["tb"], halves[1]["tb"]
+            if k == 1:
+                es[0].pass_device(tree1)
+            else:
+                VerifyEngine.pass_multi(es, [tree1] * len(es), shares=k)
+        plans = []
+        for e, rq in sub:
+            y = e.tokens(GEN + 9)
+            if k == 1:
+                rq["y1"], rq["plan1"] = y, plan(rq["i"], y)
+            r["differ"] += int(y != rq["y1"])
+            plans.append(rq["plan1"] if y == rq["y1"] else plan(rq["i"], y))
+            e.restore(rq["snap"])
+        L = max(len(p["tb"]) for p in plans)
 
-        def run_pair():
-            for k in range(max(len(a), len(b))):
-                if k < len(a) and k < len(b):
-                    VerifyEngine.pass_multi(engs, [a[k], b[k]])
-                elif k < len(a):
-                    VerifyEngine.pass_multi(engs[:1], [a[k]])
+        def go():
+            for j in range(L):
+                act = [q for q in range(len(sub)) if j < len(plans[q]["tb"])]
+                if k == 1:
+                    es[0].pass_device(plans[0]["tb"][j])
                 else:
-                    VerifyEngine.pass_multi(engs[1:], [b[k]])
+                    VerifyEngine.pass_multi([es[q] for q in act], [plans[q]["tb"][j] for q in act], shares=k)
 
-        ms2 += timed(run_pair)
-        launches2 += max(len(a), len(b))
-        for eng, rq in zip(engs, halves):
-            good, tok = check_out(eng, rq)
-            ok = ok and good
-            tokens2 += tok
+        r["ms"] += timed(go)
+        r["launches"] += L
+        for (e, rq), p in zip(sub, plans):
+            st = e.state()
+            r["ok"] = r["ok"] and e.tokens(st["step"]) == p["y"][:st["step"]] and st["step"] >= GEN
+            r["tok"] += st["step"] - 1  # the first token comes from the prefill
+            n = len(p["cnts"])
+            r["passes"] += n
+            pre = prefixes[rq["i"]]
+            r["nbytes"] += n * wbytes + 12288 * sum(pre + 1 + sum(p["cnts"][:j]) + ROWS for j in range(n)) * args.layers / 24
+
+    for grp in shard.groups(mine, prefixes, kmax):
+        reqs = []
+        for e, i in zip(engs, grp):
+            e.begin(0, GEN + 9, no_eos)
+            e.prefill(synth.make_prompt(prefixes[i], seed=5000 + i))
+            reqs.append(dict(i=i, snap=e.snapshot()))
+        sub = list(zip(engs, reqs))
+        for k in sorted(C5_MODES):
+            for j in range(0, len(sub), k):
+                if k == 1:
+                    run_mode(sub[j:j + 1], 1)
+                else:
+                    run_mode(sub[j:j + k], k)
     for e in engs:
         e.close()
-    return dict(ms=ms1, ms2=ms2, tok=tokens, tok2=tokens2, passes=passes, launches2=launches2,
-                kv_slots=kv_slots, ok=ok, n=len(mine), differ=differ)
+    return dict(modes=res, n=len(mine))
 
 
 def config5_table(args, r, world):
-    """Per-rank config-5 figures gathered on every rank: [device ms one request per launch, tokens,
-    passes, ok, GB/s, device ms two per launch, GB/s two per launch, launches two per launch,
-    tokens two per launch, requests whose half-SM truth differs from the whole-GPU one]."""
+    """Per-rank config-5 figures gathered on every rank: per mode of C5_MODES [device ms, tokens,
+    request passes, launches, ok, GB/s, requests whose truth differs from the whole-GPU one]."""
     import torch
 
-    from instantllm_b200 import synth
-
-    wbytes = synth.weight_bytes("q4", args.layers)
-    # every request's pass streams the weights once in both modes (each half of a two-request
-    # launch streams its own copy), so both modes move the same bytes
-    nbytes = r["passes"] * wbytes + 12288 * r["kv_slots"] * args.layers / 24
-    gbs = nbytes / (max(r["ms"], 1e-9) * 1e-3) / 1e9
-    gbs2 = nbytes / (max(r["ms2"], 1e-9) * 1e-3) / 1e9
-    vals = [r["ms"], float(r["tok"]), float(r["passes"]), 1.0 if r["ok"] else 0.0, gbs, r["ms2"], gbs2,
-            float(r["launches2"]), float(r["tok2"]), float(r["differ"])]
+    vals = []
+    for k in C5_MODES:
+        m = r["modes"][k]
+        gbs = m["nbytes"] / (max(m["ms"], 1e-9) * 1e-3) / 1e9
+        vals += [m["ms"], float(m["tok"]), float(m["passes"]), float(m["launches"]), 1.0 if m["ok"] else 0.0, gbs,
+                 float(m["differ"])]
     if world > 1:
         rows = [torch.zeros(len(vals), dtype=torch.float64) for _ in range(world)]
         torch.distributed.all_gather(rows, torch.tensor(vals, dtype=torch.float64))
@@ -425,22 +415,25 @@ def config5_table(args, r, world):
 
 
 def config5_summary(table, n_requests) -> dict:
-    """Two requests per launch is the serving mode of the headline value; one request per launch,
-    on the same requests and trees, is reported beside it."""
-    tok = sum(t[1] for t in table)
-    tok2 = sum(t[8] for t in table)
-    ms1 = max(t[0] for t in table)
-    ms2 = max(t[5] for t in table)
-    return {"value": tok2 / (ms2 * 1e-3), "unit": "tok/s", "requests": n_requests, "tokens": int(tok2),
-            "requests_per_launch": 2, "launches": int(sum(t[7] for t in table)),
-            "half_sm_truth_differs": int(sum(t[9] for t in table)),
-            "ms_per_rank": [round(t[5], 3) for t in table],
-            "per_gpu_hbm_gbs": [round(t[6], 1) for t in table],
-            "one_request_per_launch": {"value": tok / (ms1 * 1e-3), "unit": "tok/s", "tokens": int(tok),
-                                       "passes": int(sum(t[2] for t in table)),
-                                       "ms_per_rank": [round(t[0], 3) for t in table],
-                                       "per_gpu_hbm_gbs": [round(t[4], 1) for t in table]},
-            "tree_equals_sequential": all(t[3] > 0 for t in table)}
+    """The headline value is C5_HEADLINE requests per launch; every mode of C5_MODES, on the same
+    requests and trees, is reported under "modes"."""
+    F = 7
+    modes = {}
+    for q, k in enumerate(C5_MODES):
+        col = [t[q * F:(q + 1) * F] for t in table]
+        tok = sum(c[1] for c in col)
+        ms = max(c[0] for c in col)
+        modes[str(k)] = {"value": tok / (ms * 1e-3), "unit": "tok/s", "tokens": int(tok),
+                         "request_passes": int(sum(c[2] for c in col)), "launches": int(sum(c[3] for c in col)),
+                         "ms_per_rank": [round(c[0], 3) for c in col],
+                         "per_gpu_hbm_gbs": [round(c[5], 1) for c in col],
+                         "tree_equals_sequential": all(c[4] > 0 for c in col),
+                         "truth_differs_from_whole_gpu": int(sum(c[6] for c in col))}
+    h = modes[str(C5_HEADLINE)]
+    return {"value": h["value"], "unit": "tok/s", "requests": n_requests, "requests_per_launch": C5_HEADLINE,
+            "tokens": h["tokens"], "ms_per_rank": h["ms_per_rank"], "per_gpu_hbm_gbs": h["per_gpu_hbm_gbs"],
+            "tree_equals_sequential": all(m["tree_equals_sequential"] for m in modes.values()),
+            "modes": modes}
 
 
 def main_config5(args, rank, world):
@@ -453,8 +446,9 @@ def main_config5(args, rank, world):
             **config5_summary(table, args.requests),
             "config": {"workload": "BASELINE config 5: requests with prefixes uniform in [128, 2048], "
                                    "64 tokens each, seeded 16-row trees as in config 2, "
-                                   "longest-processing-time-first sharding (no collective), two "
-                                   "requests per launch (vp_pass_multi) and one per launch",
+                                   "longest-processing-time-first sharding (no collective), "
+                                   f"{C5_HEADLINE} requests per launch (vp_pass_batch); one, two and four "
+                                   "per launch under modes",
                        "layers": args.layers, "timed": "tree passes only (device time, max over ranks)"},
             "data": "synthetic (seeded random-init q4 weights, uniform prompt ids, seeded trees)",
         }
@@ -1065,9 +1059,10 @@ def main():
         if rank == 0:
             line["config5"] = dict(config5_summary(table, args.c5_requests), scaling="strong",
                                    workload="BASELINE config 5: prefixes uniform in [128, 2048], 64 tokens "
-                                            "each, seeded 16-row trees; two requests per launch "
-                                            "(vp_pass_multi) and one per launch on the same requests; "
-                                            "device time of the tree passes, max over ranks")
+                                            f"each, seeded 16-row trees; {C5_HEADLINE} requests per launch "
+                                            "(vp_pass_batch), and one, two and four per launch on the same "
+                                            "requests under modes; device time of the tree passes, max "
+                                            "over ranks")
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

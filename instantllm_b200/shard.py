@@ -47,11 +47,18 @@ def config5_requests(n: int = 256, seed: int = 5, lo: int = 128, hi: int = 2048)
     return [int(v) for v in rng.integers(lo, hi + 1, size=n)]
 
 
-def pairs(indices, prefixes) -> list:
-    """A rank's requests grouped two per launch (vp_pass_multi puts each request of a pair on half
-    of the SMs, and the launch lasts as long as its slower half): sorted by prefix length, longest
-    first, and paired with their neighbours, so the two halves of a launch read KV prefixes of
-    similar length. An odd request out is the last, shortest one, alone. Deterministic: ties broken
-    by index."""
+def groups(indices, prefixes, k: int) -> list:
+    """A rank's requests grouped k per launch (vp_pass_batch puts each request of a group on 1/k of
+    the SMs, and the launch lasts as long as its slowest share): sorted by prefix length, longest
+    first, and grouped with their neighbours, so the shares of a launch read KV prefixes of similar
+    length. The last group holds the shortest requests left (fewer than k if k does not divide the
+    count). Deterministic: ties broken by index."""
+    if k < 1:
+        raise ValueError("k must be >= 1")
     order = sorted(indices, key=lambda i: (-prefixes[i], i))
-    return [tuple(order[k:k + 2]) for k in range(0, len(order), 2)]
+    return [tuple(order[j:j + k]) for j in range(0, len(order), k)]
+
+
+def pairs(indices, prefixes) -> list:
+    """groups(indices, prefixes, 2): two requests per launch."""
+    return groups(indices, prefixes, 2)

@@ -89,17 +89,21 @@ def test_adaptive_pass_shape_follows_the_reference_rule():
 def test_config5_summary_takes_the_max_over_ranks_in_each_mode():
     import bench
 
-    # [ms one per launch, tokens, passes, ok, GB/s, ms two per launch, GB/s two, launches two,
-    #  tokens two, half-SM truths that differ]
-    table = [[100.0, 500.0, 200.0, 1.0, 300.0, 70.0, 430.0, 110.0, 501.0, 1.0],
-             [120.0, 520.0, 210.0, 1.0, 290.0, 80.0, 435.0, 115.0, 520.0, 0.0]]
-    s = bench.config5_summary(table, 16)
-    assert s["value"] == 1021 / 0.080 and s["requests_per_launch"] == 2 and s["launches"] == 225
-    assert s["half_sm_truth_differs"] == 1 and s["tokens"] == 1021
-    assert s["one_request_per_launch"]["value"] == 1020 / 0.120
-    assert s["one_request_per_launch"]["passes"] == 410 and s["tree_equals_sequential"]
-    table[1][3] = 0.0
-    assert not bench.config5_summary(table, 16)["tree_equals_sequential"]
+    # per mode of bench.C5_MODES (1, 2, 4): [ms, tokens, request passes, launches, ok, GB/s, differ]
+    r0 = [100.0, 500.0, 200.0, 200.0, 1.0, 300.0, 0.0] + [70.0, 501.0, 200.0, 110.0, 1.0, 430.0, 1.0] \
+        + [50.0, 500.0, 200.0, 60.0, 1.0, 600.0, 0.0]
+    r1 = [120.0, 520.0, 210.0, 210.0, 1.0, 290.0, 0.0] + [80.0, 520.0, 210.0, 115.0, 1.0, 435.0, 0.0] \
+        + [55.0, 520.0, 210.0, 62.0, 1.0, 610.0, 2.0]
+    s = bench.config5_summary([r0, r1], 16)
+    assert bench.C5_MODES == (1, 2, 4) and bench.C5_HEADLINE == 4
+    assert s["value"] == 1020 / 0.055 and s["requests_per_launch"] == 4 and s["tokens"] == 1020
+    m = s["modes"]
+    assert m["1"]["value"] == 1020 / 0.120 and m["1"]["launches"] == 410
+    assert m["2"]["value"] == 1021 / 0.080 and m["2"]["truth_differs_from_whole_gpu"] == 1
+    assert m["4"]["ms_per_rank"] == [50.0, 55.0] and m["4"]["truth_differs_from_whole_gpu"] == 2
+    assert s["tree_equals_sequential"]
+    r1[4 + 7] = 0.0  # one rank's two-per-launch run failed its check
+    assert not bench.config5_summary([r0, r1], 16)["tree_equals_sequential"]
 
 
 def test_trace_timeline_reads_the_stamp_layout():

@@ -77,6 +77,7 @@ def test_pairs_cover_a_rank_and_match_neighbouring_lengths():
             lens = [prefixes[i] for p in ps for i in p]
             assert lens == sorted(lens, reverse=True)  # longest first, neighbours together
     assert shard.pairs([3, 1, 2], [10, 30, 30, 20]) == [(1, 2), (3,)]
+    assert shard.groups([0, 1, 2, 3, 4], [5, 9, 7, 8, 6], 4) == [(1, 3, 2, 4), (0,)]
 
 
 def test_two_gloo_ranks_agree_on_the_partition():
