@@ -6,7 +6,9 @@ each step of the stages of one layer (layer 5) and of the lm_head, and at every 
 warp. This module runs one config-2 tree pass through it on cuda:0 (q4 weights, a 256-token cached
 prefix, a seeded 16-row tree after the true continuation) and prints the timeline:
 
-    python -m instantllm_b200.trace [--layers 24] [--passes 6]
+    python -m instantllm_b200.trace [--layers 24] [--passes 6] [--rows 16]
+
+(--rows 1 traces a 1-row pass, plain decoding, instead of the 16-row tree.)
 
 Layout of the stamps (trace[MK_TRACE_BASE + 256 * event + cta], csrc/vp_mega.cuh): event
 8 * stage + step for the GEMM stages (stages QKV, O, gate/up, down, lm_head; steps entry, inputs in
@@ -92,9 +94,10 @@ def timeline(buf: np.ndarray, G: int) -> dict:
     return out
 
 
-def run(layers: int = 24, passes: int = 6, seed: int = 0) -> dict:
-    """Build the trace library if needed, run `passes` identical config-2 tree passes through it
-    and return the timeline of the last one, with the CUDA-event time of every pass."""
+def run(layers: int = 24, passes: int = 6, seed: int = 0, rows: int = 16) -> dict:
+    """Build the trace library if needed, run `passes` identical config-2 tree passes (rows = 16) or
+    1-row passes (rows = 1) through it and return the timeline of the last one, with the CUDA-event
+    time of every pass."""
     from pathlib import Path
 
     import torch
@@ -120,7 +123,9 @@ def run(layers: int = 24, passes: int = 6, seed: int = 0) -> dict:
         for _ in range(23):
             eng.pass_device(root)
         y = eng.tokens(24)
-        tree = synth.seeded_tree(np.random.default_rng(seed + 7), y[1:10], n=16)
+        if rows not in (1, 16):
+            raise ValueError("rows must be 1 or 16")
+        tree = synth.seeded_tree(np.random.default_rng(seed + 7), y[1:10], n=16) if rows == 16 else synth.root_tree()
         tb = torch.tensor(synth.tree_to_buffer(tree), device=dev)
         buf = eng.buffer(6, (TRACE_LEN,), "<i8")
         G = eng.argmax_partials()[0].shape[1]
@@ -164,8 +169,9 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--passes", type=int, default=6)
+    ap.add_argument("--rows", type=int, default=16, choices=(1, 16))
     a = ap.parse_args()
-    print(report(run(a.layers, a.passes)))
+    print(report(run(a.layers, a.passes, rows=a.rows)))
 
 
 if __name__ == "__main__":
