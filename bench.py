@@ -670,7 +670,8 @@ def run_decode_loop(args):
     the committed table subset tests/golden/draft_subset.ildraft) + one verify pass, enqueued one
     step ahead, the shape from the adaptive rule. Against it: the same request by plain greedy
     decoding (1-row passes), by the loop with fixed trees and by the loop replaying each step as a
-    CUDA graph; and k_draft alone. The weights are
+    CUDA graph; k_draft alone; and four requests at once (generate_drafted_batch, each on a quarter
+    of the SMs, batch4_*). The weights are
     random-init, so the drafter's candidates (trained on real text) are rarely accepted: the line
     measures the loop's overhead, not a speed-up. One JSON line of its own, 1 GPU."""
     import os
@@ -683,8 +684,8 @@ def run_decode_loop(args):
 
     w = synth.make_weights("q4", n_layers=args.layers, seed=args.seed)
     eng = VerifyEngine(w, max_ctx=4096, max_steps=4096, device=0)
-    d = DeviceDrafter(os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden",
-                                   "draft_subset.ildraft"))
+    d_path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "draft_subset.ildraft")
+    d = DeviceDrafter(d_path)
     s = eng.stream
     prompt = synth.make_prompt(PREFIX, seed=args.seed + 7).tolist()
     n_new = 64
@@ -730,6 +731,37 @@ def run_decode_loop(args):
         e1.record(s)
         torch.cuda.synchronize()
         draft_us[f"B{B}_branch{br}"] = 1000 * e0.elapsed_time(e1) / 20
+    # the prefill alone (the 256-token prompt in 16-row chunks on all SMs), part of every loop above
+    def prefill():
+        eng.begin(0, n_new, synth.STOP_IDS)
+        eng.prefill(prompt)
+    ms_prefill, _ = timed(prefill)
+    # four requests at once (generate_drafted_batch): drafts side by side, one vp_pass_batch launch
+    # per step, each request on a quarter of the SMs; checked against greedy 1-row passes on the
+    # same share
+    K = 4
+    engs = [eng] + [VerifyEngine(w, max_ctx=4096, max_steps=4096, device=0) for _ in range(K - 1)]
+    ds = [d] + [DeviceDrafter(d_path) for _ in range(K - 1)]
+    prompts = [synth.make_prompt(PREFIX, seed=args.seed + 7 + q).tolist() for q in range(K)]
+    ms_b, rb = timed(lambda: VerifyEngine.generate_drafted_batch(engs, prompts, n_new, ds, pids=prompts, depth=1))
+    root = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=eng.device)
+    for e in engs:
+        e.begin(0, n_new, synth.STOP_IDS)
+    VerifyEngine.prefill_batch(engs, prompts)
+    for _ in range(n_new - 1):
+        VerifyEngine.pass_multi(engs, [root] * K, shares=K)
+    batch_equal = all(e.tokens(e.state()["step"]) == q["tokens"] for e, q in zip(engs, rb))
+
+    def prefill4():
+        for e in engs:
+            e.begin(0, n_new, synth.STOP_IDS)
+        VerifyEngine.prefill_batch(engs, prompts)
+    ms_prefill4, _ = timed(prefill4)
+    batch_tok = sum(len(q["tokens"]) for q in rb)
+    for x in ds[1:]:
+        x.close()
+    for x in engs[1:]:
+        x.close()
     ntok = len(r["tokens"])
     line = {
         "metric": "device-resident decode loop (k_draft + verify pass per step, one step enqueued ahead): "
@@ -745,6 +777,13 @@ def run_decode_loop(args):
         "greedy_tok_s": len(g["tokens"]) / (ms_greedy * 1e-3),
         "tokens_equal_greedy": r["tokens"] == g["tokens"] == rt["tokens"] == rg["tokens"],
         "k_draft_us": draft_us,
+        "prefill_ms": ms_prefill,
+        "decode_tok_s": ntok / ((ms_loop - ms_prefill) * 1e-3),
+        "batch4_loop_tok_s": batch_tok / (ms_b * 1e-3),
+        "batch4_prefill_ms": ms_prefill4,
+        "batch4_decode_tok_s": batch_tok / ((ms_b - ms_prefill4) * 1e-3),
+        "batch4_ms": ms_b,
+        "batch4_tokens_equal_greedy_on_share": bool(batch_equal),
         "dtype": "q4 weights, fp16 activations, fp32 accumulate; drafter float64",
         "data": "synthetic (seeded random-init q4 weights, uniform prompt ids); drafter table: the committed "
                 "subset of the reference's table",

@@ -190,6 +190,12 @@ int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, v
  * (37 to 49 CTAs per request on a B200) the QKV, O and down projections run one or two row-blocks per
  * CTA. Returns VP_ERR_ARG for a bad n / shares, VP_ERR_DEVICE if a share is below 36 SMs. */
 int vp_pass_batch(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, int32_t shares, void* stream);
+/* Prefill of k requests (vp_prefill of each, Engine.encodePrefill :588-601) with every request on
+ * gridDim / shares CTAs: launch c runs chunk c (16 rows) of every prompt that has one. A request
+ * prefilled on a share and then decoded with vp_pass_batch on the same share gives the tokens of
+ * its greedy 1-row passes on that share. d_tokens[i]: n[i] prompt ids on the device. */
+int vp_prefill_batch(vp_ctx* const* ctxs, const int32_t* const* d_tokens, const int32_t* n, int32_t k,
+                     int32_t shares, void* stream);
 
 /* One step of the host's decode loop (the body of Engine.generate's loop, Engine.swift:937-1015:
  * fill State, encode the pass, wait, read State and the committed tokens) in one call from host

@@ -18,7 +18,7 @@ MAT_PLAIN, MAT_QKV, MAT_GATEUP = 0, 1, 2
 EXPORTS = (
     "vp_packed_bytes", "vp_pack_matrix", "vp_create", "vp_destroy", "vp_set_weights",
     "vp_last_error", "vp_begin", "vp_prefill", "vp_verify", "vp_verify_chain", "vp_commit",
-    "vp_pass", "vp_pass_multi", "vp_pass_batch", "vp_step", "vp_read_state", "vp_write_state", "vp_prefix_bytes", "vp_save_prefix", "vp_load_prefix",
+    "vp_pass", "vp_pass_multi", "vp_pass_batch", "vp_prefill_batch", "vp_step", "vp_read_state", "vp_write_state", "vp_prefix_bytes", "vp_save_prefix", "vp_load_prefix",
     "vp_read_tokens", "vp_device_tokens", "vp_device_state",
     "vp_debug_logits", "vp_buffer", "vp_head_argmax_noalloc",
     "vp_sketch_bytes", "vp_pack_sketch", "vp_sketch_work_bytes", "vp_sketch_bounds_offset",
@@ -84,6 +84,7 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
         "vp_pass": (ctypes.c_int, [vp, vp, vp]),
         "vp_pass_multi": (ctypes.c_int, [ctypes.POINTER(vp), ctypes.POINTER(vp), i32, vp]),
         "vp_pass_batch": (ctypes.c_int, [ctypes.POINTER(vp), ctypes.POINTER(vp), i32, i32, vp]),
+        "vp_prefill_batch": (ctypes.c_int, [ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(i32), i32, i32, vp]),
         "vp_step": (ctypes.c_int, [vp, ctypes.c_void_p, vp, ctypes.POINTER(VpState), vp, vp]),
         "vp_read_state": (ctypes.c_int, [vp, ctypes.POINTER(VpState), vp]),
         "vp_write_state": (ctypes.c_int, [vp, ctypes.c_void_p, ctypes.c_int32, vp]),

@@ -188,6 +188,32 @@ int launch_commit(vp_ctx* c, cudaStream_t st) {
   return VP_OK;
 }
 
+// One launch of the batch kernel: bp.groups requests, each on `per` CTAs (the small-group layout
+// below 72 CTAs, where QKV has more row-blocks than CTAs).
+int launch_groups(int format, int per, const BatchParams& bp, cudaStream_t st) {
+  const bool small = per < QKV / 16;
+  const int grid = per * bp.groups;
+  switch (format) {
+    case VP_FMT_Q4:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q4, true> : k_pass_groups<VP_FMT_Q4, false>, grid, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
+    case VP_FMT_Q8:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8, true> : k_pass_groups<VP_FMT_Q8, false>, grid, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
+    case VP_FMT_Q8G32:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8G32, true> : k_pass_groups<VP_FMT_Q8G32, false>, grid,
+                     MK_THREADS, MK_SMEM, st, true, bp));
+      break;
+    default:
+      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_F16, true> : k_pass_groups<VP_FMT_F16, false>, grid, MK_THREADS,
+                     MK_SMEM, st, true, bp));
+      break;
+  }
+  return VP_OK;
+}
+
 // Whether a pass fits G CTAs: QKV / O / down take one or two row-blocks per CTA (72 / 56 / 56
 // row-blocks), and every CTA keeps its row-blocks' partial tiles of a stage in the MK_PART_SLOTS
 // shared-memory slots (QKV and gate/up past the MK_SS_SLOTS of staged RMSNorm partials).
@@ -495,24 +521,46 @@ int vp_pass_batch(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, i
     bp.p[i].do_lm = 1;
     bp.p[i].do_commit = 1;
   }
-  const bool small = per < QKV / 16;  // fewer CTAs per request than QKV row-blocks
-  switch (c0->cfg.format) {
-    case VP_FMT_Q4:
-      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q4, true> : k_pass_groups<VP_FMT_Q4, false>, per * n, MK_THREADS,
-                     MK_SMEM, st, true, bp));
-      break;
-    case VP_FMT_Q8:
-      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8, true> : k_pass_groups<VP_FMT_Q8, false>, per * n, MK_THREADS,
-                     MK_SMEM, st, true, bp));
-      break;
-    case VP_FMT_Q8G32:
-      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_Q8G32, true> : k_pass_groups<VP_FMT_Q8G32, false>, per * n,
-                     MK_THREADS, MK_SMEM, st, true, bp));
-      break;
-    default:
-      VP_CUDA(launch(small ? k_pass_groups<VP_FMT_F16, true> : k_pass_groups<VP_FMT_F16, false>, per * n, MK_THREADS,
-                     MK_SMEM, st, true, bp));
-      break;
+  return launch_groups(c0->cfg.format, per, bp, st);
+}
+
+int vp_prefill_batch(vp_ctx* const* ctxs, const int32_t* const* d_tokens, const int32_t* n, int32_t k,
+                     int32_t shares, void* stream) {
+  if (!ctxs || !d_tokens || !n || shares < 1 || shares > MK_MAX_GROUPS || k < 1 || k > shares)
+    return fail(VP_ERR_ARG, "need 1 <= k <= shares <= 4");
+  int r = VP_OK, longest = 0;
+  for (int i = 0; i < k; ++i) {
+    if ((r = check_ctx(ctxs[i]))) return r;
+    if (!d_tokens[i] || n[i] < 1) return fail(VP_ERR_ARG, "empty prompt");
+    for (int j = 0; j < i; ++j)
+      if (ctxs[j] == ctxs[i]) return fail(VP_ERR_ARG, "the same context twice");
+    if (ctxs[i]->cfg.device != ctxs[0]->cfg.device || ctxs[i]->cfg.format != ctxs[0]->cfg.format)
+      return fail(VP_ERR_ARG, "contexts on different devices or formats");
+    longest = std::max(longest, (int)n[i]);
+  }
+  vp_ctx* c0 = ctxs[0];
+  const int per = c0->grid / shares;
+  for (int i = 0; i < k; ++i)
+    if (!split_fits(per, ctxs[i]->cfg.vocab)) return fail(VP_ERR_DEVICE, "too few SMs for that many pass groups");
+  VP_CUDA(cudaSetDevice(c0->cfg.device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // chunk c of every request whose prompt has one, the requests of a launch on their shares
+  for (int c = 0; c < longest; c += ROWS) {
+    BatchParams bp = {};
+    for (int i = 0; i < k; ++i) {
+      if (c >= n[i]) continue;
+      const int cn = n[i] - c < ROWS ? n[i] - c : ROWS;
+      const bool last = c + cn == n[i];
+      MegaParams& p = bp.p[bp.groups++];
+      p = mega_params(ctxs[i]);
+      p.prompt = d_tokens[i] + c;
+      p.chunk_n = cn;
+      p.chunk_start = c;
+      p.total_n = n[i];
+      p.do_lm = last;
+      p.do_commit = last;
+    }
+    if ((r = launch_groups(c0->cfg.format, per, bp, st))) return r;
   }
   return VP_OK;
 }

@@ -418,6 +418,130 @@ class VerifyEngine:
         assert len(out) == st["step"], (len(out), st["step"])
         return {"tokens": out, "passes": passes, "state": st}
 
+    @staticmethod
+    def prefill_batch(engines, prompts, shares: Optional[int] = None) -> None:
+        """Prefill of several requests together (vp_prefill_batch), each on 1/shares of the SMs
+        (shares = the number of requests unless given): launch c runs the 16-row chunk c of every
+        prompt that has one. Each engine must have begun its request (begin)."""
+        k = len(engines)
+        shares = k if shares is None else shares
+        if len(prompts) != k:
+            raise ValueError("one prompt per engine")
+        ptrs, ns = [], []
+        for eng, p in zip(engines, prompts):
+            toks = torch.as_tensor(np.asarray(p, dtype=np.int32))
+            n = int(toks.numel())
+            if n > eng._prompt.numel():
+                eng._prompt = torch.empty(n, dtype=torch.int32, device=eng.device)
+            eng._prompt[:n].copy_(toks, non_blocking=False)
+            ptrs.append(eng._prompt.data_ptr())
+            ns.append(n)
+        ctxs = (ctypes.c_void_p * k)(*[eng.ctx.value for eng in engines])
+        arr = (ctypes.c_void_p * k)(*ptrs)
+        narr = (ctypes.c_int32 * k)(*ns)
+        e0 = engines[0]
+        check(e0.lib.vp_prefill_batch(ctxs, arr, narr, k, shares, e0._s), "vp_prefill_batch")
+
+    @staticmethod
+    def generate_drafted_batch(engines, prompts, max_new: int, drafters, pids=None, texts=None, eos=STOP_IDS,
+                               shares: Optional[int] = None, depth: int = 1, adaptive: bool = True) -> list:
+        """generate_drafted for up to four requests at once, one engine and one drafter each: every
+        step drafts each live request's next tree (k_draft, one CTA, each on its own side stream, so
+        the drafts run side by side) and then verifies all of them in one launch (vp_pass_batch,
+        each request on 1/shares of the SMs, shares = the number of requests unless given); the
+        prompts are prefilled together on the same shares (prefill_batch). Steps
+        are enqueued `depth` ahead of the last one the host has seen finish; each request's shape
+        follows its own counters (PassShape); a request the host has seen stop leaves the batch
+        (the others keep their shares). A request's output is its greedy decoding on the same share
+        (prefill_batch, then 1-row vp_pass_batch passes), token for token: its arithmetic depends on
+        its share only, not on its partners. Returns one generate_drafted result per request."""
+        k = len(engines)
+        shares = k if shares is None else shares
+        if not 1 <= k <= shares <= 4:
+            raise ValueError("need 1 <= requests <= shares <= 4")
+        if len(prompts) != k or len(drafters) != k or len({id(e) for e in engines}) != k:
+            raise ValueError("one prompt and one drafter per engine, engines distinct")
+        e0 = engines[0]
+        if any(e.device != e0.device or d.device != e0.device for e, d in zip(engines, drafters)):
+            raise ValueError("engines and drafters on one device")
+        if depth < 0:
+            raise ValueError("depth must be >= 0")
+        pids = [None] * k if pids is None else pids
+        texts = [""] * k if texts is None else texts
+        main = e0.stream
+        for e in engines:
+            e.begin(0, max_new, eos)
+        VerifyEngine.prefill_batch(engines, [list(p) for p in prompts], shares)
+        for d, p, q, t in zip(drafters, prompts, pids, texts):
+            d.begin(list(p) if q is None else list(q), t)  # overlaps the prefill
+        tree_ptrs = [e.buffer(7, (TREE_INTS,), "<i4").data_ptr() for e in engines]
+        st_ptrs = [e.lib.vp_device_state(e.ctx) for e in engines]
+        tok_ptrs = [e.lib.vp_device_tokens(e.ctx) for e in engines]
+        nf = len(_lib.STATE_FIELDS)
+        st_devs = [torch.as_tensor(_DevArray(p, (nf,), "<i4"), device=e0.device) for p in st_ptrs]
+        i_passes = _lib.STATE_FIELDS.index("passes")
+        i_acc = _lib.STATE_FIELDS.index("accepted")
+        i_done = _lib.STATE_FIELDS.index("done")
+        slots = depth + 2
+        host = torch.zeros((slots, k, nf), dtype=torch.int32).pin_memory()
+        side = [torch.cuda.Stream(device=e0.device) for _ in range(k)]
+        shape = [PassShape(adaptive=adaptive) for _ in range(k)]
+        seen = [[0, 0, 0] for _ in range(k)]  # passes, accepted, done
+        shapes = [[] for _ in range(k)]
+        from collections import deque
+
+        pending = deque()
+        waits, encoded, seen_steps = 0, 1, 1
+        with torch.cuda.stream(main):
+            while True:
+                while pending and pending[0][0].query():
+                    _, slot, live = pending.popleft()
+                    seen_steps += 1
+                    for r in live:
+                        row = host[slot, r].tolist()
+                        seen[r] = [row[i_passes], row[i_acc], row[i_done]]
+                live = [r for r in range(k) if not seen[r][2]]
+                if not live:
+                    break
+                if encoded < max_new and encoded - seen_steps <= depth:
+                    fork = torch.cuda.Event()
+                    fork.record(main)
+                    for r in live:
+                        B, branch = shape[r].next(seen[r][0], seen[r][1])
+                        shapes[r].append((B, branch))
+                        side[r].wait_event(fork)
+                        drafters[r].draft(tree_ptrs[r], tok_ptrs[r], state_ptr=st_ptrs[r], B=B, branch=branch,
+                                          stream=side[r].cuda_stream)
+                        join = torch.cuda.Event()
+                        join.record(side[r])
+                        main.wait_event(join)
+                    n = len(live)
+                    ctxs = (ctypes.c_void_p * n)(*[engines[r].ctx.value for r in live])
+                    trees = (ctypes.c_void_p * n)(*[tree_ptrs[r] for r in live])
+                    check(e0.lib.vp_pass_batch(ctxs, trees, n, shares, main.cuda_stream), "vp_pass_batch")
+                    slot = encoded % slots
+                    for r in live:
+                        host[slot, r].copy_(st_devs[r], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(main)
+                    pending.append((ev, slot, live))
+                    encoded += 1
+                    continue
+                if not pending:
+                    break
+                pending[0][0].synchronize()
+                waits += 1
+        out = []
+        for r, e in enumerate(engines):
+            st = e.state()
+            if st["err"]:
+                raise _lib.VpError(f"request {r}: device error bits {st['err']}")
+            if not st["done"]:
+                raise _lib.VpError(f"request {r}: decode loop ended before the request's stop")
+            out.append({"tokens": e.tokens(st["step"]), "passes": st["passes"] - 1, "state": st,
+                        "shapes": shapes[r], "host_waits": waits})
+        return out
+
     def generate_drafted(self, prompt, max_new: int, drafter, pids=None, text: str = "", eos=STOP_IDS,
                          cached: int = 0, depth: int = 1, shape: Optional[PassShape] = None,
                          graphs: bool = False) -> dict:

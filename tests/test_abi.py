@@ -57,6 +57,7 @@ def test_argument_errors_without_device(lib):
     assert lib.vp_pass(None, None, None) == -1
     assert lib.vp_pass_multi(None, None, 1, None) == -1
     assert lib.vp_pass_batch(None, None, 1, 4, None) == -1
+    assert lib.vp_prefill_batch(None, None, None, 1, 4, None) == -1
     assert lib.vp_commit(None, None) == -1
     st = _lib.VpState()
     assert lib.vp_read_state(None, ctypes.byref(st), None) == -1

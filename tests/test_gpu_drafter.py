@@ -111,6 +111,41 @@ def test_drafted_decode_loop_equals_greedy_decoding():
         eng.close()
 
 
+def test_batched_drafted_loop_equals_greedy_decoding_on_its_share():
+    """VerifyEngine.generate_drafted_batch: four (then two) requests, each step their drafts side by
+    side on their own streams and one vp_pass_batch launch; every request's output must be its
+    greedy decoding on the same share of the SMs (batched prefill, then 1-row passes), token for
+    token."""
+    from instantllm_b200 import synth
+    from instantllm_b200.drafter import DeviceDrafter
+    from instantllm_b200.engine import STOP_IDS, VerifyEngine
+
+    w = synth.make_weights("q4", seed=3)
+    engs = [VerifyEngine(w, max_ctx=1024, max_steps=256) for _ in range(4)]
+    ds = [DeviceDrafter(os.path.join(HERE, "golden", "draft_subset.ildraft")) for _ in range(4)]
+    root = torch.tensor(synth.tree_to_buffer(synth.root_tree()), device=engs[0].device)
+    try:
+        for k, depth in ((4, 1), (2, 0)):
+            cases = GOLD["cases"][:k]
+            prompts = [list(c["pids"]) for c in cases]
+            for e in engs[:k]:
+                e.begin(0, 40, STOP_IDS)
+            VerifyEngine.prefill_batch(engs[:k], prompts)
+            for _ in range(39):
+                VerifyEngine.pass_multi(engs[:k], [root] * k, shares=k)
+            truth = [e.tokens(e.state()["step"]) for e in engs[:k]]
+            got = VerifyEngine.generate_drafted_batch(engs[:k], prompts, 40, ds[:k], pids=prompts,
+                                                      texts=[c["text"] for c in cases], depth=depth)
+            for r in range(k):
+                assert got[r]["tokens"] == truth[r], (k, r)
+                assert got[r]["state"]["err"] == 0 and got[r]["shapes"][0] == (15, 8)
+    finally:
+        for d in ds:
+            d.close()
+        for e in engs:
+            e.close()
+
+
 def test_device_drafter_long_request_matches_the_oracle():
     """A request past the kernel's shared-memory staging caps for the prompt and the committed
     output (both longer than 2,048 tokens; the distinct prompt ids stay under the 1,024-candidate

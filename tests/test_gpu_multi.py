@@ -121,6 +121,30 @@ def test_four_requests_per_launch_tree_equals_sequential():
         e.close()
 
 
+def test_batched_prefill_matches_the_oracle():
+    """vp_prefill_batch: three prompts of different lengths (37, 20 and 5 tokens: three, two and one
+    16-row chunks) prefilled together on quarters of the SMs; each request's last-chunk logits
+    match the fp32 oracle and its first token is the oracle's argmax."""
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=2, vocab=V, seed=65)
+    engs = [VerifyEngine(w, max_ctx=512, max_steps=96) for _ in range(3)]
+    prompts = [(synth.make_prompt(n, seed=80 + n) % V).tolist() for n in (37, 20, 5)]
+    for e in engs:
+        e.begin(0, 32, (-1, -1))
+    VerifyEngine.prefill_batch(engs, prompts, shares=4)
+    m = Q.model_from_weights(w)
+    for e, p in zip(engs, prompts):
+        ref = Q.forward_causal(m, Q.KVCache(2, 512), p, 0, all_logits=True)
+        tail = len(p) - (len(p) - 1) // 16 * 16  # rows of the last chunk
+        gl = e.logits().cpu().numpy()[:tail]
+        assert float(np.abs(gl - ref[len(p) - tail:]).max()) < 0.05
+        assert e.tokens(1)[0] == int(np.argmax(ref[-1]))
+        assert e.state()["err"] == 0 and e.state()["pos"] == len(p)
+    for e in engs:
+        e.close()
+
+
 def test_long_prefixes_two_per_launch_then_one_on_its_half():
     """Rows past the 320 positions of one attention segment (the segmented path), two requests of
     different prefix lengths per launch, then the survivor alone on its half: tree == sequential."""
@@ -180,4 +204,7 @@ def test_pass_multi_rejects_bad_arguments():
     assert lib.vp_pass_batch(one, trees, 2, 1, None) == -1  # more requests than shares
     assert lib.vp_pass_batch(one, trees, 1, 5, None) == -1
     assert lib.vp_pass_batch(one, trees, 1, 0, None) == -1
+    ns = (ctypes.c_int32 * 2)(5, 5)
+    assert lib.vp_prefill_batch(one, trees, ns, 2, 2, None) == -1  # the same context twice
+    assert lib.vp_prefill_batch(one, trees, ns, 3, 2, None) == -1
     eng.close()
