@@ -649,6 +649,8 @@ def run_batch(args, k: int):
         "single_request_tok_s": sum(counts[0][args.warmup:]) / (msw * 1e-3),
         "tree_equals_sequential": bool(ok),
         "hbm_gbs": achieved,
+        # each request streams its own weights, so the bytes per committed token do not fall with k
+        "bytes_per_committed_token": k * (wbytes + kv) * args.steps / max(1, tokk),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "bytes_per_launch": k * (wbytes + kv), "peak_kind": peak_kind,
                      "note": "each request streams its own copy of the weights (no shared weight stream)"},
