@@ -1233,6 +1233,8 @@ struct BatchParams {
   MegaParams p[MK_MAX_GROUPS];
   int groups;
 };
+// a __grid_constant__ parameter block above the classic 4 KB: CUDA 12.1+ takes up to 32,764 bytes
+static_assert(sizeof(BatchParams) <= 32764, "kernel parameter block");
 template <int FMT, bool SMALL>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_pass_groups(const __grid_constant__ BatchParams bp) {
   const int per = gridDim.x / bp.groups, g = blockIdx.x / per;
