@@ -205,8 +205,10 @@ int vp_prefill_batch(vp_ctx* const* ctxs, const int32_t* const* d_tokens, const 
  * host: the committed tokens in order, then -1; all -1 when the request had already stopped).
  * Synchronises `stream`, also when it fails. The inputs go through the context's pinned staging
  * block in one host-to-device copy (state, token slots and tree are adjacent on the device), the
- * results in one device-to-host copy of 128 bytes. Returns VP_ERR_DEVICE when state_out->err is
- * set. */
+ * results in one device-to-host copy of 128 bytes; the copy in, the pass and the copy out are one
+ * CUDA graph of the context (one per input form, captured on a stream of its own at the first call,
+ * recaptured after vp_set_weights; three stream operations if a capture fails). Returns
+ * VP_ERR_DEVICE when state_out->err is set. */
 int vp_step(vp_ctx* ctx, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
             int32_t* tokens_out, void* stream);
 

@@ -86,6 +86,11 @@ struct vp_ctx {
   // that vp_step moves its inputs in one copy and its results (state + tokens) in one copy
   unsigned char* io = nullptr;
   unsigned char* pin = nullptr;  // pinned host staging of vp_step: the io block in, its head out
+  // vp_step as one CUDA graph per input form ([0]: tree only, [1]: state and tree), captured on
+  // first use on cap_stream; step_direct: capture failed once, launch the three operations instead
+  cudaGraphExec_t step_exec[2] = {nullptr, nullptr};
+  cudaStream_t cap_stream = nullptr;
+  bool step_direct = false;
 };
 
 constexpr size_t IO_TOK = 64;                                   // pass-token offset in ctx->io
@@ -367,6 +372,9 @@ int vp_create(const vp_config* cfg, vp_ctx** out) {
 void vp_destroy(vp_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->cfg.device);
+  for (cudaGraphExec_t& g : c->step_exec)
+    if (g) cudaGraphExecDestroy(g);
+  if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   for (void* p : c->allocs) cudaFree(p);
   if (c->pin) cudaFreeHost(c->pin);
   delete c;
@@ -380,6 +388,11 @@ int vp_set_weights(vp_ctx* c, const vp_weights* w) {
       return fail(VP_ERR_ARG, "layer weight missing");
   c->w = *w;
   c->have_w = true;
+  for (cudaGraphExec_t& g : c->step_exec)  // they hold the previous weights' pointers
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
   return VP_OK;
 }
 
@@ -570,6 +583,43 @@ int vp_pass_multi(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, v
   return vp_pass_batch(ctxs, trees, n, 2, stream);
 }
 
+namespace {
+// vp_step's operations on ctx c: the io block in from the pinned staging block (from byte `off`),
+// the pass, the state and the pass's tokens out to the staging block.
+int step_ops(vp_ctx* c, size_t off, cudaStream_t st) {
+  VP_CUDA(cudaMemcpyAsync(c->io + off, c->pin + off, IO_BYTES - off, cudaMemcpyHostToDevice, st));
+  MegaParams p = mega_params(c);
+  p.do_lm = 1;
+  p.do_commit = 1;
+  const int r = launch_pass(c, p, st);
+  if (r) return r;
+  VP_CUDA(cudaMemcpyAsync(c->pin + PIN_OUT, c->io, IO_TREE, cudaMemcpyDeviceToHost, st));
+  return VP_OK;
+}
+
+// The graph of step_ops for one input form, captured once (a thread-local capture on a stream of
+// the context's own): every later vp_step is one graph launch instead of three operations.
+cudaGraphExec_t step_graph(vp_ctx* c, int with_state) {
+  if (c->step_exec[with_state] || c->step_direct) return c->step_exec[with_state];
+  bool ok = cudaSetDevice(c->cfg.device) == cudaSuccess;
+  if (ok && !c->cap_stream) ok = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking) == cudaSuccess;
+  cudaGraph_t g = nullptr;
+  if (ok) ok = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+  if (ok) {
+    const int r = step_ops(c, with_state ? 0 : IO_TOK, c->cap_stream);
+    ok = cudaStreamEndCapture(c->cap_stream, &g) == cudaSuccess && r == VP_OK && g;
+  }
+  if (ok) ok = cudaGraphInstantiate(&c->step_exec[with_state], g, 0) == cudaSuccess;
+  if (g) cudaGraphDestroy(g);
+  if (!ok) {
+    cudaGetLastError();  // a failed capture leaves no error behind: vp_step launches directly
+    c->step_exec[with_state] = nullptr;
+    c->step_direct = true;
+  }
+  return c->step_exec[with_state];
+}
+}  // namespace
+
 int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* state_out,
             int32_t* tokens_out, void* stream) {
   int r = check_ctx(c);
@@ -581,19 +631,13 @@ int vp_step(vp_ctx* c, const vp_state* state_in, const int32_t* tree, vp_state* 
   std::memcpy(c->pin + IO_TREE, tree, VP_TREE_INTS * sizeof(int32_t));
   // no tokens unless the commit runs (a finished or failed request skips it)
   std::memset(c->pin + IO_TOK, 0xff, IO_TREE - IO_TOK);
-  size_t off = IO_TOK;
-  if (state_in) {
-    std::memcpy(c->pin, state_in, sizeof(vp_state));
-    off = 0;
-  }
-  VP_CUDA(cudaMemcpyAsync(c->io + off, c->pin + off, IO_BYTES - off, cudaMemcpyHostToDevice, st));
-  MegaParams p = mega_params(c);
-  p.do_lm = 1;
-  p.do_commit = 1;
-  r = launch_pass(c, p, st);
-  if (r == VP_OK) {
-    const cudaError_t e = cudaMemcpyAsync(c->pin + PIN_OUT, c->io, IO_TREE, cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) r = fail(VP_ERR_CUDA, std::string("cudaMemcpyAsync: ") + cudaGetErrorString(e));
+  if (state_in) std::memcpy(c->pin, state_in, sizeof(vp_state));
+  const cudaGraphExec_t g = step_graph(c, state_in ? 1 : 0);
+  if (g) {
+    const cudaError_t e = cudaGraphLaunch(g, st);
+    if (e != cudaSuccess) r = fail(VP_ERR_CUDA, std::string("cudaGraphLaunch: ") + cudaGetErrorString(e));
+  } else {
+    r = step_ops(c, state_in ? 0 : IO_TOK, st);
   }
   const cudaError_t se = cudaStreamSynchronize(st);  // also on failure: the staging block is in use
   if (r) return r;

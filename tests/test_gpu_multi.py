@@ -187,6 +187,43 @@ def test_long_prefixes_two_per_launch_then_one_on_its_half():
         e.close()
 
 
+def test_a_bad_request_in_a_batch_leaves_its_partners_alone():
+    """Failure isolation across shares: one request of a four-request launch gets a malformed tree
+    (a row its own parent); it sets its own error bit and stops, without a hang, while the other
+    three commit exactly what they commit without it."""
+    from instantllm_b200.engine import VerifyEngine
+
+    w = synth.make_weights("q4", n_layers=2, vocab=V, seed=66)
+    es = [_engine(w, 20 + k) for k in range(4)]
+    engs = [e for e, _, _ in es]
+    root = _root(engs[0])
+    rng = np.random.default_rng(66)
+    trees = []
+    for e in engs:
+        first = e.tokens(1)[0]
+        trees.append(synth.seeded_tree(rng, [first] * 9, n=16, vocab=V))
+    bad = dict(trees[2], parent=list(trees[2]["parent"]))
+    bad["parent"][5] = 5
+    dev = engs[0].device
+    VerifyEngine.pass_multi(engs[:2] + engs[3:], [torch.tensor(synth.tree_to_buffer(t), device=dev)
+                                                  for t in (trees[0], trees[1], trees[3])], shares=4)
+    alone = [e.state()["step"] for e in engs]
+    outs = [e.tokens(e.state()["step"]) for e in engs]
+    for e, (_, _, sn) in zip(engs, es):
+        e.restore(sn)
+    VerifyEngine.pass_multi(engs, [torch.tensor(synth.tree_to_buffer(t), device=dev)
+                                   for t in (trees[0], trees[1], bad, trees[3])], shares=4)
+    st = [e.state() for e in engs]
+    assert st[2]["err"] & 1 and st[2]["done"] == 1
+    for r in (0, 1, 3):
+        assert st[r]["err"] == 0 and st[r]["step"] == alone[r]
+        assert engs[r].tokens(st[r]["step"]) == outs[r]
+    VerifyEngine.pass_multi(engs, [root] * 4, shares=4)  # the failed request's later passes return at once
+    assert engs[2].state()["step"] == st[2]["step"]
+    for e in engs:
+        e.close()
+
+
 def test_pass_multi_rejects_bad_arguments():
     import ctypes
 
