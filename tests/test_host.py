@@ -134,3 +134,27 @@ def test_trace_timeline_reads_the_stamp_layout():
     t["pass_us"] = [580.0]
     text = T.report(t)
     assert "round 0: 64 jobs" in text and "grid barrier 0: last arrival 20.00" in text
+
+
+def test_batched_loop_rejects_bad_arguments_before_touching_a_device():
+    from types import SimpleNamespace
+
+    from instantllm_b200.engine import VerifyEngine
+
+    dev = SimpleNamespace()
+    e = [SimpleNamespace(device=dev) for _ in range(5)]
+    d = [SimpleNamespace(device=dev) for _ in range(5)]
+    p = [[1, 2, 3]] * 5
+    gen = VerifyEngine.generate_drafted_batch
+    with pytest.raises(ValueError):
+        gen(e[:5], p[:5], 8, d[:5])                 # five requests: at most four shares
+    with pytest.raises(ValueError):
+        gen(e[:3], p[:3], 8, d[:3], shares=2)       # more requests than shares
+    with pytest.raises(ValueError):
+        gen(e[:2], p[:1], 8, d[:2])                 # one prompt per engine
+    with pytest.raises(ValueError):
+        gen([e[0], e[0]], p[:2], 8, d[:2])          # the same engine twice
+    with pytest.raises(ValueError):
+        gen(e[:2], p[:2], 8, [d[0], SimpleNamespace(device=object())])  # drafters on another device
+    with pytest.raises(ValueError):
+        gen(e[:2], p[:2], 8, d[:2], depth=-1)
