@@ -529,7 +529,8 @@ int vp_pass_batch(vp_ctx* const* ctxs, const int32_t* const* trees, int32_t n, i
   BatchParams bp = {};
   bp.groups = n;
   for (int i = 0; i < n; ++i) {
-    VP_CUDA(cudaMemcpyAsync(ctxs[i]->s.tree, trees[i], VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
+    if (trees[i] != ctxs[i]->s.tree)  // a drafter that wrote the context's own tree buffer: no copy
+      VP_CUDA(cudaMemcpyAsync(ctxs[i]->s.tree, trees[i], VP_TREE_INTS * sizeof(int32_t), cudaMemcpyDefault, st));
     bp.p[i] = mega_params(ctxs[i]);
     bp.p[i].do_lm = 1;
     bp.p[i].do_commit = 1;
