@@ -16,7 +16,10 @@
 //    split into a fixed number of parts that
 //    different consumer warps process and that are summed in part order in shared memory;
 //  * per-row arithmetic is a fixed function of the inputs (fixed parts, fixed group order, fixed
-//    attention chunks), so tree rows reproduce 1-row passes bit for bit.
+//    attention chunks), so tree rows reproduce 1-row passes bit for bit;
+//  * the same pass body also runs as one of up to four requests in a launch (k_pass_groups), each
+//    on its own share of the CTAs; the parts follow the share's CTA count, so a request reproduces
+//    its 1-row passes bit for bit on the same share.
 #pragma once
 #include "vp_attn.cuh"
 #include "vp_commit.cuh"
