@@ -158,3 +158,15 @@ def test_batched_loop_rejects_bad_arguments_before_touching_a_device():
         gen(e[:2], p[:2], 8, [d[0], SimpleNamespace(device=object())])  # drafters on another device
     with pytest.raises(ValueError):
         gen(e[:2], p[:2], 8, d[:2], depth=-1)
+
+
+def test_bench_parses_every_workload():
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--help"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    for w in ("config2", "batch2", "batch3", "batch4", "config3", "config4", "config5", "sketch_head", "decode_loop"):
+        assert w in r.stdout
